@@ -1,0 +1,341 @@
+"""Forward-pass benchmark of the CUDA compiled executor (and the reference arm).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config gpt2] [--impl b200|reference]
+
+One step = one forward of the planned graph (BASELINE configs[1] by default:
+the GPT-2-style 2-layer decoder body, batch 8 x 1024 tokens, fp32) through
+one `execute` of the node array.  With N GPUs (torchrun, one process per
+GPU) the batch of 8 is split into 8/N sequences per rank: each rank holds a
+full weight replica, its own arena and CUDA graph; no collective is on the
+data path (the only collectives are the timing barrier and max-reduction).
+
+`value` = sequences/s of the whole job with inputs already resident in HBM;
+`e2e` = the same through CudaCompiledExecutor.run with pinned host inputs
+and outputs (host->device and device->host copies inside the timed region).
+The reference arm (--impl reference) times the reference's own C executor
+(oracle/_ref, built from its sources) on the host cores for the same config.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+from __graft_entry__ import load_package  # noqa: E402
+
+load_package()
+from lbr_b200.program import OP, Program  # noqa: E402
+
+GOLDEN = ROOT / "tests" / "golden"
+CONFIGS = {
+    "gpt2": "GPT-2-style 2-layer decoder body, d768 h12, causal, B8 S1024, fp32",
+    "qwen3": "Qwen3-0.6B-shaped 2-layer body, d1024 GQA 16/8 hd128, RoPE, B8 S1024, fp32",
+    "7b": "7B-shaped block d4096 h32 ff16384, non-causal, B8 S1024, fp32",
+    "1b8k": "1B-8K block d2048 h16 ff8192, causal, B8 S8192, fp32",
+    "toy": "toy block d64 h4 ff256, B1 S32, fp32",
+}
+GLOBAL_BATCH = {"gpt2": 8, "qwen3": 8, "7b": 8, "1b8k": 8, "toy": 1}
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained"), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def program_name(cfg, b_local):
+    return "toy" if cfg == "toy" else f"{cfg}_b{b_local}"
+
+
+def node_flops(n):
+    """Algorithmic flops of a contraction node (2*M*N*K; attention 4*BH*D*P)."""
+    if n.op in (OP["MATMUL"], OP["MATMUL_ADD"]):
+        N, K = n.out_shape[-1], n.extra[0]
+        M = int(np.prod(n.out_shape[:-1]))
+        return 2.0 * M * N * K
+    if n.op == OP["ATTENTION"]:
+        S, D, causal = n.extra[0], n.extra[1], n.extra[2]
+        BH = int(np.prod(n.out_shape[:-2]))
+        pairs = S * (S + 1) / 2 if causal else S * S
+        return 4.0 * BH * D * pairs
+    return 0.0
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in self.lines:
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_reference_run(prog, consts, inputs, budget_s, threads):
+    """Time the reference C executor (oracle/_ref) or the restated oracle on the host."""
+    import oracle
+    kind = "reference" if oracle.available("reference") else "restated"
+    if kind == "reference":
+        oracle.set_threads(threads)
+    from lbr_b200.copnode import HostBinding
+    hb = HostBinding(prog, consts, inputs)
+    oracle.execute(kind, hb)        # warm-up (page-in, BLAS thread start)
+    times = []
+    t_start = time.perf_counter()
+    while True:
+        t0 = time.perf_counter()
+        oracle.execute(kind, hb)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start > budget_s or len(times) >= 50:
+            break
+    return kind, statistics.median(times), len(times)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="gpt2", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--cpu-budget", type=float, default=15.0,
+                    help="seconds of host time for the CPU baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    n_gpus = max(args.gpus, world)
+    gb = GLOBAL_BATCH[args.config]
+    b_local = max(1, gb // n_gpus)
+    metric = "forward throughput (sequences/s) and latency (ms)"
+    unit = "sequences/s"
+
+    if args.impl == "reference":
+        return reference_arm(args, rank, world, n_gpus, gb, metric, unit)
+
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    torch.cuda.set_device(local_rank)
+    from lbr_b200.executor import CudaCompiledExecutor
+
+    prog = Program.load(GOLDEN / f"{program_name(args.config, b_local)}.json")
+    consts = prog.make_constants(0)
+    inputs = prog.make_inputs(0, batch_offset=rank * b_local)
+    ex = CudaCompiledExecutor(device=local_rank)
+    ex.compile_program(prog, consts)
+    ex.upload_inputs(inputs)
+    ext = torch.cuda.ExternalStream(ex.stream, device=torch.device("cuda", local_rank))
+    # L2 flush buffer (> 126 MB L2), written between timed steps on the same stream
+    flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=f"cuda:{local_rank}")
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(max(args.warmup, 3)):
+        ex.execute_resident(sync=False)
+    ex._lib.rt_synchronize()
+
+    # ---- device-resident timing: per-step CUDA events on the library stream
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clocks:
+        for i in range(args.steps):
+            with torch.cuda.stream(ext):
+                flush.fill_(float(i))
+                starts[i].record(ext)
+            ex.execute_resident(sync=False)
+            with torch.cuda.stream(ext):
+                ends[i].record(ext)
+        ex._lib.rt_synchronize()
+        torch.cuda.synchronize()
+        barrier()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    ms = sum(step_ms) / len(step_ms)
+
+    # ---- end to end through the public API: pinned host in/out, copies inside
+    host_in = {k: ex.input_buffer(k) for k in prog.inputs}
+    for k, v in inputs.items():
+        host_in[k][...] = v
+    h2d = sum(v.nbytes for v in host_in.values())
+    d2h = sum(int(np.prod(s["shape"])) * np.dtype(s["dtype"]).itemsize for s in prog.outputs.values())
+    for _ in range(2):
+        ex.run(host_in, copy_outputs=False)
+    barrier()
+    e2e_times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        ex.run(host_in, copy_outputs=False)
+        e2e_times.append(time.perf_counter() - t0)
+    barrier()
+    e2e_ms = 1e3 * sum(e2e_times) / len(e2e_times)
+
+    # ---- per-node device times (eager launches bracketed by CUDA events)
+    prof = ex.profile_nodes(reps=3)
+    per_node_ms = [t.time_ns / 1e6 for t in prof.op_timings]
+
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms], device=f"cuda:{local_rank}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, e2e_ms = t.tolist()
+
+    launches = ex.kernel_launches
+    if rank == 0:
+        hbm, bf16, bf16_sus, basis = load_peaks()
+        gemm_ids = [i for i, n in enumerate(prog.nodes) if n.op in (OP["MATMUL"], OP["MATMUL_ADD"])]
+        gemm_flops = sum(node_flops(prog.nodes[i]) for i in gemm_ids)
+        gemm_ms = sum(per_node_ms[i] for i in gemm_ids)
+        achieved = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms else 0.0
+        tf32 = bf16 / 2.0
+        line = {
+            "metric": metric, "value": round(gb / (ms / 1e3), 3), "unit": unit,
+            "n_gpus": n_gpus, "steps": args.steps, "warmup": max(args.warmup, 3),
+            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32 (3xTF32 tensor-core contractions)",
+            "data": "synthetic: seeded N(0,0.02) weights, N(0,1) hidden states",
+            "config": {"workload": CONFIGS[args.config], "program": program_name(args.config, b_local),
+                       "global_batch": gb, "batch_per_gpu": b_local, "parallelism": f"dp{n_gpus}",
+                       "l2": "256 MiB buffer written between timed steps (outside the step events)"},
+            "latency_ms": round(ms, 4),
+            "e2e": {"value": round(gb / (e2e_ms / 1e3), 3), "unit": unit, "latency_ms": round(e2e_ms, 4),
+                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
+            "gpu_launches": launches * args.steps,
+            "roofline": {"bound": "tensor", "kernel": "MATMUL/MATMUL_ADD nodes (sum)",
+                         "achieved": round(achieved, 3), "peak": bf16, "unit": "TFLOP/s",
+                         "frac": round(achieved / bf16, 4), "traffic": None,
+                         "peak_basis": f"{basis} bf16 dense burst",
+                         "peak_3xtf32_effective": round(tf32 / 3, 1),
+                         "frac_3xtf32": round(achieved / (tf32 / 3), 4)},
+            "clocks": clocks.summary(),
+            "per_op_ms": summarize_ops(prog, per_node_ms),
+        }
+        if n_gpus == 1 and not args.no_cpu_baseline:
+            threads = os.cpu_count() or 1
+            kind, t_cpu, runs = cpu_reference_run(prog, consts, inputs, args.cpu_budget, threads)
+            line["cpu_baseline"] = {
+                "value": round(b_local / t_cpu, 4), "unit": unit, "cores": threads,
+                "kind": "reference" if kind == "reference" else "port",
+                "sample": f"{runs} forward(s) of the same program on the host, median {t_cpu * 1e3:.1f} ms"}
+        print(json.dumps(line), flush=True)
+    ex.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def summarize_ops(prog, per_node_ms):
+    from lbr_b200.program import OP_NAME
+    agg = {}
+    for n, t in zip(prog.nodes, per_node_ms):
+        k = OP_NAME.get(n.op, str(n.op))
+        agg[k] = agg.get(k, 0.0) + t
+    return {k: round(v, 4) for k, v in sorted(agg.items(), key=lambda kv: -kv[1])}
+
+
+def reference_arm(args, rank, world, n_gpus, gb, metric, unit):
+    """The reference's own C executor on the host cores, same config and metric."""
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    prog = Program.load(GOLDEN / f"{program_name(args.config, gb)}.json")
+    consts = prog.make_constants(0)
+    inputs = prog.make_inputs(0)
+    import oracle
+    kind = "reference" if oracle.available("reference") else "restated"
+    if kind == "reference":
+        oracle.set_threads(threads)
+    from lbr_b200.copnode import HostBinding
+    hb = HostBinding(prog, consts, inputs)
+    for _ in range(max(1, min(args.warmup, 2))):
+        oracle.execute(kind, hb)
+    times = []
+    steps = max(1, min(args.steps, 5))
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        oracle.execute(kind, hb)
+        times.append(time.perf_counter() - t0)
+    ms = 1e3 * statistics.median(times)
+    value = gb / (ms / 1e3)
+    line = {
+        "impl": "reference", "metric": metric, "value": round(value, 4), "unit": unit,
+        "n_gpus": n_gpus, "steps": steps, "warmup": max(1, min(args.warmup, 2)),
+        "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic: seeded N(0,0.02) weights, N(0,1) hidden states",
+        "config": {"workload": CONFIGS[args.config], "program": program_name(args.config, gb),
+                   "global_batch": gb, "parallelism": "host CPU"},
+        "cpu_baseline": {"value": round(value, 4), "unit": unit, "cores": threads,
+                         "kind": "reference" if kind == "reference" else "port",
+                         "sample": f"{steps} full forwards (median) of the reference C executor "
+                                   f"(csrc/executor.c + csrc/ops, OpenBLAS sgemm)"},
+        "e2e": {"value": round(value, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,29 @@
+// gemm.h -- GEMM problem description shared by the GEMM paths.
+#pragma once
+#include "rt_internal.h"
+
+namespace rt {
+
+// C[b] = alpha * A[b] . op(B[b]) (+ bias[col]) for b < batches;
+// A [M,K] row-major; B [N,K] if trans_b else [K,N]; C [M,N].
+struct GemmProblem {
+    const float* a;
+    const float* b;
+    float* c;
+    const float* bias;
+    int64_t M, N, K, batches;
+    int64_t stride_a, stride_b, stride_c;
+    float alpha;
+    int trans_b;
+};
+
+Status decode_gemm(const OpNode& n, GemmProblem* p);
+Status launch_simt_gemm(const GemmProblem& p, cudaStream_t st);
+
+// tcgen05 3xTF32 path (k_gemm_tc.cu)
+bool tc_gemm_applicable(const GemmProblem& p);
+size_t tc_gemm_workspace_bytes(const GemmProblem& p);
+Status tc_gemm_prepare(const GemmProblem& p, cudaStream_t st);
+Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* launches);
+
+}  // namespace rt

@@ -1,0 +1,287 @@
+// k_norm.cu -- row-wise normalisations and reductions.
+//
+// Reference semantics:
+//   LAYERNORM csrc/ops/norm.c:48-63 (non-Apple): mean, centred variance,
+//             (x-mean) * (1/sqrt(var/C + eps)) * gamma + beta; eps = extra[0] bits
+//             (csrc/executor.c:296-301)
+//   RMSNORM   csrc/ops/norm.c:100-107: x * (1/sqrt(sum(x^2)/C + eps)) * w
+//   SOFTMAX   csrc/ops/reduce.c:84-96: exp(x - max) / sum, along the last dim
+//   MAX/SUM   csrc/ops/reduce.c:8-36 over [outer, axis, inner], extras [axis, axis_size]
+//             (csrc/executor.c:172-190)
+//
+// A row is read from HBM once and kept in registers: one warp per row when
+// the row fits 32 lanes x VPT floats, one 256-thread CTA per row up to 4096
+// floats, and a three-pass loop beyond that.  Reductions are warp shuffles
+// (+ shared memory across warps); everything accumulates in fp32.
+#include "rt_internal.h"
+
+namespace rt {
+namespace {
+
+enum NormKind { N_LAYER = 0, N_RMS = 1, N_SOFTMAX = 2 };
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Reduction across the threads of a CTA (THREADS/32 warps); all threads get it.
+template <int THREADS, bool MAX>
+__device__ __forceinline__ float block_reduce(float v, float* sh) {
+    v = MAX ? warp_max(v) : warp_sum(v);
+    if (THREADS == 32) return v;
+    int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();  // sh may still be read from a previous reduction
+    if (l == 0) sh[w] = v;
+    __syncthreads();
+    float r = l < THREADS / 32 ? sh[l] : (MAX ? -INFINITY : 0.0f);
+    return MAX ? warp_max(r) : warp_sum(r);
+}
+
+// One row per group of THREADS threads (a warp or the whole CTA); each
+// thread holds VPT floats of the row: elements (v*THREADS + t)*4 .. +3 when
+// VEC (C % 4 == 0, aligned), else elements v*THREADS + t.
+template <int KIND, int THREADS, int VPT, bool VEC>
+__global__ void __launch_bounds__(256) row_kernel(const float* __restrict__ x,
+                                                  const float* __restrict__ g,
+                                                  const float* __restrict__ b,
+                                                  float* __restrict__ y, int64_t rows, int C,
+                                                  float eps) {
+    __shared__ float sh[32];
+    constexpr int GROUPS = 256 / THREADS;  // rows handled by one CTA at a time
+    int group = threadIdx.x / THREADS;
+    int t = threadIdx.x % THREADS;
+    for (int64_t row = (int64_t)blockIdx.x * GROUPS + group; row < rows;
+         row += (int64_t)gridDim.x * GROUPS) {
+        const float* xr = x + row * C;
+        float* yr = y + row * C;
+        float v[VPT];
+        if (VEC) {
+#pragma unroll
+            for (int i = 0; i < VPT / 4; i++) {
+                int c = (i * THREADS + t) * 4;
+                float4 q = c < C ? *reinterpret_cast<const float4*>(xr + c)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+                v[4 * i] = q.x; v[4 * i + 1] = q.y; v[4 * i + 2] = q.z; v[4 * i + 3] = q.w;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < VPT; i++) {
+                int c = i * THREADS + t;
+                v[i] = c < C ? xr[c] : 0.0f;
+            }
+        }
+        auto col = [&](int i) -> int {
+            return VEC ? ((i / 4) * THREADS + t) * 4 + (i % 4) : i * THREADS + t;
+        };
+        float scale = 1.0f, shift = 0.0f;
+        if (KIND == N_LAYER) {
+            float s = 0.0f;
+#pragma unroll
+            for (int i = 0; i < VPT; i++) s += v[i];
+            float mean = block_reduce<THREADS, false>(s, sh) / C;
+            float q = 0.0f;
+#pragma unroll
+            for (int i = 0; i < VPT; i++) {
+                float d = col(i) < C ? v[i] - mean : 0.0f;
+                v[i] = d;
+                q += d * d;
+            }
+            float var = block_reduce<THREADS, false>(q, sh);
+            scale = 1.0f / sqrtf(var / C + eps);
+        } else if (KIND == N_RMS) {
+            float q = 0.0f;
+#pragma unroll
+            for (int i = 0; i < VPT; i++) q += v[i] * v[i];
+            float ss = block_reduce<THREADS, false>(q, sh);
+            scale = 1.0f / sqrtf(ss / C + eps);
+        } else {
+            float m = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < VPT; i++)
+                if (col(i) < C) m = fmaxf(m, v[i]);
+            m = block_reduce<THREADS, true>(m, sh);
+            float s = 0.0f;
+#pragma unroll
+            for (int i = 0; i < VPT; i++) {
+                v[i] = col(i) < C ? expf(v[i] - m) : 0.0f;
+                s += v[i];
+            }
+            s = block_reduce<THREADS, false>(s, sh);
+            scale = s;  // divided below, as the reference does (reduce.c:95)
+            shift = 0.0f;
+        }
+        if (VEC) {
+#pragma unroll
+            for (int i = 0; i < VPT / 4; i++) {
+                int c = (i * THREADS + t) * 4;
+                if (c < C) {
+                    float4 o;
+                    float* op = &o.x;
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        float val = v[4 * i + k];
+                        if (KIND == N_LAYER) val = val * scale * g[c + k] + b[c + k];
+                        else if (KIND == N_RMS) val = val * scale * g[c + k];
+                        else val = val / scale;
+                        op[k] = val + shift;
+                    }
+                    *reinterpret_cast<float4*>(yr + c) = o;
+                }
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < VPT; i++) {
+                int c = i * THREADS + t;
+                if (c < C) {
+                    float val = v[i];
+                    if (KIND == N_LAYER) val = val * scale * g[c] + b[c];
+                    else if (KIND == N_RMS) val = val * scale * g[c];
+                    else val = val / scale;
+                    yr[c] = val;
+                }
+            }
+        }
+    }
+}
+
+// Rows longer than the register budget: one CTA per row, three passes over HBM.
+template <int KIND>
+__global__ void __launch_bounds__(256) row_loop_kernel(const float* __restrict__ x,
+                                                       const float* __restrict__ g,
+                                                       const float* __restrict__ b,
+                                                       float* __restrict__ y, int64_t rows,
+                                                       int C, float eps) {
+    __shared__ float sh[32];
+    for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+        const float* xr = x + row * C;
+        float* yr = y + row * C;
+        float a = 0.0f, scale = 1.0f;
+        if (KIND == N_LAYER) {
+            for (int c = threadIdx.x; c < C; c += 256) a += xr[c];
+            float mean = block_reduce<256, false>(a, sh) / C;
+            float q = 0.0f;
+            for (int c = threadIdx.x; c < C; c += 256) {
+                float d = xr[c] - mean;
+                q += d * d;
+            }
+            scale = 1.0f / sqrtf(block_reduce<256, false>(q, sh) / C + eps);
+            for (int c = threadIdx.x; c < C; c += 256) yr[c] = (xr[c] - mean) * scale * g[c] + b[c];
+        } else if (KIND == N_RMS) {
+            for (int c = threadIdx.x; c < C; c += 256) a += xr[c] * xr[c];
+            scale = 1.0f / sqrtf(block_reduce<256, false>(a, sh) / C + eps);
+            for (int c = threadIdx.x; c < C; c += 256) yr[c] = xr[c] * scale * g[c];
+        } else {
+            float m = -INFINITY;
+            for (int c = threadIdx.x; c < C; c += 256) m = fmaxf(m, xr[c]);
+            m = block_reduce<256, true>(m, sh);
+            for (int c = threadIdx.x; c < C; c += 256) a += expf(xr[c] - m);
+            float s = block_reduce<256, false>(a, sh);
+            for (int c = threadIdx.x; c < C; c += 256) yr[c] = expf(xr[c] - m) / s;
+        }
+    }
+}
+
+template <int KIND, int THREADS, int VPT, bool VEC>
+void launch_rows(const float* x, const float* g, const float* b, float* y, int64_t rows, int C,
+                 float eps, cudaStream_t st) {
+    constexpr int GROUPS = 256 / THREADS;
+    int64_t blocks = (rows + GROUPS - 1) / GROUPS;
+    int64_t cap = (int64_t)g_num_sms * (THREADS == 32 ? 8 : 4) * 4;
+    int grid = (int)(blocks < cap ? blocks : cap);
+    row_kernel<KIND, THREADS, VPT, VEC><<<grid, 256, 0, st>>>(x, g, b, y, rows, C, eps);
+}
+
+template <int KIND>
+Status run_rows(const float* x, const float* g, const float* b, float* y, int64_t rows, int C,
+                float eps, cudaStream_t st) {
+    if (rows == 0 || C == 0) return Status::ok();
+    bool vec = C % 4 == 0 && aligned16(x) && aligned16(y);
+    if (vec) {
+        if (C <= 128) launch_rows<KIND, 32, 4, true>(x, g, b, y, rows, C, eps, st);
+        else if (C <= 256) launch_rows<KIND, 32, 8, true>(x, g, b, y, rows, C, eps, st);
+        else if (C <= 512) launch_rows<KIND, 32, 16, true>(x, g, b, y, rows, C, eps, st);
+        else if (C <= 1024) launch_rows<KIND, 32, 32, true>(x, g, b, y, rows, C, eps, st);
+        else if (C <= 2048) launch_rows<KIND, 256, 8, true>(x, g, b, y, rows, C, eps, st);
+        else if (C <= 4096) launch_rows<KIND, 256, 16, true>(x, g, b, y, rows, C, eps, st);
+        else vec = false;
+    }
+    if (!vec) {
+        if (C <= 128) launch_rows<KIND, 32, 4, false>(x, g, b, y, rows, C, eps, st);
+        else if (C <= 512) launch_rows<KIND, 32, 16, false>(x, g, b, y, rows, C, eps, st);
+        else {
+            int grid = (int)(rows < (int64_t)g_num_sms * 8 ? rows : (int64_t)g_num_sms * 8);
+            row_loop_kernel<KIND><<<grid, 256, 0, st>>>(x, g, b, y, rows, C, eps);
+        }
+    }
+    RT_LAUNCH_CHECK();
+    return Status::ok();
+}
+
+template <bool MAX>
+__global__ void reduce_axis_kernel(const float* __restrict__ x, float* __restrict__ y,
+                                   int64_t outer, int64_t axis, int64_t inner) {
+    int64_t n = outer * inner;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t o = i / inner, j = i % inner;
+        const float* p = x + o * axis * inner + j;
+        float acc = MAX ? -3.402823466e+38f : 0.0f;
+        for (int64_t a = 0; a < axis; a++) {
+            float v = p[a * inner];
+            acc = MAX ? (v > acc ? v : acc) : acc + v;
+        }
+        y[i] = acc;
+    }
+}
+
+}  // namespace
+
+Status launch_norm(const OpNode& nd, cudaStream_t st, int* launches) {
+    *launches += 1;
+    const float* x = (const float*)nd.inputs[0];
+    float* y = (float*)nd.output;
+    int C = last_dim(nd);
+    int64_t rows = leading_dims(nd);
+    switch (nd.op) {
+        case RT_OP_LAYERNORM:
+            return run_rows<N_LAYER>(x, (const float*)nd.inputs[1], (const float*)nd.inputs[2], y,
+                                     rows, C, extra_float(nd, 0), st);
+        case RT_OP_RMSNORM:
+            return run_rows<N_RMS>(x, (const float*)nd.inputs[1], nullptr, y, rows, C,
+                                   extra_float(nd, 0), st);
+        case RT_OP_SOFTMAX:
+            return run_rows<N_SOFTMAX>(x, nullptr, nullptr, y, rows, C, 0.f, st);
+        default:
+            return Status::err(RT_ERR_BAD_OP, "norm: unexpected op");
+    }
+}
+
+Status launch_reduce(const OpNode& nd, cudaStream_t st, int* launches) {
+    *launches += 1;
+    // csrc/executor.c:172-190: outer = prod(out_shape[:axis]),
+    // inner = prod(out_shape[axis:]) (the reduced dim is absent from out_shape)
+    int axis = nd.extra[0];
+    int64_t axis_size = nd.extra[1];
+    if (axis < 0 || axis > nd.n_dims) return Status::err(RT_ERR_BAD_NODE, "reduce: bad axis");
+    int64_t outer = 1, inner = 1;
+    for (int i = 0; i < axis; i++) outer *= nd.out_shape[i];
+    for (int i = axis; i < nd.n_dims; i++) inner *= nd.out_shape[i];
+    int grid = grid_for(outer * inner, 256);
+    if (nd.op == RT_OP_MAX)
+        reduce_axis_kernel<true><<<grid, 256, 0, st>>>((const float*)nd.inputs[0],
+                                                       (float*)nd.output, outer, axis_size, inner);
+    else
+        reduce_axis_kernel<false><<<grid, 256, 0, st>>>((const float*)nd.inputs[0],
+                                                        (float*)nd.output, outer, axis_size, inner);
+    RT_LAUNCH_CHECK();
+    return Status::ok();
+}
+
+}  // namespace rt

@@ -1,0 +1,112 @@
+// rt_internal.h -- shared declarations of the CUDA backend (not part of the ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include <string>
+
+#include "b200exec.h"
+
+namespace rt {
+
+// Number of SMs on a B200; grids of bandwidth kernels are sized as
+// multiples of it (queried at init, this is only the default).
+extern int g_num_sms;
+
+inline float extra_float(const OpNode& n, int i) {
+    float f;
+    memcpy(&f, &n.extra[i], 4);
+    return f;
+}
+inline int64_t total_elements(const OpNode& n) {
+    int64_t t = 1;
+    for (int i = 0; i < n.n_dims; i++) t *= n.out_shape[i];
+    return t;
+}
+inline int64_t leading_dims(const OpNode& n) {
+    int64_t t = 1;
+    for (int i = 0; i < n.n_dims - 1; i++) t *= n.out_shape[i];
+    return t;
+}
+inline int last_dim(const OpNode& n) { return n.out_shape[n.n_dims - 1]; }
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Status carried out of planning/launch helpers.
+struct Status {
+    int code = RT_OK;
+    std::string msg;
+    static Status ok() { return {}; }
+    static Status err(int c, std::string m) {
+        Status s;
+        s.code = c;
+        s.msg = std::move(m);
+        return s;
+    }
+    bool good() const { return code == RT_OK; }
+};
+
+// Scratch requirements a node reports at plan time and receives at launch.
+struct Workspace {
+    char* base = nullptr;
+    size_t bytes = 0;
+};
+
+// Derived (split) forms of constant matrix operands, cached by the runtime
+// for as long as the constant range stays registered and plans are kept.
+struct SplitOperand {
+    float* hi = nullptr;   // [batches][rows][K] tf32-exact high parts, K-major
+    float* lo = nullptr;   // residuals a - hi
+};
+struct SplitKey {
+    const void* src;
+    int64_t batches, rows, k;
+    int trans;
+    bool operator<(const SplitKey& o) const;
+};
+// Returns the cached split of `key`, or null.
+const SplitOperand* find_constant_split(const SplitKey& key);
+// Allocates (device, zeroed) and registers an empty split of `elems` floats
+// per part; the caller fills it.
+Status create_constant_split(const SplitKey& key, size_t elems, SplitOperand* out);
+// True when [p, p+bytes) lies inside a range marked with rt_mark_constant.
+bool is_constant_range(const void* p, size_t bytes);
+
+// ---- kernel families: each returns a Status; `ws` is the node's scratch.
+// Planning hooks report scratch bytes a node needs beyond its arena buffers.
+size_t gemm_workspace_bytes(const OpNode& n);
+Status launch_gemm(const OpNode& n, cudaStream_t st, Workspace ws, int* launches);
+Status prepare_gemm(const OpNode& n, cudaStream_t st);   // constant splits, before capture
+
+Status launch_attention(const OpNode& n, cudaStream_t st, int* launches);
+Status launch_elementwise(const OpNode& n, cudaStream_t st, int* launches);
+Status launch_norm(const OpNode& n, cudaStream_t st, int* launches);
+Status launch_reduce(const OpNode& n, cudaStream_t st, int* launches);
+Status launch_layout(const OpNode& n, cudaStream_t st, int* launches);
+
+inline int grid_for(int64_t work_items, int threads, int per_sm = 8) {
+    int64_t blocks = (work_items + threads - 1) / threads;
+    int64_t cap = (int64_t)g_num_sms * per_sm;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    return (int)blocks;
+}
+
+#define RT_CUDA_CHECK(expr)                                                           \
+    do {                                                                              \
+        cudaError_t _e = (expr);                                                      \
+        if (_e != cudaSuccess)                                                        \
+            return ::rt::Status::err(RT_ERR_CUDA, std::string(#expr ": ") +           \
+                                                      cudaGetErrorString(_e));        \
+    } while (0)
+
+#define RT_LAUNCH_CHECK()                                                             \
+    do {                                                                              \
+        cudaError_t _e = cudaGetLastError();                                          \
+        if (_e != cudaSuccess)                                                        \
+            return ::rt::Status::err(RT_ERR_CUDA, std::string("launch: ") +           \
+                                                      cudaGetErrorString(_e));        \
+    } while (0)
+
+}  // namespace rt

@@ -1,0 +1,704 @@
+// runtime.cu -- the C ABI of libb200exec.so: device memory, node-array
+// validation, the launch sequence and its CUDA graph, profiling, errors.
+//
+// The reference's executor (csrc/executor.c:409-467) is a loop over the
+// OpNode array calling dispatch_table[op].  Here the same loop runs once per
+// distinct node array, at plan time, inside a CUDA stream capture; the
+// resulting graph is instantiated and every later `execute` with the same
+// array replays it with one cudaGraphLaunch.  Node arrays are identified by
+// their contents (a 64-bit FNV-1a hash plus a full compare), so the caller
+// may rebuild the array between calls, as the reference's compiled executor
+// does when it patches input pointers (runtime/executor/compiled.py:77-82);
+// with device staging buffers for graph inputs those pointers never change.
+#include <stdio.h>
+
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "rt_internal.h"
+
+namespace rt {
+
+int g_num_sms = 148;
+
+namespace {
+
+struct Alloc {
+    size_t bytes;
+    bool host;
+    bool constant;
+};
+
+struct Plan {
+    std::vector<OpNode> nodes;
+    std::vector<size_t> ws_offset;   // per node, into `ws`
+    std::vector<size_t> ws_bytes;
+    char* ws = nullptr;
+    size_t ws_total = 0;
+    cudaGraphExec_t exec = nullptr;
+    int launches = 0;
+};
+
+struct State {
+    bool initialized = false;
+    int device = -1;
+    cudaStream_t stream = nullptr;
+    std::map<uintptr_t, Alloc> allocs;                        // base -> info
+    std::map<SplitKey, SplitOperand> splits;                 // derived constants
+    std::unordered_map<uint64_t, std::vector<std::unique_ptr<Plan>>> plans;
+    int last_error = RT_OK;
+    std::string last_msg;
+};
+
+State& S() {
+    static State s;
+    return s;
+}
+
+std::recursive_mutex& M() {
+    static std::recursive_mutex m;
+    return m;
+}
+
+int fail(int code, const std::string& msg) {
+    S().last_error = code;
+    S().last_msg = msg;
+    return code;
+}
+int fail(const Status& s) { return fail(s.code, s.msg); }
+
+uint64_t fnv1a(const void* data, size_t n, uint64_t h = 1469598103934665603ull) {
+    const unsigned char* p = static_cast<const unsigned char*>(data);
+    for (size_t i = 0; i < n; i++) {
+        h ^= p[i];
+        h *= 1099511628211ull;
+    }
+    return h;
+}
+
+// The allocation registered by this library that contains [p, p+bytes).
+const Alloc* find_alloc(const void* p, size_t bytes, uintptr_t* base_out = nullptr) {
+    auto& a = S().allocs;
+    uintptr_t x = reinterpret_cast<uintptr_t>(p);
+    auto it = a.upper_bound(x);
+    if (it == a.begin()) return nullptr;
+    --it;
+    if (x < it->first || x + bytes > it->first + it->second.bytes) return nullptr;
+    if (base_out) *base_out = it->first;
+    return &it->second;
+}
+
+// Device-memory check for a buffer a node reads or writes.
+Status check_buffer(const void* p, size_t bytes, int node, const char* what) {
+    char buf[160];
+    if (!p) {
+        snprintf(buf, sizeof buf, "node %d: %s is NULL", node, what);
+        return Status::err(RT_ERR_NULL_POINTER, buf);
+    }
+    uintptr_t base;
+    const Alloc* a = find_alloc(p, 1, &base);
+    if (a) {
+        if (a->host) {
+            snprintf(buf, sizeof buf, "node %d: %s points into pinned host memory", node, what);
+            return Status::err(RT_ERR_HOST_POINTER, buf);
+        }
+        if (reinterpret_cast<uintptr_t>(p) + bytes > base + a->bytes) {
+            snprintf(buf, sizeof buf, "node %d: %s [%p, +%zu) leaves its allocation", node, what, p,
+                     bytes);
+            return Status::err(RT_ERR_OUT_OF_RANGE, buf);
+        }
+        return Status::ok();
+    }
+    // not ours: accept device memory of this device allocated elsewhere
+    cudaPointerAttributes attr;
+    cudaError_t e = cudaPointerGetAttributes(&attr, p);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        snprintf(buf, sizeof buf, "node %d: %s %p is not a device pointer", node, what, p);
+        return Status::err(RT_ERR_HOST_POINTER, buf);
+    }
+    if (attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged) {
+        snprintf(buf, sizeof buf, "node %d: %s %p is not device memory", node, what, p);
+        return Status::err(RT_ERR_HOST_POINTER, buf);
+    }
+    if (attr.device != S().device) {
+        snprintf(buf, sizeof buf, "node %d: %s lives on device %d, not %d", node, what, attr.device,
+                 S().device);
+        return Status::err(RT_ERR_HOST_POINTER, buf);
+    }
+    return Status::ok();
+}
+
+enum Family { F_NONE, F_ELEM, F_NORM, F_REDUCE, F_GEMM, F_ATTN, F_LAYOUT };
+
+Family family_of(int op) {
+    switch (op) {
+        case RT_OP_RELU: case RT_OP_EXP: case RT_OP_TANH: case RT_OP_POW: case RT_OP_GELU:
+        case RT_OP_RSQRT: case RT_OP_SILU: case RT_OP_NEG: case RT_OP_COS: case RT_OP_SIN:
+        case RT_OP_ADD: case RT_OP_SUB: case RT_OP_MUL: case RT_OP_DIV:
+        case RT_OP_FUSED_BIAS_RELU: case RT_OP_GATED_ACT:
+            return F_ELEM;
+        case RT_OP_LAYERNORM: case RT_OP_RMSNORM: case RT_OP_SOFTMAX:
+            return F_NORM;
+        case RT_OP_MAX: case RT_OP_SUM:
+            return F_REDUCE;
+        case RT_OP_MATMUL: case RT_OP_MATMUL_ADD:
+            return F_GEMM;
+        case RT_OP_ATTENTION:
+            return F_ATTN;
+        case RT_OP_RESHAPE: case RT_OP_TRANSPOSE: case RT_OP_SLICE: case RT_OP_CAT:
+        case RT_OP_EMBEDDING:
+            return F_LAYOUT;
+        default:
+            return F_NONE;   // includes PERMUTE (502): no dispatch entry in the reference
+    }
+}
+
+// Per-node buffer extents (bytes) the kernels will touch; 0 = not checked
+// beyond being device memory.  Mirrors what each reference dispatch_*
+// function reads (csrc/executor.c:54-397).
+Status validate_node(const OpNode& n, int i) {
+    char buf[160];
+    Family f = family_of(n.op);
+    if (f == F_NONE) {
+        snprintf(buf, sizeof buf, "node %d: unknown op %d", i, n.op);
+        return Status::err(RT_ERR_BAD_OP, buf);
+    }
+    if (n.n_inputs < 0 || n.n_inputs > RT_MAX_INPUTS || n.n_dims < 1 || n.n_dims > RT_MAX_DIMS ||
+        n.elem_size <= 0) {
+        snprintf(buf, sizeof buf, "node %d (op %d): bad n_inputs/n_dims/elem_size", i, n.op);
+        return Status::err(RT_ERR_BAD_NODE, buf);
+    }
+    int64_t numel = total_elements(n);
+    for (int d = 0; d < n.n_dims; d++)
+        if (n.out_shape[d] < 0) {
+            snprintf(buf, sizeof buf, "node %d: negative out_shape", i);
+            return Status::err(RT_ERR_BAD_NODE, buf);
+        }
+    size_t out_bytes = (size_t)numel * n.elem_size;
+    std::vector<size_t> need(n.n_inputs, 1);
+    int required = 1;
+    int64_t C = last_dim(n);
+    switch (n.op) {
+        case RT_OP_ADD:
+            required = n.extra[0] == 2 ? 1 : 2;
+            if (n.extra[0] == 1 && n.n_inputs >= 2) need[1] = out_bytes;
+            if (n.extra[0] == 0 && n.n_inputs >= 2) need[1] = C * 4;
+            if (n.extra[0] != 3 && n.n_inputs >= 1) need[0] = out_bytes;
+            break;
+        case RT_OP_SUB: case RT_OP_MUL: case RT_OP_DIV:
+            required = n.extra[0] == 1 ? 1 : 2;
+            if (n.extra[0] == 0 && n.n_inputs >= 2) need[1] = out_bytes;
+            if (n.extra[0] != 2 && n.n_inputs >= 1) need[0] = out_bytes;
+            break;
+        case RT_OP_FUSED_BIAS_RELU:
+            required = 2;
+            if (n.n_inputs >= 2) { need[0] = out_bytes; need[1] = C * 4; }
+            break;
+        case RT_OP_GATED_ACT:
+            required = n.extra[0] ? 3 : 2;
+            if (n.n_inputs >= required) {
+                need[0] = out_bytes;
+                need[required - 1] = out_bytes;
+                if (n.extra[0]) need[1] = C * 4;
+            }
+            break;
+        case RT_OP_LAYERNORM: case RT_OP_RMSNORM:
+            required = n.op == RT_OP_LAYERNORM ? 3 : 2;
+            if (n.n_inputs >= required) {
+                need[0] = out_bytes;
+                for (int k = 1; k < required; k++) need[k] = C * 4;
+            }
+            break;
+        case RT_OP_MATMUL: case RT_OP_MATMUL_ADD:
+            required = n.op == RT_OP_MATMUL ? 2 : 3;
+            break;
+        case RT_OP_ATTENTION:
+            required = 3 + (n.extra[3] ? 1 : 0);
+            if (n.n_inputs >= 1) need[0] = out_bytes;
+            break;
+        case RT_OP_CAT:
+            required = n.n_inputs;
+            break;
+        case RT_OP_EMBEDDING:
+            required = 2;
+            break;
+        default:   // unary, softmax, reductions, reshape, transpose, slice
+            required = 1;
+            if (n.n_inputs >= 1 && (f == F_ELEM || n.op == RT_OP_SOFTMAX || n.op == RT_OP_RESHAPE ||
+                                    n.op == RT_OP_TRANSPOSE))
+                need[0] = out_bytes;
+            break;
+    }
+    if (n.n_inputs < required) {
+        snprintf(buf, sizeof buf, "node %d (op %d): %d inputs, needs %d", i, n.op, n.n_inputs, required);
+        return Status::err(RT_ERR_BAD_NODE, buf);
+    }
+    // elementwise/norm/gemm/attention kernels compute in fp32 only
+    if ((f == F_ELEM || f == F_NORM || f == F_REDUCE || f == F_GEMM || f == F_ATTN) &&
+        n.elem_size != 4) {
+        snprintf(buf, sizeof buf, "node %d (op %d): elem_size %d, only fp32 supported", i, n.op,
+                 n.elem_size);
+        return Status::err(RT_ERR_UNSUPPORTED, buf);
+    }
+    Status s = check_buffer(n.output, out_bytes ? out_bytes : 1, i, "output");
+    if (!s.good()) return s;
+    for (int k = 0; k < required; k++) {
+        char what[32];
+        snprintf(what, sizeof what, "input %d", k);
+        s = check_buffer(n.inputs[k], need[k] ? need[k] : 1, i, what);
+        if (!s.good()) return s;
+    }
+    return Status::ok();
+}
+
+size_t node_workspace(const OpNode& n) {
+    if (family_of(n.op) == F_GEMM) return gemm_workspace_bytes(n);
+    return 0;
+}
+
+Status launch_node(const OpNode& n, cudaStream_t st, Workspace ws, int* launches) {
+    switch (family_of(n.op)) {
+        case F_ELEM: return launch_elementwise(n, st, launches);
+        case F_NORM: return launch_norm(n, st, launches);
+        case F_REDUCE: return launch_reduce(n, st, launches);
+        case F_GEMM: return launch_gemm(n, st, ws, launches);
+        case F_ATTN: return launch_attention(n, st, launches);
+        case F_LAYOUT: return launch_layout(n, st, launches);
+        default: return Status::err(RT_ERR_BAD_OP, "no kernel for op");
+    }
+}
+
+Status launch_all(Plan& p, cudaStream_t st, int* launches) {
+    for (size_t i = 0; i < p.nodes.size(); i++) {
+        Workspace ws{p.ws + p.ws_offset[i], p.ws_bytes[i]};
+        Status s = launch_node(p.nodes[i], st, ws, launches);
+        if (!s.good()) {
+            s.msg = "node " + std::to_string(i) + " (op " + std::to_string(p.nodes[i].op) + "): " + s.msg;
+            return s;
+        }
+    }
+    return Status::ok();
+}
+
+void free_plan(Plan& p) {
+    if (p.exec) cudaGraphExecDestroy(p.exec);
+    if (p.ws) cudaFree(p.ws);
+    p.exec = nullptr;
+    p.ws = nullptr;
+}
+
+Status build_plan(const OpNode* nodes, int n, bool capture, Plan** out) {
+    auto plan = std::make_unique<Plan>();
+    plan->nodes.assign(nodes, nodes + n);
+    for (int i = 0; i < n; i++) {
+        Status s = validate_node(nodes[i], i);
+        if (!s.good()) return s;
+    }
+    size_t total = 0;
+    for (int i = 0; i < n; i++) {
+        size_t b = (node_workspace(nodes[i]) + 255) & ~(size_t)255;
+        plan->ws_offset.push_back(total);
+        plan->ws_bytes.push_back(b);
+        total += b;
+    }
+    // Nodes run one after another on one stream, so their scratch can share
+    // one region: every node gets offset 0 of a region sized for the largest.
+    size_t peak = 0;
+    for (size_t i = 0; i < plan->ws_bytes.size(); i++) {
+        plan->ws_offset[i] = 0;
+        if (plan->ws_bytes[i] > peak) peak = plan->ws_bytes[i];
+    }
+    plan->ws_total = peak;
+    if (peak) {
+        cudaError_t e = cudaMalloc(&plan->ws, peak);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return Status::err(RT_ERR_OOM, "workspace allocation failed");
+        }
+    }
+    cudaStream_t st = S().stream;
+    for (int i = 0; i < n; i++) {
+        if (family_of(nodes[i].op) == F_GEMM) {
+            Status s = prepare_gemm(nodes[i], st);
+            if (!s.good()) {
+                free_plan(*plan);
+                return s;
+            }
+        }
+    }
+    if (capture) {
+        cudaError_t e = cudaStreamSynchronize(st);
+        if (e != cudaSuccess) {
+            free_plan(*plan);
+            return Status::err(RT_ERR_CUDA, std::string("prepare: ") + cudaGetErrorString(e));
+        }
+        e = cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed);
+        if (e != cudaSuccess) {
+            free_plan(*plan);
+            return Status::err(RT_ERR_CUDA, std::string("begin capture: ") + cudaGetErrorString(e));
+        }
+        int launches = 0;
+        Status s = launch_all(*plan, st, &launches);
+        cudaGraph_t graph = nullptr;
+        cudaError_t e2 = cudaStreamEndCapture(st, &graph);
+        if (!s.good() || e2 != cudaSuccess) {
+            if (graph) cudaGraphDestroy(graph);
+            cudaGetLastError();
+            free_plan(*plan);
+            if (!s.good()) return s;
+            return Status::err(RT_ERR_CUDA, std::string("end capture: ") + cudaGetErrorString(e2));
+        }
+        e = cudaGraphInstantiate(&plan->exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            free_plan(*plan);
+            return Status::err(RT_ERR_CUDA, std::string("instantiate: ") + cudaGetErrorString(e));
+        }
+        plan->launches = launches;
+    }
+    uint64_t h = fnv1a(nodes, sizeof(OpNode) * (size_t)n, (uint64_t)n);
+    *out = plan.get();
+    S().plans[h].push_back(std::move(plan));
+    return Status::ok();
+}
+
+Plan* find_plan(const OpNode* nodes, int n) {
+    uint64_t h = fnv1a(nodes, sizeof(OpNode) * (size_t)n, (uint64_t)n);
+    auto it = S().plans.find(h);
+    if (it == S().plans.end()) return nullptr;
+    for (auto& p : it->second)
+        if ((int)p->nodes.size() == n && memcmp(p->nodes.data(), nodes, sizeof(OpNode) * n) == 0)
+            return p.get();
+    return nullptr;
+}
+
+Status get_plan(const OpNode* nodes, int n, Plan** out) {
+    if (!S().initialized) return Status::err(RT_ERR_NOT_INITIALIZED, "rt_init not called");
+    if (n < 0 || (n > 0 && !nodes)) return Status::err(RT_ERR_ARGUMENT, "bad node array");
+    Plan* p = find_plan(nodes, n);
+    if (p) {
+        *out = p;
+        return Status::ok();
+    }
+    return build_plan(nodes, n, true, out);
+}
+
+void clear_plans() {
+    for (auto& kv : S().plans)
+        for (auto& p : kv.second) free_plan(*p);
+    S().plans.clear();
+    for (auto& kv : S().splits) {
+        cudaFree(kv.second.hi);
+        cudaFree(kv.second.lo);
+    }
+    S().splits.clear();
+}
+
+}  // namespace
+
+bool SplitKey::operator<(const SplitKey& o) const {
+    if (src != o.src) return src < o.src;
+    if (batches != o.batches) return batches < o.batches;
+    if (rows != o.rows) return rows < o.rows;
+    if (k != o.k) return k < o.k;
+    return trans < o.trans;
+}
+
+const SplitOperand* find_constant_split(const SplitKey& key) {
+    auto it = S().splits.find(key);
+    return it == S().splits.end() ? nullptr : &it->second;
+}
+
+Status create_constant_split(const SplitKey& key, size_t elems, SplitOperand* out) {
+    SplitOperand s;
+    if (cudaMalloc(&s.hi, elems * sizeof(float)) != cudaSuccess ||
+        cudaMalloc(&s.lo, elems * sizeof(float)) != cudaSuccess) {
+        cudaGetLastError();
+        if (s.hi) cudaFree(s.hi);
+        return Status::err(RT_ERR_OOM, "split operand allocation failed");
+    }
+    S().splits[key] = s;
+    *out = s;
+    return Status::ok();
+}
+
+bool is_constant_range(const void* p, size_t bytes) {
+    const Alloc* a = find_alloc(p, bytes);
+    return a && a->constant;
+}
+
+}  // namespace rt
+
+// ============================================================== C ABI
+using namespace rt;
+
+#define RT_GUARD std::lock_guard<std::recursive_mutex> _g(M())
+#define RT_NEED_INIT \
+    if (!S().initialized) return fail(RT_ERR_NOT_INITIALIZED, "rt_init not called")
+
+extern "C" {
+
+const char* rt_version(void) { return "b200exec 0.1 (sm_100a)"; }
+
+int rt_init(int device) {
+    RT_GUARD;
+    if (S().initialized) {
+        if (S().device == device) return RT_OK;
+        return fail(RT_ERR_ARGUMENT, "already initialised on another device; rt_destroy first");
+    }
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) return fail(RT_ERR_CUDA, std::string("cudaSetDevice: ") + cudaGetErrorString(e));
+    e = cudaStreamCreateWithFlags(&S().stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) return fail(RT_ERR_CUDA, std::string("stream: ") + cudaGetErrorString(e));
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) == cudaSuccess && sms > 0)
+        g_num_sms = sms;
+    S().device = device;
+    S().initialized = true;
+    return RT_OK;
+}
+
+int rt_destroy(void) {
+    RT_GUARD;
+    if (!S().initialized) return RT_OK;
+    cudaStreamSynchronize(S().stream);
+    clear_plans();
+    for (auto& kv : S().allocs) {
+        if (kv.second.host) cudaFreeHost(reinterpret_cast<void*>(kv.first));
+        else cudaFree(reinterpret_cast<void*>(kv.first));
+    }
+    S().allocs.clear();
+    cudaStreamDestroy(S().stream);
+    S().stream = nullptr;
+    S().initialized = false;
+    S().device = -1;
+    return RT_OK;
+}
+
+void* rt_alloc(size_t bytes) {
+    RT_GUARD;
+    if (!S().initialized) { fail(RT_ERR_NOT_INITIALIZED, "rt_init not called"); return nullptr; }
+    void* p = nullptr;
+    size_t b = bytes ? bytes : 1;
+    if (cudaMalloc(&p, b) != cudaSuccess) {
+        cudaGetLastError();
+        fail(RT_ERR_OOM, "cudaMalloc failed for " + std::to_string(bytes) + " bytes");
+        return nullptr;
+    }
+    // the reference arena is zero-initialised (runtime/executor/common.py:86)
+    if (cudaMemset(p, 0, b) != cudaSuccess) {
+        cudaFree(p);
+        fail(RT_ERR_CUDA, "cudaMemset failed");
+        return nullptr;
+    }
+    S().allocs[reinterpret_cast<uintptr_t>(p)] = Alloc{b, false, false};
+    return p;
+}
+
+int rt_free(void* dev) {
+    RT_GUARD;
+    RT_NEED_INIT;
+    auto it = S().allocs.find(reinterpret_cast<uintptr_t>(dev));
+    if (it == S().allocs.end() || it->second.host) return fail(RT_ERR_ARGUMENT, "rt_free: unknown pointer");
+    if (it->second.constant) {
+        // derived forms of this constant must go with it
+        cudaStreamSynchronize(S().stream);
+        clear_plans();
+    }
+    cudaFree(dev);
+    S().allocs.erase(it);
+    return RT_OK;
+}
+
+void* rt_host_alloc(size_t bytes) {
+    RT_GUARD;
+    if (!S().initialized) { fail(RT_ERR_NOT_INITIALIZED, "rt_init not called"); return nullptr; }
+    void* p = nullptr;
+    size_t b = bytes ? bytes : 1;
+    if (cudaMallocHost(&p, b) != cudaSuccess) {
+        cudaGetLastError();
+        fail(RT_ERR_OOM, "cudaMallocHost failed");
+        return nullptr;
+    }
+    memset(p, 0, b);
+    S().allocs[reinterpret_cast<uintptr_t>(p)] = Alloc{b, true, false};
+    return p;
+}
+
+int rt_host_free(void* host) {
+    RT_GUARD;
+    RT_NEED_INIT;
+    auto it = S().allocs.find(reinterpret_cast<uintptr_t>(host));
+    if (it == S().allocs.end() || !it->second.host) return fail(RT_ERR_ARGUMENT, "rt_host_free: unknown pointer");
+    cudaFreeHost(host);
+    S().allocs.erase(it);
+    return RT_OK;
+}
+
+int rt_upload(void* dst, const void* src, size_t bytes) {
+    RT_GUARD;
+    RT_NEED_INIT;
+    cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, S().stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(S().stream);
+    if (e != cudaSuccess) return fail(RT_ERR_CUDA, std::string("upload: ") + cudaGetErrorString(e));
+    return RT_OK;
+}
+
+int rt_download(void* dst, const void* src, size_t bytes) {
+    RT_GUARD;
+    RT_NEED_INIT;
+    cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, S().stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(S().stream);
+    if (e != cudaSuccess) return fail(RT_ERR_CUDA, std::string("download: ") + cudaGetErrorString(e));
+    return RT_OK;
+}
+
+int rt_mark_constant(void* dev, size_t bytes) {
+    RT_GUARD;
+    RT_NEED_INIT;
+    auto it = S().allocs.find(reinterpret_cast<uintptr_t>(dev));
+    if (it == S().allocs.end() || it->second.host || it->second.bytes < bytes)
+        return fail(RT_ERR_ARGUMENT, "rt_mark_constant: not the base of a library device allocation");
+    it->second.constant = true;
+    return RT_OK;
+}
+
+int rt_prepare(const OpNode* nodes, int n) {
+    RT_GUARD;
+    Plan* p;
+    Status s = get_plan(nodes, n, &p);
+    return s.good() ? RT_OK : fail(s);
+}
+
+int rt_execute(const OpNode* nodes, int n, int flags) {
+    RT_GUARD;
+    RT_NEED_INIT;
+    cudaStream_t st = S().stream;
+    if (flags & RT_FLAG_EAGER) {
+        Plan* p = find_plan(nodes, n);
+        Status s;
+        if (!p) {
+            s = build_plan(nodes, n, false, &p);
+            if (!s.good()) return fail(s);
+        }
+        int launches = 0;
+        s = launch_all(*p, st, &launches);
+        if (!s.good()) return fail(s);
+    } else {
+        Plan* p;
+        Status s = get_plan(nodes, n, &p);
+        if (!s.good()) return fail(s);
+        if (p->exec) {
+            cudaError_t e = cudaGraphLaunch(p->exec, st);
+            if (e != cudaSuccess) return fail(RT_ERR_CUDA, std::string("graph launch: ") + cudaGetErrorString(e));
+        } else {
+            int launches = 0;
+            s = launch_all(*p, st, &launches);
+            if (!s.good()) return fail(s);
+        }
+    }
+    if (!(flags & RT_FLAG_ASYNC)) {
+        cudaError_t e = cudaStreamSynchronize(st);
+        if (e != cudaSuccess) return fail(RT_ERR_CUDA, std::string("execute: ") + cudaGetErrorString(e));
+    }
+    return RT_OK;
+}
+
+void execute(OpNode* nodes, int n_nodes) { rt_execute(nodes, n_nodes, 0); }
+
+int rt_execute_io(const OpNode* nodes, int n, const RtCopy* h2d, int n_in, const RtCopy* d2h,
+                  int n_out) {
+    RT_GUARD;
+    RT_NEED_INIT;
+    cudaStream_t st = S().stream;
+    Plan* p;
+    Status s = get_plan(nodes, n, &p);
+    if (!s.good()) return fail(s);
+    for (int i = 0; i < n_in; i++) {
+        cudaError_t e = cudaMemcpyAsync(h2d[i].dst, h2d[i].src, h2d[i].bytes, cudaMemcpyHostToDevice, st);
+        if (e != cudaSuccess) return fail(RT_ERR_CUDA, std::string("h2d: ") + cudaGetErrorString(e));
+    }
+    if (p->exec) {
+        cudaError_t e = cudaGraphLaunch(p->exec, st);
+        if (e != cudaSuccess) return fail(RT_ERR_CUDA, std::string("graph launch: ") + cudaGetErrorString(e));
+    }
+    for (int i = 0; i < n_out; i++) {
+        cudaError_t e = cudaMemcpyAsync(d2h[i].dst, d2h[i].src, d2h[i].bytes, cudaMemcpyDeviceToHost, st);
+        if (e != cudaSuccess) return fail(RT_ERR_CUDA, std::string("d2h: ") + cudaGetErrorString(e));
+    }
+    cudaError_t e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return fail(RT_ERR_CUDA, std::string("execute_io: ") + cudaGetErrorString(e));
+    return RT_OK;
+}
+
+int rt_kernel_launches(const OpNode* nodes, int n) {
+    RT_GUARD;
+    Plan* p;
+    Status s = get_plan(nodes, n, &p);
+    if (!s.good()) return -fail(s);
+    return p->launches;
+}
+
+int rt_profile(const OpNode* nodes, int n, int reps, float* ms_per_node) {
+    RT_GUARD;
+    RT_NEED_INIT;
+    if (reps < 1 || !ms_per_node) return fail(RT_ERR_ARGUMENT, "rt_profile: reps >= 1 and an output array");
+    Plan* p;
+    Status s = get_plan(nodes, n, &p);
+    if (!s.good()) return fail(s);
+    cudaStream_t st = S().stream;
+    std::vector<cudaEvent_t> ev(n + 1);
+    for (auto& e : ev) cudaEventCreate(&e);
+    std::vector<double> acc(n, 0.0);
+    for (int r = 0; r < reps && s.good(); r++) {
+        cudaEventRecord(ev[0], st);
+        int launches = 0;
+        for (int i = 0; i < n && s.good(); i++) {
+            Workspace ws{p->ws + p->ws_offset[i], p->ws_bytes[i]};
+            s = launch_node(p->nodes[i], st, ws, &launches);
+            cudaEventRecord(ev[i + 1], st);
+        }
+        if (cudaEventSynchronize(ev[n]) != cudaSuccess) s = Status::err(RT_ERR_CUDA, "profile sync");
+        for (int i = 0; i < n && s.good(); i++) {
+            float ms = 0;
+            cudaEventElapsedTime(&ms, ev[i], ev[i + 1]);
+            acc[i] += ms;
+        }
+    }
+    for (auto& e : ev) cudaEventDestroy(e);
+    if (!s.good()) return fail(s);
+    for (int i = 0; i < n; i++) ms_per_node[i] = (float)(acc[i] / reps);
+    return RT_OK;
+}
+
+int rt_reset_plans(void) {
+    RT_GUARD;
+    RT_NEED_INIT;
+    cudaStreamSynchronize(S().stream);
+    clear_plans();
+    return RT_OK;
+}
+
+int rt_synchronize(void) {
+    RT_GUARD;
+    RT_NEED_INIT;
+    cudaError_t e = cudaStreamSynchronize(S().stream);
+    return e == cudaSuccess ? RT_OK : fail(RT_ERR_CUDA, cudaGetErrorString(e));
+}
+
+void* rt_stream(void) { return S().stream; }
+
+int rt_last_error(void) { return S().last_error; }
+const char* rt_last_error_message(void) { return S().last_msg.c_str(); }
+void rt_clear_error(void) {
+    S().last_error = RT_OK;
+    S().last_msg.clear();
+}
+
+}  // extern "C"

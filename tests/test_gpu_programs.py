@@ -1,0 +1,99 @@
+"""GPU parity on whole planned graphs (the hot path: one execute per graph).
+
+Tolerance (north star): per graph output, allclose(atol=1e-4, rtol=1e-3)
+against the reference C executor on the same seeded inputs.
+"""
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import GOLDEN, load_golden, mini_programs
+from lbr_b200.program import Program
+
+pytestmark = pytest.mark.gpu
+ATOL, RTOL = 1e-4, 1e-3
+
+
+def assert_parity(got, ref, what):
+    err = np.abs(got - ref)
+    assert np.allclose(got, ref, atol=ATOL, rtol=RTOL), \
+        f"{what}: max abs {err.max():.3e}, max rel {(err / (np.abs(ref) + 1e-30)).max():.3e}"
+
+
+@pytest.mark.parametrize("name", mini_programs())
+def test_mini_program_matches_reference_golden(name, gpu_executor_factory):
+    prog, ins, outs = load_golden(name)
+    ex = gpu_executor_factory(prog, prog.make_constants())
+    got = ex.run(ins)
+    for k, ref in outs.items():
+        assert_parity(got[k], ref, f"{name}:{k}")
+    assert ex.kernel_launches >= len(prog.nodes)
+
+
+@pytest.mark.parametrize("name", ["toy", "qwen3_mini_s272", "block_mini_causal_s300"])
+def test_graph_replay_equals_eager_and_is_deterministic(name, gpu_executor_factory):
+    prog, ins, outs = load_golden(name)
+    ex = gpu_executor_factory(prog, prog.make_constants())
+    a = ex.run(ins)
+    b = ex.run(ins)
+    ex.upload_inputs(ins)
+    ex.execute_eager()
+    c = ex.download_outputs()
+    for k in a:
+        np.testing.assert_array_equal(a[k], b[k])
+        np.testing.assert_array_equal(a[k], c[k])
+
+
+def test_new_inputs_reuse_the_captured_graph(gpu_executor_factory):
+    """Like the reference's reuse-across-inputs tests (test_end_to_end.py:90-110)."""
+    prog = Program.load(GOLDEN / "gpt2_mini_s64.json")
+    consts = prog.make_constants()
+    ex = gpu_executor_factory(prog, consts)
+    for seed in range(4):
+        ins = prog.make_inputs(seed + 10)
+        got = ex.run(ins)
+        ref = oracle.run_program("restated", prog, consts, ins)
+        for k in got:
+            assert_parity(got[k], ref[k], f"seed {seed}")
+
+
+FULL = [("gpt2_b8", None), ("qwen3_b8", None), ("7b_b1", None), ("1b8k_b1", None)]
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("name,_", FULL)
+def test_full_size_program_matches_reference_executor(name, _, gpu_executor_factory):
+    """BASELINE configurations at full size against the reference C executor
+    (oracle/_ref) run live on the host cores."""
+    kind = "reference" if oracle.available("reference") else "restated"
+    prog = Program.load(GOLDEN / f"{name}.json")
+    consts = prog.make_constants()
+    ins = prog.make_inputs(0)
+    ex = gpu_executor_factory(prog, consts)
+    got = ex.run(ins)
+    ex.close()
+    if kind == "reference":
+        import os
+        oracle.set_threads(os.cpu_count() or 1)
+    ref = oracle.run_program(kind, prog, consts, ins)
+    for k in got:
+        assert_parity(got[k], ref[k], f"{name}:{k} vs {kind}")
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("family", ["gpt2", "qwen3"])
+def test_batch_rows_are_independent(family, gpu_executor_factory):
+    """Size-independent property behind data-parallel sharding: row r of the
+    batch-8 program equals the batch-1 program run on sequence r."""
+    p8 = Program.load(GOLDEN / f"{family}_b8.json")
+    p1 = Program.load(GOLDEN / f"{family}_b1.json")
+    c8, c1 = p8.make_constants(), p1.make_constants()
+    ex8 = gpu_executor_factory(p8, c8)
+    full = ex8.run(p8.make_inputs(0))
+    ex8.close()
+    ex1 = gpu_executor_factory(p1, c1)
+    for r in (0, 3, 7):
+        one = ex1.run(p1.make_inputs(0, batch_offset=r))
+        for k in one:
+            assert_parity(one[k][0], full[k][r], f"row {r}")
