@@ -77,7 +77,8 @@ enum RtStatus {
     RT_ERR_UNSUPPORTED = 7,     /* valid reference node this build cannot run */
     RT_ERR_CUDA = 8,            /* a CUDA runtime/driver call failed */
     RT_ERR_OOM = 9,
-    RT_ERR_ARGUMENT = 10
+    RT_ERR_ARGUMENT = 10,
+    RT_ERR_KERNEL_TIMEOUT = 11  /* a kernel gave up a bounded wait (it recorded a code and returned) */
 };
 
 /* Execution flags for rt_execute. */

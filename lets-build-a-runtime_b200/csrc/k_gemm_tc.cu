@@ -1,10 +1,486 @@
-// k_gemm_tc.cu -- placeholder until the tcgen05 path lands.
+// k_gemm_tc.cu -- MATMUL / MATMUL_ADD on the 5th-generation tensor cores.
+//
+// fp32 accuracy from tf32 tensor cores by the 3xTF32 split: every operand
+// x is written as hi + lo with hi = x rounded to tf32 (cvt.rna.tf32.f32,
+// low 13 mantissa bits zero) and lo = x - hi (exact in fp32), and
+//     A.B ~= A_hi.B_hi + A_hi.B_lo + A_lo.B_hi
+// (the dropped A_lo.B_lo term is ~2^-22 relative).  Constant B operands
+// (weights) are split once per plan and cached; A (activations) is split per
+// launch by a bandwidth-bound pre-pass into the node's workspace.  Both split
+// operands are stored K-major.
+//
+// The tensor core's fp32 accumulation does not round like IEEE adds, and its
+// error grows with the number of MMAs summed into one accumulator (measured
+// on B200: 1.5e-3 max abs at K=16384 with one accumulator per tile).  So each
+// tile's K is accumulated in TMEM in chunks (128 by default) and the chunk
+// sums are added in fp32 registers on the CUDA cores: error stays at the
+// level of OpenBLAS sgemm (1.6e-5 at K=16384) at no measurable cost.
+//
+// Kernel: persistent, one CTA per SM, 320 threads in three roles:
+//   warp 0     TMA producer: per K-block, four tile loads (A_hi, A_lo,
+//              B_hi, B_lo; 64-byte swizzle, 16 fp32 of K per row) into a
+//              4-stage shared-memory ring;
+//   warp 1     allocates 512 TMEM columns (two 128x256 fp32 accumulators)
+//              and issues the tcgen05.mma (kind::tf32, M=128, N=256, K=8)
+//              from one thread; tcgen05.commit frees ring stages and
+//              publishes each finished K chunk;
+//   warps 2-9  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM
+//              lanes 32*(w%4)..+31 = tile rows, one half of the columns),
+//              sums the chunks in registers, then alpha / bias and one
+//              store to C -- overlapping the next chunk's / tile's MMAs.
+// Every mbarrier wait is bounded (ptx::wait_bounded); on timeout the kernel
+// records an error code in host-mapped memory, drains its copies and MMAs
+// (bounded), frees TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <stdlib.h>
+
+#include <mutex>
+
 #include "gemm.h"
+#include "sm100_ptx.h"
+
 namespace rt {
-bool tc_gemm_applicable(const GemmProblem&) { return false; }
-size_t tc_gemm_workspace_bytes(const GemmProblem&) { return 0; }
-Status tc_gemm_prepare(const GemmProblem&, cudaStream_t) { return Status::ok(); }
-Status tc_gemm_launch(const GemmProblem&, cudaStream_t, Workspace, int*) {
-    return Status::err(RT_ERR_UNSUPPORTED, "tcgen05 GEMM not built");
+
+int* kernel_error_flag();   // runtime.cu: device view of the host-mapped error word
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 16, STAGES = 4;
+constexpr int EPI_WARPS = 8, EPI_COLS = BN / 2;      // 2 warps per TMEM lane quarter
+constexpr int THREADS = 64 + 32 * EPI_WARPS;          // producer + MMA + epilogue
+constexpr int A_TILE = BM * BK * 4;                   // 8 KiB
+constexpr int B_TILE = BN * BK * 4;                   // 16 KiB
+constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;  // 48 KiB
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;     // 2 s per wait
+constexpr int ERR_PRODUCER = 0x101, ERR_MMA = 0x102, ERR_EPILOGUE = 0x103, ERR_DRAIN = 0x104;
+
+struct TcParams {
+    CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;   // 3-D {K, rows, batches}
+    float* c;
+    const float* bias;
+    float alpha;
+    int M, N, K, batches;
+    int m_tiles, n_tiles, k_blocks, total_tiles;
+    int kb_per_chunk, n_chunks;   // K accumulated in TMEM in chunks of kb_per_chunk blocks
+    int* err;
+};
+
+__device__ __forceinline__ void tile_coords(const TcParams& p, int t, int& m_blk, int& n_blk, int& bz) {
+    n_blk = t % p.n_tiles;
+    int rest = t / p.n_tiles;
+    m_blk = rest % p.m_tiles;
+    bz = rest / p.m_tiles;
 }
+
+__global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem =
+        reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+    uint64_t* full = bars;                        // [STAGES]
+    uint64_t* empty = bars + STAGES;              // [STAGES]
+    uint64_t* acc_full = bars + 2 * STAGES;       // [2]
+    uint64_t* acc_empty = bars + 2 * STAGES + 2;  // [2]
+    uint64_t* drain = bars + 2 * STAGES + 4;      // [1]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    int* issued_phase = const_cast<int*>(abort_flag) + 1;   // [STAGES], -1 = nothing outstanding
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            ptx::mbar_init(&full[s], 1);
+            ptx::mbar_init(&empty[s], 1);
+            issued_phase[s] = -1;
+        }
+        for (int b = 0; b < 2; b++) {
+            ptx::mbar_init(&acc_full[b], 1);
+            ptx::mbar_init(&acc_empty[b], 32 * EPI_WARPS);
+        }
+        ptx::mbar_init(drain, 1);
+        *abort_flag = 0;
+        ptx::fence_mbar_init();
+        ptx::prefetch_tmap(&p.ta_hi);
+        ptx::prefetch_tmap(&p.ta_lo);
+        ptx::prefetch_tmap(&p.tb_hi);
+        ptx::prefetch_tmap(&p.tb_lo);
+    }
+    if (warp == 1) ptx::tmem_alloc(tmem_slot, 512);
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------ TMA producer
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+                int m_blk, n_blk, bz;
+                tile_coords(p, t, m_blk, n_blk, bz);
+                for (int kb = 0; kb < p.k_blocks; kb++) {
+                    if (!ptx::wait_bounded(&empty[stage], phase ^ 1, abort_flag, p.err, ERR_PRODUCER,
+                                           WAIT_LIMIT_NS)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* st = smem + stage * STAGE_BYTES;
+                    ptx::mbar_expect_tx(&full[stage], STAGE_BYTES);
+                    issued_phase[stage] = (int)phase;
+                    int k0 = kb * BK;
+                    ptx::tma_load_3d(st, &p.ta_hi, &full[stage], k0, m_blk * BM, bz);
+                    ptx::tma_load_3d(st + A_TILE, &p.ta_lo, &full[stage], k0, m_blk * BM, bz);
+                    ptx::tma_load_3d(st + 2 * A_TILE, &p.tb_hi, &full[stage], k0, n_blk * BN, bz);
+                    ptx::tma_load_3d(st + 2 * A_TILE + B_TILE, &p.tb_lo, &full[stage], k0, n_blk * BN, bz);
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = ptx::idesc_tf32(BM, BN);
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            int it = 0;   // accumulator hand-offs so far (one per K chunk)
+            for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+                for (int c = 0; c < p.n_chunks && ok; c++, it++) {
+                    int b = it & 1;
+                    uint32_t acc_phase = (it >> 1) & 1;
+                    if (!ptx::wait_bounded(&acc_empty[b], acc_phase ^ 1, abort_flag, p.err, ERR_MMA,
+                                           WAIT_LIMIT_NS)) {
+                        ok = false;
+                        break;
+                    }
+                    ptx::tc_fence_after();
+                    const uint32_t d_tmem = tmem_base + b * BN;
+                    const int kb0 = c * p.kb_per_chunk;
+                    const int kb_end = min(p.k_blocks, kb0 + p.kb_per_chunk);
+                    for (int kb = kb0; kb < kb_end; kb++) {
+                        if (!ptx::wait_bounded(&full[stage], phase, abort_flag, p.err, ERR_MMA, WAIT_LIMIT_NS)) {
+                            ok = false;
+                            break;
+                        }
+                        ptx::tc_fence_after();
+                        uint8_t* st = smem + stage * STAGE_BYTES;
+#pragma unroll
+                        for (int kk = 0; kk < BK / 8; kk++) {
+                            // K advance inside the 64-byte swizzle atom: +32 bytes per 8 fp32
+                            uint64_t a_hi = ptx::smem_desc(st + kk * 32, 512, 4);
+                            uint64_t a_lo = ptx::smem_desc(st + A_TILE + kk * 32, 512, 4);
+                            uint64_t b_hi = ptx::smem_desc(st + 2 * A_TILE + kk * 32, 512, 4);
+                            uint64_t b_lo = ptx::smem_desc(st + 2 * A_TILE + B_TILE + kk * 32, 512, 4);
+                            uint32_t acc = (kb > kb0 || kk > 0) ? 1u : 0u;
+                            ptx::mma_tf32(d_tmem, a_hi, b_hi, idesc, acc);
+                            ptx::mma_tf32(d_tmem, a_hi, b_lo, idesc, 1u);
+                            ptx::mma_tf32(d_tmem, a_lo, b_hi, idesc, 1u);
+                        }
+                        ptx::mma_commit(&empty[stage]);
+                        if (++stage == STAGES) {
+                            stage = 0;
+                            phase ^= 1;
+                        }
+                    }
+                    if (!ok) break;
+                    ptx::mma_commit(&acc_full[b]);
+                }
+            }
+            // every MMA this thread issued has completed once `drain` flips
+            ptx::mma_commit(drain);
+            volatile int no_abort = 0;
+            ptx::wait_bounded(drain, 0, &no_abort, p.err, ERR_DRAIN, WAIT_LIMIT_NS);
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------ epilogue (warps 2..9)
+        // Thread = one tile row (TMEM lane) x 128 columns (half of BN).
+        const int quarter = warp & 3;
+        const int half = (warp - 2) >> 2;
+        const int row_in_tile = quarter * 32 + lane;
+        int it = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+            int m_blk, n_blk, bz;
+            tile_coords(p, t, m_blk, n_blk, bz);
+            float acc[EPI_COLS];
+            for (int c = 0; c < p.n_chunks; c++, it++) {
+                int b = it & 1;
+                uint32_t acc_phase = (it >> 1) & 1;
+                if (!ptx::wait_bounded(&acc_full[b], acc_phase, abort_flag, p.err, ERR_EPILOGUE,
+                                       WAIT_LIMIT_NS)) {
+                    ok = false;
+                    break;
+                }
+                ptx::tc_fence_after();
+                const uint32_t tbase =
+                    tmem_base + ((uint32_t)(quarter * 32) << 16) + b * BN + half * EPI_COLS;
+#pragma unroll
+                for (int q = 0; q < EPI_COLS / 16; q++) {
+                    uint32_t r[16];
+                    ptx::tmem_ld16(tbase + q * 16, r);
+                    ptx::tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 16; j++)
+                        acc[q * 16 + j] =
+                            c == 0 ? __uint_as_float(r[j]) : acc[q * 16 + j] + __uint_as_float(r[j]);
+                }
+                ptx::tc_fence_before();
+                ptx::mbar_arrive(&acc_empty[b]);
+            }
+            if (!ok) break;
+            int64_t row = (int64_t)m_blk * BM + row_in_tile;
+            if (row >= p.M) continue;
+            float* crow = p.c + ((int64_t)bz * p.M + row) * p.N;
+            const int col0 = n_blk * BN + half * EPI_COLS;
+            if ((p.N & 3) == 0 && col0 + EPI_COLS <= p.N) {
+#pragma unroll
+                for (int j = 0; j < EPI_COLS; j += 4) {
+                    float4 v = make_float4(p.alpha * acc[j], p.alpha * acc[j + 1], p.alpha * acc[j + 2],
+                                           p.alpha * acc[j + 3]);
+                    if (p.bias) {
+                        float4 bb = *reinterpret_cast<const float4*>(p.bias + col0 + j);
+                        v.x += bb.x; v.y += bb.y; v.z += bb.z; v.w += bb.w;
+                    }
+                    *reinterpret_cast<float4*>(crow + col0 + j) = v;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < EPI_COLS; j++) {
+                    if (col0 + j < p.N) {
+                        float v = p.alpha * acc[j];
+                        if (p.bias) v += p.bias[col0 + j];
+                        crow[col0 + j] = v;
+                    }
+                }
+            }
+        }
+    }
+
+    __syncthreads();
+    if (threadIdx.x == 0 && *abort_flag) {
+        // drain: copies still in flight land before the CTA's smem goes away
+        volatile int no_abort = 0;
+        for (int s = 0; s < STAGES; s++)
+            if (issued_phase[s] >= 0)
+                ptx::wait_bounded(&full[s], (uint32_t)issued_phase[s], &no_abort, nullptr, 0, 100000000ull);
+    }
+    __syncthreads();
+    if (warp == 1) {
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc(tmem_base, 512);
+    }
+}
+
+// ---- operand split: hi = tf32(x) (round to nearest), lo = x - hi ----------
+__device__ __forceinline__ float tf32_hi(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
+__global__ void split_kernel(const float* __restrict__ x, float* __restrict__ hi, float* __restrict__ lo,
+                             int64_t n, bool vec) {
+    int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    if (vec) {
+        for (int64_t i = tid; i < n / 4; i += stride) {
+            float4 v = reinterpret_cast<const float4*>(x)[i];
+            float4 h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
+            reinterpret_cast<float4*>(hi)[i] = h;
+            reinterpret_cast<float4*>(lo)[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+        }
+    } else {
+        for (int64_t i = tid; i < n; i += stride) {
+            float h = tf32_hi(x[i]);
+            hi[i] = h;
+            lo[i] = x[i] - h;
+        }
+    }
+}
+
+// [batches][K][N] -> split of the transpose, [batches][N][K]
+__global__ void split_transpose_kernel(const float* __restrict__ x, float* __restrict__ hi,
+                                       float* __restrict__ lo, int K, int N) {
+    __shared__ float tile[32][33];
+    int64_t bz = blockIdx.z;
+    const float* xb = x + bz * (int64_t)K * N;
+    float* hb = hi + bz * (int64_t)K * N;
+    float* lb = lo + bz * (int64_t)K * N;
+    int k0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
+    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+        int k = k0 + r, n = n0 + threadIdx.x;
+        tile[r][threadIdx.x] = (k < K && n < N) ? xb[(int64_t)k * N + n] : 0.0f;
+    }
+    __syncthreads();
+    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+        int n = n0 + r, k = k0 + threadIdx.x;
+        if (n < N && k < K) {
+            float v = tile[threadIdx.x][r];
+            float h = tf32_hi(v);
+            hb[(int64_t)n * K + k] = h;
+            lb[(int64_t)n * K + k] = v - h;
+        }
+    }
+}
+
+Status run_split(const float* x, float* hi, float* lo, int64_t batches, int64_t rows, int64_t K, bool trans,
+                 cudaStream_t st) {
+    if (!trans) {
+        int64_t n = batches * rows * K;
+        bool vec = aligned16(x) && n % 4 == 0;
+        int grid = grid_for(vec ? n / 4 : n, 256, 16);
+        split_kernel<<<grid, 256, 0, st>>>(x, hi, lo, n, vec);
+    } else {
+        // x is [batches][K][rows]; output [batches][rows][K]
+        dim3 grid((unsigned)((rows + 31) / 32), (unsigned)((K + 31) / 32), (unsigned)batches);
+        split_transpose_kernel<<<grid, dim3(32, 8), 0, st>>>(x, hi, lo, (int)K, (int)rows);
+    }
+    RT_LAUNCH_CHECK();
+    return Status::ok();
+}
+
+// ---- tensor maps (driver entry point fetched through the runtime) --------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    });
+    return fn;
+}
+
+Status make_tmap(CUtensorMap* m, const float* base, int64_t K, int64_t rows, int64_t batches, int box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return Status::err(RT_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)rows, (cuuint64_t)batches};
+    cuuint64_t strides[2] = {(cuuint64_t)K * 4, (cuuint64_t)(rows * K * 4)};
+    cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)box_rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return Status::err(RT_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+    return Status::ok();
+}
+
+// K accumulated per TMEM chunk (see the file comment).  RT_GEMM_KCHUNK (a
+// multiple of 16) overrides the default of 128.
+int k_chunk() {
+    static int v = [] {
+        const char* e = getenv("RT_GEMM_KCHUNK");
+        int k = e ? atoi(e) : 128;
+        if (k < BK || k % BK) k = 128;
+        return k;
+    }();
+    return v;
+}
+
+bool b_is_constant(const GemmProblem& p) {
+    return is_constant_range(p.b, (size_t)p.batches * p.N * p.K * 4);
+}
+
+size_t a_split_bytes(const GemmProblem& p) { return (size_t)p.batches * p.M * p.K * 4; }
+size_t b_split_bytes(const GemmProblem& p) { return (size_t)p.batches * p.N * p.K * 4; }
+size_t round256(size_t b) { return (b + 255) & ~(size_t)255; }
+
+}  // namespace
+
+bool tc_gemm_applicable(const GemmProblem& p) {
+    if (p.K % 4 != 0) return false;                                  // TMA row stride: 16-byte multiple
+    if ((double)p.M * p.N * p.K < 8.0 * 1024 * 1024) return false;   // tiny: the CUDA-core GEMM wins
+    if (p.M > INT32_MAX / 2 || p.N > INT32_MAX / 2 || p.K > INT32_MAX / 2 || p.batches > 65535) return false;
+    return true;
+}
+
+size_t tc_gemm_workspace_bytes(const GemmProblem& p) {
+    if (!tc_gemm_applicable(p)) return 0;
+    size_t b = 2 * round256(a_split_bytes(p));
+    if (!b_is_constant(p)) b += 2 * round256(b_split_bytes(p));
+    return b;
+}
+
+Status tc_gemm_prepare(const GemmProblem& p, cudaStream_t st) {
+    if (!tc_gemm_applicable(p)) return Status::ok();
+    static bool attr_set = false;
+    if (!attr_set) {
+        RT_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           SMEM_BYTES));
+        attr_set = true;
+    }
+    if (!b_is_constant(p)) return Status::ok();
+    SplitKey key{p.b, p.batches, p.N, p.K, p.trans_b ? 0 : 1};
+    if (find_constant_split(key)) return Status::ok();
+    SplitOperand s;
+    Status r = create_constant_split(key, (size_t)p.batches * p.N * p.K, &s);
+    if (!r.good()) return r;
+    return run_split(p.b, s.hi, s.lo, p.batches, p.N, p.K, !p.trans_b, st);
+}
+
+Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* launches) {
+    if (p.M == 0) return Status::ok();
+    if (ws.bytes < tc_gemm_workspace_bytes(p)) return Status::err(RT_ERR_ARGUMENT, "gemm: workspace too small");
+    const size_t abytes = round256(a_split_bytes(p));
+    float* a_hi = reinterpret_cast<float*>(ws.base);
+    float* a_lo = reinterpret_cast<float*>(ws.base + abytes);
+    const float *b_hi, *b_lo;
+    Status s = run_split(p.a, a_hi, a_lo, p.batches, p.M, p.K, false, st);
+    if (!s.good()) return s;
+    *launches += 1;
+    if (b_is_constant(p)) {
+        const SplitOperand* so = find_constant_split(SplitKey{p.b, p.batches, p.N, p.K, p.trans_b ? 0 : 1});
+        if (!so) return Status::err(RT_ERR_ARGUMENT, "gemm: constant operand not prepared");
+        b_hi = so->hi;
+        b_lo = so->lo;
+    } else {
+        const size_t bbytes = round256(b_split_bytes(p));
+        float* bh = reinterpret_cast<float*>(ws.base + 2 * abytes);
+        float* bl = reinterpret_cast<float*>(ws.base + 2 * abytes + bbytes);
+        s = run_split(p.b, bh, bl, p.batches, p.N, p.K, !p.trans_b, st);
+        if (!s.good()) return s;
+        *launches += 1;
+        b_hi = bh;
+        b_lo = bl;
+    }
+    TcParams prm;
+    memset(&prm, 0, sizeof prm);
+    if (!(s = make_tmap(&prm.ta_hi, a_hi, p.K, p.M, p.batches, BM)).good()) return s;
+    if (!(s = make_tmap(&prm.ta_lo, a_lo, p.K, p.M, p.batches, BM)).good()) return s;
+    if (!(s = make_tmap(&prm.tb_hi, b_hi, p.K, p.N, p.batches, BN)).good()) return s;
+    if (!(s = make_tmap(&prm.tb_lo, b_lo, p.K, p.N, p.batches, BN)).good()) return s;
+    prm.c = p.c;
+    prm.bias = p.bias;
+    prm.alpha = p.alpha;
+    prm.M = (int)p.M;
+    prm.N = (int)p.N;
+    prm.K = (int)p.K;
+    prm.batches = (int)p.batches;
+    prm.m_tiles = (int)((p.M + BM - 1) / BM);
+    prm.n_tiles = (int)((p.N + BN - 1) / BN);
+    prm.k_blocks = (int)((p.K + BK - 1) / BK);
+    prm.kb_per_chunk = k_chunk() / BK;
+    prm.n_chunks = (prm.k_blocks + prm.kb_per_chunk - 1) / prm.kb_per_chunk;
+    int64_t total = (int64_t)prm.m_tiles * prm.n_tiles * p.batches;
+    if (total > INT32_MAX) return Status::err(RT_ERR_UNSUPPORTED, "gemm: too many tiles");
+    prm.total_tiles = (int)total;
+    prm.err = kernel_error_flag();
+    int grid = prm.total_tiles < g_num_sms ? prm.total_tiles : g_num_sms;
+    tc_gemm_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(prm);
+    RT_LAUNCH_CHECK();
+    *launches += 1;
+    return Status::ok();
+}
+
 }  // namespace rt

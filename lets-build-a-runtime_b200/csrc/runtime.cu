@@ -52,6 +52,8 @@ struct State {
     std::unordered_map<uint64_t, std::vector<std::unique_ptr<Plan>>> plans;
     int last_error = RT_OK;
     std::string last_msg;
+    volatile int* kerr_host = nullptr;   // host-mapped error word written by kernels
+    int* kerr_dev = nullptr;
 };
 
 State& S() {
@@ -433,6 +435,16 @@ bool is_constant_range(const void* p, size_t bytes) {
     return a && a->constant;
 }
 
+int* kernel_error_flag() { return S().kerr_dev; }
+
+// After a synchronise: a kernel that gave up a bounded wait left its code.
+int take_kernel_error() {
+    if (!S().kerr_host) return 0;
+    int v = *S().kerr_host;
+    if (v) *S().kerr_host = 0;
+    return v;
+}
+
 }  // namespace rt
 
 // ============================================================== C ABI
@@ -459,6 +471,15 @@ int rt_init(int device) {
     int sms = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) == cudaSuccess && sms > 0)
         g_num_sms = sms;
+    void* flag = nullptr;
+    e = cudaHostAlloc(&flag, 64, cudaHostAllocMapped);
+    if (e != cudaSuccess) return fail(RT_ERR_CUDA, std::string("mapped flag: ") + cudaGetErrorString(e));
+    memset(flag, 0, 64);
+    void* dflag = nullptr;
+    e = cudaHostGetDevicePointer(&dflag, flag, 0);
+    if (e != cudaSuccess) return fail(RT_ERR_CUDA, std::string("mapped flag: ") + cudaGetErrorString(e));
+    S().kerr_host = static_cast<volatile int*>(flag);
+    S().kerr_dev = static_cast<int*>(dflag);
     S().device = device;
     S().initialized = true;
     return RT_OK;
@@ -476,6 +497,9 @@ int rt_destroy(void) {
     S().allocs.clear();
     cudaStreamDestroy(S().stream);
     S().stream = nullptr;
+    if (S().kerr_host) cudaFreeHost(const_cast<int*>(S().kerr_host));
+    S().kerr_host = nullptr;
+    S().kerr_dev = nullptr;
     S().initialized = false;
     S().device = -1;
     return RT_OK;
@@ -606,6 +630,8 @@ int rt_execute(const OpNode* nodes, int n, int flags) {
     if (!(flags & RT_FLAG_ASYNC)) {
         cudaError_t e = cudaStreamSynchronize(st);
         if (e != cudaSuccess) return fail(RT_ERR_CUDA, std::string("execute: ") + cudaGetErrorString(e));
+        if (int k = take_kernel_error())
+            return fail(RT_ERR_KERNEL_TIMEOUT, "a kernel abandoned a bounded wait, code " + std::to_string(k));
     }
     return RT_OK;
 }
@@ -634,6 +660,8 @@ int rt_execute_io(const OpNode* nodes, int n, const RtCopy* h2d, int n_in, const
     }
     cudaError_t e = cudaStreamSynchronize(st);
     if (e != cudaSuccess) return fail(RT_ERR_CUDA, std::string("execute_io: ") + cudaGetErrorString(e));
+    if (int k = take_kernel_error())
+        return fail(RT_ERR_KERNEL_TIMEOUT, "a kernel abandoned a bounded wait, code " + std::to_string(k));
     return RT_OK;
 }
 
@@ -689,7 +717,10 @@ int rt_synchronize(void) {
     RT_GUARD;
     RT_NEED_INIT;
     cudaError_t e = cudaStreamSynchronize(S().stream);
-    return e == cudaSuccess ? RT_OK : fail(RT_ERR_CUDA, cudaGetErrorString(e));
+    if (e != cudaSuccess) return fail(RT_ERR_CUDA, cudaGetErrorString(e));
+    if (int k = take_kernel_error())
+        return fail(RT_ERR_KERNEL_TIMEOUT, "a kernel abandoned a bounded wait, code " + std::to_string(k));
+    return RT_OK;
 }
 
 void* rt_stream(void) { return S().stream; }

@@ -118,7 +118,7 @@ def test_row_ops(op, C, gpu_executor_factory):
     else:
         ins, extra = [x], []
     got, ref = run_both(gpu_executor_factory, single_node_program(OP[op], ins, [rows, C], extra))
-    np.testing.assert_allclose(got, ref, rtol=1e-5, atol=2e-6)
+    np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-5)
 
 
 @pytest.mark.parametrize("op", ["MAX", "SUM"])
