@@ -515,8 +515,11 @@ void* rt_alloc(size_t bytes) {
         fail(RT_ERR_OOM, "cudaMalloc failed for " + std::to_string(bytes) + " bytes");
         return nullptr;
     }
-    // the reference arena is zero-initialised (runtime/executor/common.py:86)
-    if (cudaMemset(p, 0, b) != cudaSuccess) {
+    // the reference arena is zero-initialised (runtime/executor/common.py:86).
+    // On the library stream and waited for: the stream does not synchronise
+    // with the legacy default stream, so a plain cudaMemset could still be
+    // running when the first graph writes this memory.
+    if (cudaMemsetAsync(p, 0, b, S().stream) != cudaSuccess || cudaStreamSynchronize(S().stream) != cudaSuccess) {
         cudaFree(p);
         fail(RT_ERR_CUDA, "cudaMemset failed");
         return nullptr;
