@@ -139,6 +139,25 @@ int rt_synchronize(void);
 /* The library stream (a cudaStream_t), for callers that order work on it. */
 void* rt_stream(void);
 
+/* ---- allocation-free GEMM ------------------------------------------------ */
+/* No counterpart in the reference.  C[M,N] = alpha * A[M,K] . op(B) + bias
+ * (bias may be NULL; op(B) = B^T when trans_b, B stored [N,K], else B [K,N]),
+ * computed by the same 3xTF32 tensor-core kernel as MATMUL/MATMUL_ADD, for
+ * callers that may not allocate device memory (host callbacks, allocator
+ * hooks, plugins whose host owns every device allocation).  It allocates
+ * nothing and needs no rt_init: it runs on the current device and `stream`
+ * (a cudaStream_t; NULL = legacy default stream) and returns after C is
+ * written.  Scratch: a fixed RT_NOALLOC_SCRATCH_BYTES device array inside
+ * the library (held by every GPU that loads it), so 8*(M*K + N*K) bytes
+ * must fit: larger problems return RT_ERR_OUT_OF_RANGE; K % 4 != 0 returns
+ * RT_ERR_UNSUPPORTED.  The first call on each device performs a one-time
+ * set-up (symbol address, kernel attribute): make it before any stream
+ * capture.  All calls share the scratch: calls that overlap on the GPU race.
+ * Returns an RT_* status (not recorded in rt_last_error). */
+#define RT_NOALLOC_SCRATCH_BYTES (32u << 20)
+int rt_matmul_noalloc(const float* a, const float* b, const float* bias, float* c,
+                      int M, int N, int K, int trans_b, float alpha, void* stream);
+
 /* ---- errors ------------------------------------------------------------- */
 int rt_last_error(void);                  /* status of the last failing call; 0 if none */
 const char* rt_last_error_message(void);

@@ -484,3 +484,133 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
 }
 
 }  // namespace rt
+
+// ===========================================================================
+// rt_matmul_noalloc: the same tensor-core GEMM for callers that cannot
+// allocate device memory.
+//
+// Who needs it: code that runs where cudaMalloc is off limits -- inside a
+// host callback or an allocator hook, a plugin whose host application owns
+// all device memory through its own pool, or a process that must not grow
+// its footprint after start-up.  rt_execute plans a workspace per node array
+// (cudaMalloc), so those callers use this entry point instead.  It needs no
+// rt_init either: it works on the current device and the stream it is given.
+//
+// Its scratch (the hi/lo split copies of both operands) lives in the file-
+// scope device array below, NOALLOC_SCRATCH_BYTES (32 MiB) per GPU that loads
+// the library, held until the process exits.  The caller passes inputs and
+// output only.  Host code must not hand the array's name to a kernel (on the
+// host it is a stand-in symbol, not a device address): the address is taken
+// with cudaGetSymbolAddress once per device, on the first call made while
+// that device is current -- that first call also sets the kernel's shared-
+// memory attribute, so make it before any stream capture.  Nothing in the
+// scratch has to start at zero (every word read is written first by the
+// same call).  All calls share the one array, so calls whose GPU work
+// overlaps (different streams, or host threads) race on it.
+// ===========================================================================
+namespace rt {
+namespace {
+
+constexpr size_t NOALLOC_SCRATCH_BYTES = (size_t)32 << 20;
+static __device__ __align__(256) float g_noalloc_scratch[NOALLOC_SCRATCH_BYTES / sizeof(float)];
+static __device__ int g_noalloc_error;   // bounded-wait timeout code of the last call
+
+struct NoallocDevice {
+    float* scratch = nullptr;   // device address of g_noalloc_scratch on this device
+    int* error = nullptr;       // device address of g_noalloc_error
+    int sms = 0;
+};
+
+std::mutex& noalloc_mutex() {
+    static std::mutex m;
+    return m;
+}
+
+// Per-device set-up, run with the device current.  No allocation.
+int noalloc_setup(int device, NoallocDevice** out) {
+    static NoallocDevice table[64];
+    if (device < 0 || device >= 64) return RT_ERR_ARGUMENT;
+    NoallocDevice& d = table[device];
+    if (!d.scratch) {
+        float* s = nullptr;
+        int* e = nullptr;
+        if (cudaGetSymbolAddress(reinterpret_cast<void**>(&s), g_noalloc_scratch) != cudaSuccess ||
+            cudaGetSymbolAddress(reinterpret_cast<void**>(&e), g_noalloc_error) != cudaSuccess) {
+            cudaGetLastError();
+            return RT_ERR_CUDA;
+        }
+        if (cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
+            cudaSuccess) {
+            cudaGetLastError();
+            return RT_ERR_CUDA;
+        }
+        int sms = 0;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || sms <= 0)
+            sms = 148;
+        d.error = e;
+        d.sms = sms;
+        d.scratch = s;   // published last: a set-up that failed is retried next call
+    }
+    *out = &d;
+    return RT_OK;
+}
+
+}  // namespace
+}  // namespace rt
+
+extern "C" int rt_matmul_noalloc(const float* a, const float* b, const float* bias, float* c, int M, int N,
+                                 int K, int trans_b, float alpha, void* stream) {
+    using namespace rt;
+    if (!a || !b || !c) return RT_ERR_NULL_POINTER;
+    if (M < 0 || N <= 0 || K <= 0) return RT_ERR_ARGUMENT;
+    if (K % 4 != 0) return RT_ERR_UNSUPPORTED;   // TMA rows must be a multiple of 16 bytes
+    const size_t a_elems = round256((size_t)M * K * 4) / 4;
+    const size_t b_elems = round256((size_t)N * K * 4) / 4;
+    if (2 * (a_elems + b_elems) * sizeof(float) > NOALLOC_SCRATCH_BYTES)
+        return RT_ERR_OUT_OF_RANGE;   // needs 8*(M*K + N*K) bytes <= 32 MiB of scratch
+    if (M == 0) return RT_OK;
+    std::lock_guard<std::mutex> lock(noalloc_mutex());
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess) return RT_ERR_CUDA;
+    NoallocDevice* d = nullptr;
+    int rc = noalloc_setup(device, &d);
+    if (rc != RT_OK) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+    float* a_hi = d->scratch;
+    float* a_lo = a_hi + a_elems;
+    float* b_hi = a_lo + a_elems;
+    float* b_lo = b_hi + b_elems;
+    if (!run_split(a, a_hi, a_lo, 1, M, K, false, st).good()) return RT_ERR_CUDA;
+    if (!run_split(b, b_hi, b_lo, 1, N, K, !trans_b, st).good()) return RT_ERR_CUDA;
+
+    TcParams prm;
+    memset(&prm, 0, sizeof prm);
+    if (!make_tmap(&prm.ta_hi, a_hi, K, M, 1, BM).good() || !make_tmap(&prm.ta_lo, a_lo, K, M, 1, BM).good() ||
+        !make_tmap(&prm.tb_hi, b_hi, K, N, 1, BN).good() || !make_tmap(&prm.tb_lo, b_lo, K, N, 1, BN).good())
+        return RT_ERR_CUDA;
+    prm.c = c;
+    prm.bias = bias;
+    prm.alpha = alpha;
+    prm.M = M;
+    prm.N = N;
+    prm.K = K;
+    prm.batches = 1;
+    prm.m_tiles = (M + BM - 1) / BM;
+    prm.n_tiles = (N + BN - 1) / BN;
+    prm.k_blocks = (K + BK - 1) / BK;
+    prm.kb_per_chunk = k_chunk() / BK;
+    prm.n_chunks = (prm.k_blocks + prm.kb_per_chunk - 1) / prm.kb_per_chunk;
+    int64_t total = (int64_t)prm.m_tiles * prm.n_tiles;
+    prm.total_tiles = (int)total;
+    prm.err = d->error;
+    if (cudaMemsetAsync(d->error, 0, sizeof(int), st) != cudaSuccess) return RT_ERR_CUDA;
+    int grid = prm.total_tiles < d->sms ? prm.total_tiles : d->sms;
+    tc_gemm_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(prm);
+    if (cudaGetLastError() != cudaSuccess) return RT_ERR_CUDA;
+    // synchronous: returns once C is written, and reports a kernel that gave up a wait
+    if (cudaStreamSynchronize(st) != cudaSuccess) return RT_ERR_CUDA;
+    int kerr = 0;
+    if (cudaMemcpyFromSymbol(&kerr, g_noalloc_error, sizeof(int)) != cudaSuccess) return RT_ERR_CUDA;
+    return kerr ? RT_ERR_KERNEL_TIMEOUT : RT_OK;
+}

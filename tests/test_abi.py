@@ -16,6 +16,7 @@ HEADER = ROOT / "include" / "b200exec.h"
 def declared_functions():
     text = HEADER.read_text()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    text = re.sub(r"^#.*$", "", text, flags=re.M)
     return sorted(set(re.findall(r"\b(\w+)\s*\([^;{]*\)\s*;", text)) - {"if", "sizeof"})
 
 
