@@ -27,3 +27,13 @@ Status tc_gemm_prepare(const GemmProblem& p, cudaStream_t st);
 Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* launches);
 
 }  // namespace rt
+
+#include <cuda.h>
+namespace rt {
+// [batches][rows][K] -> hi/lo of the same layout, or (transpose) [batches][K][rows] -> [batches][rows][K].
+Status split_operand(const float* x, float* hi, float* lo, int64_t batches, int64_t rows, int64_t K,
+                     bool transpose, cudaStream_t st);
+// fp32 3-D tensor map {d0 (contiguous), d1, d2}, box {box0, box1, 1}, swizzle 0/64/128 bytes.
+Status encode_tmap_f32_3d(CUtensorMap* m, const float* base, int64_t d0, int64_t d1, int64_t d2, int box0,
+                          int box1, int swizzle_bytes);
+}  // namespace rt

@@ -195,7 +195,15 @@ Status launch_simt(const AttnParams& p, int64_t BH, cudaStream_t st) {
 
 }  // namespace
 
-Status launch_attention(const OpNode& n, cudaStream_t st, int* launches) {
+bool attention_tc_applicable(int64_t S, int D, bool has_mask, int64_t BH);
+size_t attention_tc_workspace(int64_t BHkv, int64_t S, int D);
+Status attention_tc_prepare();
+Status launch_attention_tc(const float* q, const float* k, const float* v, float* o, int64_t BH, int64_t S,
+                           int D, int group, int causal, Workspace ws, cudaStream_t st, int* launches);
+
+namespace {
+
+Status decode_attention(const OpNode& n, AttnParams* out, int64_t* BH_out, bool* has_mask_out) {
     AttnParams p{};
     p.S = n.extra[0];
     p.D = n.extra[1];
@@ -216,6 +224,43 @@ Status launch_attention(const OpNode& n, cudaStream_t st, int* launches) {
     p.o = (float*)n.output;
     if (p.mask) p.causal = 0;   // the reference applies a custom mask instead of causal
     p.scale = 1.0f / sqrtf((float)p.D);
+    *out = p;
+    *BH_out = BH;
+    *has_mask_out = has_mask != 0;
+    return Status::ok();
+}
+
+bool use_tc(const AttnParams& p, int64_t BH, bool has_mask) {
+    return attention_tc_applicable(p.S, p.D, has_mask, BH) && aligned16(p.q) && aligned16(p.o);
+}
+
+}  // namespace
+
+size_t attention_workspace_bytes(const OpNode& n) {
+    AttnParams p;
+    int64_t BH;
+    bool m;
+    if (!decode_attention(n, &p, &BH, &m).good() || !use_tc(p, BH, m)) return 0;
+    return attention_tc_workspace(BH / p.group, p.S, p.D);
+}
+
+Status prepare_attention(const OpNode& n) {
+    AttnParams p;
+    int64_t BH;
+    bool m;
+    Status s = decode_attention(n, &p, &BH, &m);
+    if (!s.good() || !use_tc(p, BH, m)) return s;
+    return attention_tc_prepare();
+}
+
+Status launch_attention(const OpNode& n, cudaStream_t st, Workspace ws, int* launches) {
+    AttnParams p;
+    int64_t BH;
+    bool has_mask;
+    Status s = decode_attention(n, &p, &BH, &has_mask);
+    if (!s.good()) return s;
+    if (use_tc(p, BH, has_mask) && ws.bytes >= attention_tc_workspace(BH / p.group, p.S, p.D))
+        return launch_attention_tc(p.q, p.k, p.v, p.o, BH, p.S, p.D, p.group, p.causal, ws, st, launches);
     *launches += 1;
     if (p.D <= 16) return launch_simt<16>(p, BH, st);
     if (p.D <= 32) return launch_simt<32>(p, BH, st);

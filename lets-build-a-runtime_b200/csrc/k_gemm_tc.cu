@@ -614,3 +614,32 @@ extern "C" int rt_matmul_noalloc(const float* a, const float* b, const float* bi
     if (cudaMemcpyFromSymbol(&kerr, g_noalloc_error, sizeof(int)) != cudaSuccess) return RT_ERR_CUDA;
     return kerr ? RT_ERR_KERNEL_TIMEOUT : RT_OK;
 }
+
+namespace rt {
+
+// Shared with the attention kernel: the 3xTF32 operand split and tensor maps.
+Status split_operand(const float* x, float* hi, float* lo, int64_t batches, int64_t rows, int64_t K,
+                     bool transpose, cudaStream_t st) {
+    return run_split(x, hi, lo, batches, rows, K, transpose, st);
+}
+
+Status encode_tmap_f32_3d(CUtensorMap* m, const float* base, int64_t d0, int64_t d1, int64_t d2, int box0,
+                          int box1, int swizzle_bytes) {
+    auto fn = encode_fn();
+    if (!fn) return Status::err(RT_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[3] = {(cuuint64_t)d0, (cuuint64_t)d1, (cuuint64_t)d2};
+    cuuint64_t strides[2] = {(cuuint64_t)d0 * 4, (cuuint64_t)(d0 * d1 * 4)};
+    cuuint32_t box[3] = {(cuuint32_t)box0, (cuuint32_t)box1, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUtensorMapSwizzle sw = swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                            : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                  : CU_TENSOR_MAP_SWIZZLE_NONE;
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return Status::err(RT_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+    return Status::ok();
+}
+
+}  // namespace rt

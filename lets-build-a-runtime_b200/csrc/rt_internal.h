@@ -79,7 +79,9 @@ size_t gemm_workspace_bytes(const OpNode& n);
 Status launch_gemm(const OpNode& n, cudaStream_t st, Workspace ws, int* launches);
 Status prepare_gemm(const OpNode& n, cudaStream_t st);   // constant splits, before capture
 
-Status launch_attention(const OpNode& n, cudaStream_t st, int* launches);
+Status launch_attention(const OpNode& n, cudaStream_t st, Workspace ws, int* launches);
+size_t attention_workspace_bytes(const OpNode& n);
+Status prepare_attention(const OpNode& n);
 Status launch_elementwise(const OpNode& n, cudaStream_t st, int* launches);
 Status launch_norm(const OpNode& n, cudaStream_t st, int* launches);
 Status launch_reduce(const OpNode& n, cudaStream_t st, int* launches);

@@ -260,6 +260,7 @@ Status validate_node(const OpNode& n, int i) {
 
 size_t node_workspace(const OpNode& n) {
     if (family_of(n.op) == F_GEMM) return gemm_workspace_bytes(n);
+    if (family_of(n.op) == F_ATTN) return attention_workspace_bytes(n);
     return 0;
 }
 
@@ -269,7 +270,7 @@ Status launch_node(const OpNode& n, cudaStream_t st, Workspace ws, int* launches
         case F_NORM: return launch_norm(n, st, launches);
         case F_REDUCE: return launch_reduce(n, st, launches);
         case F_GEMM: return launch_gemm(n, st, ws, launches);
-        case F_ATTN: return launch_attention(n, st, launches);
+        case F_ATTN: return launch_attention(n, st, ws, launches);
         case F_LAYOUT: return launch_layout(n, st, launches);
         default: return Status::err(RT_ERR_BAD_OP, "no kernel for op");
     }
@@ -325,8 +326,8 @@ Status build_plan(const OpNode* nodes, int n, bool capture, Plan** out) {
     }
     cudaStream_t st = S().stream;
     for (int i = 0; i < n; i++) {
-        if (family_of(nodes[i].op) == F_GEMM) {
-            Status s = prepare_gemm(nodes[i], st);
+        if (family_of(nodes[i].op) == F_GEMM || family_of(nodes[i].op) == F_ATTN) {
+            Status s = family_of(nodes[i].op) == F_GEMM ? prepare_gemm(nodes[i], st) : prepare_attention(nodes[i]);
             if (!s.good()) {
                 free_plan(*plan);
                 return s;

@@ -172,6 +172,10 @@ ATT_CASES = [
     (2, 2, 1, 64, 128, 0, False),
     (1, 2, 2, 48, 80, 0, True),
     (1, 3, 3, 513, 64, 1, False),
+    (1, 2, 2, 1024, 128, 1, False),
+    (2, 4, 2, 256, 64, 0, False),
+    (1, 2, 2, 132, 64, 1, False),
+    (1, 4, 1, 640, 128, 0, False),
 ]
 
 
