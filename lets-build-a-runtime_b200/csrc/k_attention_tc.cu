@@ -7,10 +7,10 @@
 // stay at fp32 level; each P.V tile is accumulated in TMEM and folded into
 // fp32 registers, like the GEMM's K chunks.
 //
-// One CTA = 128 queries of one (batch, head); 320 threads:
-//   warp 0     TMA producer: per key tile (64 keys for D=64, 32 for D=128),
-//              K (hi/lo, [keys][D]) and V^T (hi/lo, [D][keys]) in
-//              128-byte-swizzled 32-float chunks, two slots each;
+// One CTA = 128 queries of one (batch, head); 352 threads:
+//   warps 0,10 producers (K and V separately): one contiguous bulk copy per
+//              key tile (64 keys for D=64, 32 for D=128) of a pre-packed,
+//              pre-swizzled image, two slots each;
 //   warp 1     allocates 512 TMEM columns and issues the MMAs from one
 //              thread in the order S_0, S_1, PV_0, S_2, PV_1, ... so the next
 //              score tile is computed while the softmax works on this one:
@@ -23,9 +23,10 @@
 //              mask, online softmax in log2 units (exp2f), write P hi/lo to
 //              TMEM, fold the previous O tile into registers, rescaling only
 //              when the running max grows.
-// TMEM columns: Q_hi [0,D) | S x2 | P_hi | P_lo | O tile.
-// K and V are split (and V transposed) into the node's workspace by a
-// bandwidth-bound pre-pass.  All waits are bounded (see sm100_ptx.h).
+// TMEM columns: Q_hi [0,D) | S x2 | (P_hi, P_lo) x2 | O tile.
+// K and V are split, V transposed and both packed into per-tile shared-memory
+// images in the node's workspace by a bandwidth-bound pre-pass
+// (pack_kv_kernel).  All waits are bounded (see sm100_ptx.h).
 #include <float.h>
 
 #include "gemm.h"
@@ -37,7 +38,7 @@ int* kernel_error_flag();
 
 namespace {
 
-constexpr int BQ = 128, SOFT_WARPS = 8, ATHREADS = 64 + 32 * SOFT_WARPS;
+constexpr int BQ = 128, SOFT_WARPS = 8, ATHREADS = 96 + 32 * SOFT_WARPS;   // K producer, MMA, softmax x8, V producer
 constexpr uint64_t WAIT_NS = 2000000000ull;
 constexpr int ERR_A_PROD = 0x201, ERR_A_MMA = 0x202, ERR_A_SOFT = 0x203, ERR_A_DRAIN = 0x204;
 
@@ -50,13 +51,14 @@ struct AttnTcCfg {
     static constexpr int K_SLOT = 2 * KH_BYTES, V_SLOT = 2 * VH_BYTES;
     static constexpr int SMEM = QL_BYTES + 2 * K_SLOT + 2 * V_SLOT + 1024 + 256 + 6 * BQ * 4;
     // TMEM columns
-    static constexpr uint32_t COL_S = D, COL_PH = D + 2 * BKV, COL_PL = D + 3 * BKV, COL_O = D + 4 * BKV;
-    static_assert(2 * D + 4 * BKV <= 512, "TMEM budget");
+    // S x2 | (P_hi, P_lo) x2 | O tile
+    static constexpr uint32_t COL_S = D, COL_P = D + 2 * BKV, COL_O = D + 6 * BKV;
+    static_assert(2 * D + 6 * BKV <= 512, "TMEM budget");
 };
 
 struct AttnTcParams {
-    CUtensorMap tk_hi, tk_lo;   // {D, S, BHkv}, box {32, BKV}
-    CUtensorMap tv_hi, tv_lo;   // {S, D, BHkv}, box {32, D}
+    const uint8_t* kv;          // packed tiles: [BHkv][n_kv][K image | V image] (pack_kv_kernel)
+    int n_kv;                   // key tiles per head
     const float* q;
     float* o;
     int S, group, causal, n_qblocks;
@@ -115,10 +117,6 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
         *abort_flag = 0;
         k_issued[0] = k_issued[1] = v_issued[0] = v_issued[1] = -1;
         ptx::fence_mbar_init();
-        ptx::prefetch_tmap(&p.tk_hi);
-        ptx::prefetch_tmap(&p.tk_lo);
-        ptx::prefetch_tmap(&p.tv_hi);
-        ptx::prefetch_tmap(&p.tv_lo);
     }
     if (warp == 1) ptx::tmem_alloc(tmem_slot, 512);
     ptx::tc_fence_before();
@@ -126,30 +124,26 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
     ptx::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 0) {
-        // ---------------------------------------------------- TMA producer
+    if (warp == 0 || warp == 2 + SOFT_WARPS) {
+        // ---------------------------------------------------- TMA producers
+        // K and V tiles come from separate warps so that K loads run ahead:
+        // a K slot frees when its S tile is done, a V slot only after P.V.
+        const bool is_k = warp == 0;
         if (lane == 0) {
             for (int j = 0; j < n_tiles; j++) {
                 const int slot = j & 1;
                 const uint32_t par = ((j >> 1) & 1) ^ 1;
-                const int k0 = j * BKV;
-                uint8_t* kh = kbuf + slot * C::K_SLOT;
-                uint8_t* vh = vbuf + slot * C::V_SLOT;
-                if (!ptx::wait_bounded(&k_empty[slot], par, abort_flag, p.err, ERR_A_PROD, WAIT_NS)) break;
-                ptx::mbar_expect_tx(&k_full[slot], C::K_SLOT);
-                k_issued[slot] = (j >> 1) & 1;
-#pragma unroll
-                for (int c = 0; c < D / 32; c++) {
-                    ptx::tma_load_3d(kh + c * BKV * 128, &p.tk_hi, &k_full[slot], c * 32, k0, bhkv);
-                    ptx::tma_load_3d(kh + C::KH_BYTES + c * BKV * 128, &p.tk_lo, &k_full[slot], c * 32, k0, bhkv);
-                }
-                if (!ptx::wait_bounded(&v_empty[slot], par, abort_flag, p.err, ERR_A_PROD, WAIT_NS)) break;
-                ptx::mbar_expect_tx(&v_full[slot], C::V_SLOT);
-                v_issued[slot] = (j >> 1) & 1;
-#pragma unroll
-                for (int c = 0; c < BKV / 32; c++) {
-                    ptx::tma_load_3d(vh + c * D * 128, &p.tv_hi, &v_full[slot], k0 + c * 32, 0, bhkv);
-                    ptx::tma_load_3d(vh + C::VH_BYTES + c * D * 128, &p.tv_lo, &v_full[slot], k0 + c * 32, 0, bhkv);
+                const uint8_t* tile = p.kv + ((size_t)bhkv * p.n_kv + j) * (C::K_SLOT + C::V_SLOT);
+                if (is_k) {
+                    if (!ptx::wait_bounded(&k_empty[slot], par, abort_flag, p.err, ERR_A_PROD, WAIT_NS)) break;
+                    ptx::mbar_expect_tx(&k_full[slot], C::K_SLOT);
+                    k_issued[slot] = (j >> 1) & 1;
+                    ptx::bulk_load(kbuf + slot * C::K_SLOT, tile, C::K_SLOT, &k_full[slot]);
+                } else {
+                    if (!ptx::wait_bounded(&v_empty[slot], par, abort_flag, p.err, ERR_A_PROD, WAIT_NS)) break;
+                    ptx::mbar_expect_tx(&v_full[slot], C::V_SLOT);
+                    v_issued[slot] = (j >> 1) & 1;
+                    ptx::bulk_load(vbuf + slot * C::V_SLOT, tile + C::K_SLOT, C::V_SLOT, &v_full[slot]);
                 }
             }
         }
@@ -168,16 +162,18 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
                 ptx::tc_fence_after();
                 const uint8_t* kh = kbuf + slot * C::K_SLOT;
                 const uint32_t d_s = tmem + C::COL_S + slot * BKV;
+                // descriptors built once per tile; K steps advance the start address field
+                const uint64_t bh0 = ptx::smem_desc(kh, 1024, 2);
+                const uint64_t bl0 = ptx::smem_desc(kh + C::KH_BYTES, 1024, 2);
+                const uint64_t al0 = ptx::smem_desc(ql, 1024, 2);
 #pragma unroll
                 for (int kk = 0; kk < D / 8; kk++) {
-                    const int c = kk >> 2, off = (kk & 3) * 32;
-                    uint64_t b_hi = ptx::smem_desc(kh + c * BKV * 128 + off, 1024, 2);
-                    uint64_t b_lo = ptx::smem_desc(kh + C::KH_BYTES + c * BKV * 128 + off, 1024, 2);
-                    uint64_t a_lo = ptx::smem_desc(ql + c * BQ * 128 + off, 1024, 2);
+                    const uint64_t boff = (uint64_t)(((kk >> 2) * BKV * 128 + (kk & 3) * 32) >> 4);
+                    const uint64_t aoff = (uint64_t)(((kk >> 2) * BQ * 128 + (kk & 3) * 32) >> 4);
                     const uint32_t a_hi = tmem + kk * 8;
-                    ptx::mma_tf32_ts(d_s, a_hi, b_hi, idesc_s, kk > 0 ? 1u : 0u);
-                    ptx::mma_tf32_ts(d_s, a_hi, b_lo, idesc_s, 1u);
-                    ptx::mma_tf32(d_s, a_lo, b_hi, idesc_s, 1u);
+                    ptx::mma_tf32_ts(d_s, a_hi, bh0 + boff, idesc_s, kk > 0 ? 1u : 0u);
+                    ptx::mma_tf32_ts(d_s, a_hi, bl0 + boff, idesc_s, 1u);
+                    ptx::mma_tf32(d_s, al0 + aoff, bh0 + boff, idesc_s, 1u);
                 }
                 ptx::mma_commit(&k_empty[slot]);
                 ptx::mma_commit(&s_full[slot]);
@@ -194,14 +190,15 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
                     break;
                 ptx::tc_fence_after();
                 const uint8_t* vh = vbuf + slot * C::V_SLOT;
+                const uint32_t p_hi = tmem + C::COL_P + (j & 1) * 2 * BKV, p_lo = p_hi + BKV;
+                const uint64_t vh0 = ptx::smem_desc(vh, 1024, 2);
+                const uint64_t vl0 = ptx::smem_desc(vh + C::VH_BYTES, 1024, 2);
 #pragma unroll
                 for (int kk = 0; kk < BKV / 8; kk++) {
-                    const int c = kk >> 2, off = (kk & 3) * 32;
-                    uint64_t b_hi = ptx::smem_desc(vh + c * D * 128 + off, 1024, 2);
-                    uint64_t b_lo = ptx::smem_desc(vh + C::VH_BYTES + c * D * 128 + off, 1024, 2);
-                    ptx::mma_tf32_ts(tmem + C::COL_O, tmem + C::COL_PH + kk * 8, b_hi, idesc_o, kk > 0 ? 1u : 0u);
-                    ptx::mma_tf32_ts(tmem + C::COL_O, tmem + C::COL_PH + kk * 8, b_lo, idesc_o, 1u);
-                    ptx::mma_tf32_ts(tmem + C::COL_O, tmem + C::COL_PL + kk * 8, b_hi, idesc_o, 1u);
+                    const uint64_t off = (uint64_t)(((kk >> 2) * D * 128 + (kk & 3) * 32) >> 4);
+                    ptx::mma_tf32_ts(tmem + C::COL_O, p_hi + kk * 8, vh0 + off, idesc_o, kk > 0 ? 1u : 0u);
+                    ptx::mma_tf32_ts(tmem + C::COL_O, p_hi + kk * 8, vl0 + off, idesc_o, 1u);
+                    ptx::mma_tf32_ts(tmem + C::COL_O, p_lo + kk * 8, vh0 + off, idesc_o, 1u);
                 }
                 ptx::mma_commit(&v_empty[slot]);
                 ptx::mma_commit(pv_full);
@@ -212,7 +209,7 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
         }
         __syncwarp();
     } else {
-        // ---------------------------------------------------- softmax rows
+        // ---------------------------------------------------- softmax rows (warps 2 .. 1+SOFT_WARPS)
         // Two threads per query row (warps w and w+4 share TMEM lanes): each
         // owns half of the row's scores and half of its output columns.
         const int quarter = warp & 3;
@@ -274,13 +271,14 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
             // every key of this half-tile valid for this row: no mask arithmetic
             const bool full = k0 + KH <= p.S && (!p.causal || k0 + KH - 1 <= q);
             float sv[KH];
+            {
+                uint32_t r[KH];
 #pragma unroll
-            for (int c16 = 0; c16 < KH / 16; c16++) {
-                uint32_t r[16];
-                ptx::tmem_ld16(tmem + lane_off + s_col + c16 * 16, r);
+                for (int c16 = 0; c16 < KH / 16; c16++)
+                    ptx::tmem_ld16(tmem + lane_off + s_col + c16 * 16, *reinterpret_cast<uint32_t(*)[16]>(&r[c16 * 16]));
                 ptx::tmem_ld_wait();
 #pragma unroll
-                for (int i = 0; i < 16; i++) sv[c16 * 16 + i] = __uint_as_float(r[i]) * sl2;
+                for (int i = 0; i < KH; i++) sv[i] = __uint_as_float(r[i]) * sl2;
             }
             float mt = -INFINITY;
             if (full) {
@@ -297,39 +295,45 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
             red[((j & 1) * 2 + half) * BQ + row] = mt;
             if (!(ok = pair_sync(j & 1, (j >> 1) & 1))) break;
             mt = fmaxf(mt, red[((j & 1) * 2 + (half ^ 1)) * BQ + row]);
-            if (j > 0) {   // O tile j-1: fold into registers (also frees P and the O tile)
-                if (!(ok = ptx::wait_bounded(pv_full, (j - 1) & 1, abort_flag, p.err, ERR_A_SOFT, WAIT_NS))) break;
-                ptx::tc_fence_after();
-#pragma unroll
-                for (int c16 = 0; c16 < DH / 16; c16++) {
-                    uint32_t r[16];
-                    ptx::tmem_ld16(tmem + lane_off + C::COL_O + half * DH + c16 * 16, r);
-                    ptx::tmem_ld_wait();
-#pragma unroll
-                    for (int i = 0; i < 16; i++) o[c16 * 16 + i] += __uint_as_float(r[i]);
-                }
-            }
-            if (mt > m) {   // running max grows: rescale (corr would be 1 otherwise)
-                const float corr = exp2f(m - mt);
-                l *= corr;
-#pragma unroll
-                for (int i = 0; i < DH; i++) o[i] *= corr;
-                m = mt;
-            }
+            const float m_new = mt > m ? mt : m;
+            // P_j (relative to m_new) into P buffer j&1; that buffer's last reader,
+            // PV_{j-2}, finished before this thread's previous p_full arrive
+            const uint32_t p_hi = tmem + lane_off + C::COL_P + (j & 1) * 2 * BKV + half * KH;
+            float lt = 0.0f;
 #pragma unroll
             for (int c16 = 0; c16 < KH / 16; c16++) {
                 uint32_t ph[16], pl[16];
 #pragma unroll
                 for (int i = 0; i < 16; i++) {
-                    float pv = exp2f(sv[c16 * 16 + i] - m);   // masked: 2^-inf = 0
-                    l += pv;
+                    float pv = exp2f(sv[c16 * 16 + i] - m_new);   // masked: 2^-inf = 0
+                    lt += pv;
                     float h = tf32_round(pv);
                     ph[i] = __float_as_uint(h);
                     pl[i] = __float_as_uint(pv - h);
                 }
-                ptx::tmem_st16(tmem + lane_off + C::COL_PH + half * KH + c16 * 16, ph);
-                ptx::tmem_st16(tmem + lane_off + C::COL_PL + half * KH + c16 * 16, pl);
+                ptx::tmem_st16(p_hi + c16 * 16, ph);
+                ptx::tmem_st16(p_hi + BKV + c16 * 16, pl);
             }
+            if (j > 0) {   // O tile j-1 (relative to the old max): fold into registers, freeing the tile
+                if (!(ok = ptx::wait_bounded(pv_full, (j - 1) & 1, abort_flag, p.err, ERR_A_SOFT, WAIT_NS))) break;
+                ptx::tc_fence_after();
+                uint32_t r[DH];
+#pragma unroll
+                for (int c16 = 0; c16 < DH / 16; c16++)
+                    ptx::tmem_ld16(tmem + lane_off + C::COL_O + half * DH + c16 * 16,
+                                   *reinterpret_cast<uint32_t(*)[16]>(&r[c16 * 16]));
+                ptx::tmem_ld_wait();
+#pragma unroll
+                for (int i = 0; i < DH; i++) o[i] += __uint_as_float(r[i]);
+            }
+            if (m_new > m) {   // running max grew: rescale (corr would be 1 otherwise)
+                const float corr = exp2f(m - m_new);
+                l *= corr;
+#pragma unroll
+                for (int i = 0; i < DH; i++) o[i] *= corr;
+                m = m_new;
+            }
+            l += lt;
             ptx::tmem_st_wait();
             ptx::tc_fence_before();
             ptx::mbar_arrive(p_full);
@@ -337,13 +341,15 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
         if (ok && n_tiles > 0 &&
             ptx::wait_bounded(pv_full, (n_tiles - 1) & 1, abort_flag, p.err, ERR_A_SOFT, WAIT_NS)) {
             ptx::tc_fence_after();
+            {
+                uint32_t r[DH];
 #pragma unroll
-            for (int c16 = 0; c16 < DH / 16; c16++) {
-                uint32_t r[16];
-                ptx::tmem_ld16(tmem + lane_off + C::COL_O + half * DH + c16 * 16, r);
+                for (int c16 = 0; c16 < DH / 16; c16++)
+                    ptx::tmem_ld16(tmem + lane_off + C::COL_O + half * DH + c16 * 16,
+                                   *reinterpret_cast<uint32_t(*)[16]>(&r[c16 * 16]));
                 ptx::tmem_ld_wait();
 #pragma unroll
-                for (int i = 0; i < 16; i++) o[c16 * 16 + i] += __uint_as_float(r[i]);
+                for (int i = 0; i < DH; i++) o[i] += __uint_as_float(r[i]);
             }
             red[(4 + half) * BQ + row] = l;
             const bool paired = pair_sync(2, 0);
@@ -376,6 +382,44 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
     }
 }
 
+// Packs K and V into per-tile images that are byte-for-byte the shared-memory
+// layout the MMA reads (K: [D/32 chunks][BKV keys][128 B], V^T: [BKV/32
+// chunks][D][128 B]; 16-byte units swizzled by row % 8 as the 128-byte
+// swizzle mode expects; hi then lo), so each tile is one contiguous bulk copy.
+// Keys past S are zero.
+template <int D>
+__global__ void pack_kv_kernel(const float* __restrict__ k, const float* __restrict__ v,
+                               uint8_t* __restrict__ out, int S, int n_kv) {
+    using C = AttnTcCfg<D>;
+    constexpr int BKV = C::BKV;
+    const int j = blockIdx.x, h = blockIdx.y;
+    const int k0 = j * BKV;
+    uint8_t* tile = out + ((size_t)h * n_kv + j) * (C::K_SLOT + C::V_SLOT);
+    const float* kb = k + (size_t)h * S * D;
+    const float* vb = v + (size_t)h * S * D;
+    for (int e = threadIdx.x; e < BKV * D; e += blockDim.x) {
+        const int r = e / D, d = e % D;   // key within tile, feature
+        const bool ok = k0 + r < S;
+        const float kx = ok ? kb[(size_t)(k0 + r) * D + d] : 0.0f;
+        const float vx = ok ? vb[(size_t)(k0 + r) * D + d] : 0.0f;
+        const float kh = tf32_round(kx), vh = tf32_round(vx);
+        // K image: chunk d/32, row r, unit (d%32)/4
+        {
+            const int c = d >> 5, w = d & 31;
+            const size_t off = (size_t)c * BKV * 128 + r * 128 + ((((w >> 2) ^ (r & 7))) << 4) + (w & 3) * 4;
+            *reinterpret_cast<float*>(tile + off) = kh;
+            *reinterpret_cast<float*>(tile + C::KH_BYTES + off) = kx - kh;
+        }
+        // V^T image: chunk r/32, row d, unit (r%32)/4
+        {
+            const int c = r >> 5, w = r & 31;
+            const size_t off = (size_t)c * D * 128 + d * 128 + ((((w >> 2) ^ (d & 7))) << 4) + (w & 3) * 4;
+            *reinterpret_cast<float*>(tile + C::K_SLOT + off) = vh;
+            *reinterpret_cast<float*>(tile + C::K_SLOT + C::VH_BYTES + off) = vx - vh;
+        }
+    }
+}
+
 template <int D>
 Status launch_tc(const AttnTcParams& prm, int BH, cudaStream_t st) {
     dim3 grid((unsigned)prm.n_qblocks, (unsigned)BH);
@@ -392,7 +436,12 @@ bool attention_tc_applicable(int64_t S, int D, bool has_mask, int64_t BH) {
     return !has_mask && (D == 64 || D == 128) && S % 4 == 0 && S >= 128 && BH <= 65535 && S < (1 << 30);
 }
 
-size_t attention_tc_workspace(int64_t BHkv, int64_t S, int D) { return 4 * (size_t)BHkv * S * D * 4 + 4 * 256; }
+size_t attention_tc_workspace(int64_t BHkv, int64_t S, int D) {
+    const int bkv = D == 128 ? AttnTcCfg<128>::BKV : AttnTcCfg<64>::BKV;
+    const size_t tile = D == 128 ? AttnTcCfg<128>::K_SLOT + AttnTcCfg<128>::V_SLOT
+                                 : AttnTcCfg<64>::K_SLOT + AttnTcCfg<64>::V_SLOT;
+    return (size_t)BHkv * ((S + bkv - 1) / bkv) * tile;
+}
 
 Status attention_tc_prepare() {
     static bool done = false;
@@ -409,23 +458,20 @@ Status attention_tc_prepare() {
 Status launch_attention_tc(const float* q, const float* k, const float* v, float* o, int64_t BH, int64_t S,
                            int D, int group, int causal, Workspace ws, cudaStream_t st, int* launches) {
     const int64_t BHkv = BH / group;
-    const size_t part = (((size_t)BHkv * S * D * 4) + 255) & ~(size_t)255;
-    if (ws.bytes < 4 * part) return Status::err(RT_ERR_ARGUMENT, "attention: workspace too small");
-    float* khi = reinterpret_cast<float*>(ws.base);
-    float* klo = reinterpret_cast<float*>(ws.base + part);
-    float* vhi = reinterpret_cast<float*>(ws.base + 2 * part);
-    float* vlo = reinterpret_cast<float*>(ws.base + 3 * part);
-    Status s = split_operand(k, khi, klo, 1, BHkv * S, D, false, st);
-    if (!s.good()) return s;
-    s = split_operand(v, vhi, vlo, BHkv, D, S, true, st);   // [BHkv][S][D] -> [BHkv][D][S]
-    if (!s.good()) return s;
-    *launches += 2;
+    if (ws.bytes < attention_tc_workspace(BHkv, S, D)) return Status::err(RT_ERR_ARGUMENT, "attention: workspace too small");
+    const int bkv = D == 128 ? AttnTcCfg<128>::BKV : AttnTcCfg<64>::BKV;
+    const int n_kv = (int)((S + bkv - 1) / bkv);
+    dim3 pgrid((unsigned)n_kv, (unsigned)BHkv);
+    if (D == 64)
+        pack_kv_kernel<64><<<pgrid, 256, 0, st>>>(k, v, reinterpret_cast<uint8_t*>(ws.base), (int)S, n_kv);
+    else
+        pack_kv_kernel<128><<<pgrid, 256, 0, st>>>(k, v, reinterpret_cast<uint8_t*>(ws.base), (int)S, n_kv);
+    RT_LAUNCH_CHECK();
+    *launches += 1;
     AttnTcParams prm;
     memset(&prm, 0, sizeof prm);
-    if (!(s = encode_tmap_f32_3d(&prm.tk_hi, khi, D, S, BHkv, 32, D == 128 ? 32 : 64, 128)).good()) return s;
-    if (!(s = encode_tmap_f32_3d(&prm.tk_lo, klo, D, S, BHkv, 32, D == 128 ? 32 : 64, 128)).good()) return s;
-    if (!(s = encode_tmap_f32_3d(&prm.tv_hi, vhi, S, D, BHkv, 32, D, 128)).good()) return s;
-    if (!(s = encode_tmap_f32_3d(&prm.tv_lo, vlo, S, D, BHkv, 32, D, 128)).good()) return s;
+    prm.kv = reinterpret_cast<const uint8_t*>(ws.base);
+    prm.n_kv = n_kv;
     prm.q = q;
     prm.o = o;
     prm.S = (int)S;
