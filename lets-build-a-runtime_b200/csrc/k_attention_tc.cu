@@ -4,29 +4,31 @@
 // scores = (Q K^T) * 1/sqrtf(D), causal mask as -inf, online softmax with
 // running max starting at -FLT_MAX, O = P V / l, GQA kv head = bh / group.
 // Both products run as 3xTF32 on tcgen05 (hi.hi + hi.lo + lo.hi) so results
-// stay at fp32 level; each P.V tile is accumulated in TMEM and folded into
-// fp32 registers, like the GEMM's K chunks.
+// stay at fp32 level; each P.V tile (128 keys) is accumulated in TMEM and
+// folded into fp32 registers, like the GEMM's K chunks.
 //
-// One CTA = 128 queries of one (batch, head); 352 threads:
-//   warps 0,10 producers (K and V separately): one contiguous bulk copy per
-//              key tile (64 keys for D=64, 32 for D=128) of a pre-packed,
-//              pre-swizzled image, two slots each;
-//   warp 1     allocates 512 TMEM columns and issues the MMAs from one
-//              thread in the order S_0, S_1, PV_0, S_2, PV_1, ... so the next
-//              score tile is computed while the softmax works on this one:
-//              S = Q_hi.K_hi + Q_hi.K_lo (A from TMEM) + Q_lo.K_hi (A from
-//              shared memory); O_tile = P_hi.V_hi + P_hi.V_lo + P_lo.V_hi;
-//   warps 2-9  two threads per query row (half of the scores and half of
-//              the output columns each; row maxima and sums exchanged through
-//              shared memory behind bounded mbarrier waits): stage Q (hi to
-//              TMEM, lo to shared memory), then per tile read S from TMEM,
-//              mask, online softmax in log2 units (exp2f), write P hi/lo to
-//              TMEM, fold the previous O tile into registers, rescaling only
-//              when the running max grows.
-// TMEM columns: Q_hi [0,D) | S x2 | (P_hi, P_lo) x2 | O tile.
-// K and V are split, V transposed and both packed into per-tile shared-memory
-// images in the node's workspace by a bandwidth-bound pre-pass
-// (pack_kv_kernel).  All waits are bounded (see sm100_ptx.h).
+// Tiles are 128 queries x 128 keys, so every score MMA is M=128 x N=128
+// (narrower MMAs are dominated by per-instruction cost on this hardware).
+// One CTA = 128 queries of one (batch, head); 320 threads:
+//   warp 0     producer: streams 32 KiB chunks through a shared-memory ring in
+//              exactly the order the MMAs consume them -- K_0, K_1, V_0, K_2,
+//              V_1, ... (K tile = D/32 chunks of 32 features x 128 keys, V^T
+//              tile = chunks of 32 or 64 keys x D), each chunk one contiguous
+//              bulk copy of a pre-packed, pre-swizzled image;
+//   warp 1     allocates TMEM and issues the MMAs from one thread:
+//              S = Q_hi.K_hi + Q_hi.K_lo + Q_lo.K_hi (Q from shared memory),
+//              O_tile = P_hi.V_hi + P_hi.V_lo + P_lo.V_hi (P from TMEM);
+//              S_{j+1} runs while the softmax works on S_j;
+//   warps 2-9  two threads per query row (64 keys and D/2 output columns
+//              each; row maxima / sums exchanged through shared memory behind
+//              bounded mbarrier waits): stage Q hi/lo into shared memory, then
+//              per tile read S from TMEM (freeing it), mask, online softmax in
+//              log2 units, fold the previous O tile into registers, write P
+//              hi/lo to TMEM.
+// TMEM columns: S [0,128) | P_hi [128,256) | P_lo [256,384) | O tile [384, 384+D).
+// K and V are split, V transposed and both packed into per-tile images in the
+// node's workspace by a bandwidth-bound pre-pass (pack_kv_kernel).  All waits
+// are bounded (see sm100_ptx.h).
 #include <float.h>
 
 #include "gemm.h"
@@ -38,27 +40,29 @@ int* kernel_error_flag();
 
 namespace {
 
-constexpr int BQ = 128, SOFT_WARPS = 8, ATHREADS = 96 + 32 * SOFT_WARPS;   // K producer, MMA, softmax x8, V producer
+constexpr int BQ = 128, BKV = 128, SOFT_WARPS = 8, ATHREADS = 64 + 32 * SOFT_WARPS;
+constexpr int CHUNK = 32 * 1024;                      // ring stage / packed chunk
 constexpr uint64_t WAIT_NS = 2000000000ull;
 constexpr int ERR_A_PROD = 0x201, ERR_A_MMA = 0x202, ERR_A_SOFT = 0x203, ERR_A_DRAIN = 0x204;
+constexpr uint32_t COL_S = 0, COL_PH = 128, COL_PL = 256, COL_O = 384;
 
 template <int D>
 struct AttnTcCfg {
-    static constexpr int BKV = D == 128 ? 32 : 64;       // keys per tile
-    static constexpr int QL_BYTES = D * BQ * 4;          // Q_lo, D/32 chunks of [128 rows][128 B]
-    static constexpr int KH_BYTES = D * BKV * 4;         // one of K_hi / K_lo, one slot
-    static constexpr int VH_BYTES = BKV * D * 4;         // one of V_hi / V_lo, one slot
-    static constexpr int K_SLOT = 2 * KH_BYTES, V_SLOT = 2 * VH_BYTES;
-    static constexpr int SMEM = QL_BYTES + 2 * K_SLOT + 2 * V_SLOT + 1024 + 256 + 6 * BQ * 4;
-    // TMEM columns
-    // S x2 | (P_hi, P_lo) x2 | O tile
-    static constexpr uint32_t COL_S = D, COL_P = D + 2 * BKV, COL_O = D + 6 * BKV;
-    static_assert(2 * D + 6 * BKV <= 512, "TMEM budget");
+    static constexpr int Q_BYTES = D * BQ * 4;                  // one of Q_hi / Q_lo: D/32 x [128][128 B]
+    static constexpr int K_CHUNKS = D / 32;                     // 32 features x 128 keys, hi | lo
+    static constexpr int V_KEYS = D == 128 ? 32 : 64;           // keys per V chunk (D x keys, hi | lo)
+    static constexpr int V_CHUNKS = BKV / V_KEYS;
+    static constexpr int TILE_BYTES = (K_CHUNKS + V_CHUNKS) * CHUNK;
+    static constexpr int STAGES = D == 128 ? 3 : 5;
+    static constexpr int BODY = 2 * Q_BYTES + STAGES * CHUNK + 256 /*barriers*/ + 4 * BQ * 4 /*row exchange*/;
+    static constexpr int SMEM = BODY + 768;   // + alignment slack; 232448 B, the per-CTA maximum
+    static_assert(SMEM <= 232448, "shared memory budget");
+    static_assert(COL_O + D <= 512, "TMEM budget");
 };
 
 struct AttnTcParams {
-    const uint8_t* kv;          // packed tiles: [BHkv][n_kv][K image | V image] (pack_kv_kernel)
-    int n_kv;                   // key tiles per head
+    const uint8_t* kv;   // packed tiles [BHkv][n_kv][K chunks | V chunks]
+    int n_kv;            // key tiles per head
     const float* q;
     float* o;
     int S, group, causal, n_qblocks;
@@ -72,50 +76,108 @@ __device__ __forceinline__ float tf32_round(float x) {
     return __uint_as_float(r);
 }
 
-// Tile schedule (MMA issue order): S_0, S_1, PV_0, S_2, PV_1, ... so that
-// S_{j+1} runs on the tensor cores while the softmax threads work on S_j.
+// Byte offset of element (row, w) -- w = 0..31 within a 128-byte row -- in a
+// [rows][128 B] block written the way the 128-byte swizzle mode reads it.
+__device__ __forceinline__ uint32_t swz(int row, int w) {
+    return (uint32_t)row * 128 + ((((uint32_t)w >> 2) ^ ((uint32_t)row & 7)) << 4) + ((uint32_t)w & 3) * 4;
+}
+
+// Packs K (as [K chunk c: 128 keys x 32 features]) and V^T (as [V chunk c:
+// D x V_KEYS keys, in 32-key sub-blocks]) of one 128-key tile, hi then lo in
+// each chunk, byte-for-byte the shared-memory image the MMAs read.  Keys
+// past S are zero.  Every store is a whole 16-byte unit; V is transposed
+// through shared memory 32 keys at a time so its global reads stay coalesced.
+template <int D>
+__global__ void __launch_bounds__(256) pack_kv_kernel(const float* __restrict__ k, const float* __restrict__ v,
+                                                      uint8_t* __restrict__ out, int S, int n_kv) {
+    using C = AttnTcCfg<D>;
+    __shared__ float sv[32][D + 1];
+    const int j = blockIdx.x, h = blockIdx.y;
+    const int k0 = j * BKV;
+    uint8_t* tile = out + ((size_t)h * n_kv + j) * C::TILE_BYTES;
+    const float* kb = k + (size_t)h * S * D;
+    const float* vb = v + (size_t)h * S * D;
+    // K: unit = 4 consecutive features of one key
+    for (int u = threadIdx.x; u < BKV * D / 4; u += blockDim.x) {
+        const int r = u / (D / 4), d = (u % (D / 4)) * 4;
+        float4 x = k0 + r < S ? *reinterpret_cast<const float4*>(kb + (size_t)(k0 + r) * D + d)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        float4 hi = make_float4(tf32_round(x.x), tf32_round(x.y), tf32_round(x.z), tf32_round(x.w));
+        uint8_t* kc = tile + (size_t)(d >> 5) * CHUNK + swz(r, d & 31);
+        *reinterpret_cast<float4*>(kc) = hi;
+        *reinterpret_cast<float4*>(kc + CHUNK / 2) = make_float4(x.x - hi.x, x.y - hi.y, x.z - hi.z, x.w - hi.w);
+    }
+    // V^T: unit = 4 consecutive keys of one feature
+    for (int kb32 = 0; kb32 < BKV; kb32 += 32) {
+        __syncthreads();
+        for (int u = threadIdx.x; u < 32 * D / 4; u += blockDim.x) {
+            const int r = u / (D / 4), d = (u % (D / 4)) * 4;
+            const int key = k0 + kb32 + r;
+            float4 x = key < S ? *reinterpret_cast<const float4*>(vb + (size_t)key * D + d)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+            sv[r][d] = x.x; sv[r][d + 1] = x.y; sv[r][d + 2] = x.z; sv[r][d + 3] = x.w;
+        }
+        __syncthreads();
+        const int vc = kb32 / C::V_KEYS, sub = (kb32 % C::V_KEYS) >> 5;
+        uint8_t* vcp = tile + (size_t)(C::K_CHUNKS + vc) * CHUNK + (size_t)sub * D * 128;
+        for (int u = threadIdx.x; u < D * 8; u += blockDim.x) {
+            const int d = u >> 3, w = (u & 7) * 4;
+            float4 x = make_float4(sv[w][d], sv[w + 1][d], sv[w + 2][d], sv[w + 3][d]);
+            float4 hi = make_float4(tf32_round(x.x), tf32_round(x.y), tf32_round(x.z), tf32_round(x.w));
+            uint8_t* dst = vcp + swz(d, w);
+            *reinterpret_cast<float4*>(dst) = hi;
+            *reinterpret_cast<float4*>(dst + CHUNK / 2) = make_float4(x.x - hi.x, x.y - hi.y, x.z - hi.z, x.w - hi.w);
+        }
+    }
+}
+
 template <int D>
 __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_constant__ AttnTcParams p) {
     using C = AttnTcCfg<D>;
-    constexpr int BKV = C::BKV;
+    constexpr int STAGES = C::STAGES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem =
         reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    uint8_t* ql = smem;
-    uint8_t* kbuf = ql + C::QL_BYTES;           // 2 slots: [hi | lo]
-    uint8_t* vbuf = kbuf + 2 * C::K_SLOT;       // 2 slots: [hi | lo]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(vbuf + 2 * C::V_SLOT);
-    uint64_t* k_full = bars + 0;    // [2]
-    uint64_t* k_empty = bars + 2;   // [2]
-    uint64_t* v_full = bars + 4;    // [2]
-    uint64_t* v_empty = bars + 6;   // [2]
-    uint64_t* s_full = bars + 8;    // [2]
-    uint64_t* q_ready = bars + 10;
-    uint64_t* p_full = bars + 11;
-    uint64_t* pv_full = bars + 12;
-    uint64_t* drain = bars + 13;
-    uint64_t* pair_bar = bars + 14;   // [4 quarters][3]: row-pair exchange, tiles even/odd + final
-    constexpr int NBAR = 26;
+    uint8_t* qh = smem;
+    uint8_t* ql = qh + C::Q_BYTES;
+    uint8_t* ring = ql + C::Q_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(ring + STAGES * CHUNK);
+    uint64_t* full = bars;                        // [STAGES]
+    uint64_t* empty = bars + STAGES;              // [STAGES]
+    uint64_t* s_full = bars + 2 * STAGES;
+    uint64_t* s_free = s_full + 1;
+    uint64_t* p_full = s_full + 2;
+    uint64_t* pv_full = s_full + 3;
+    uint64_t* q_ready = s_full + 4;
+    uint64_t* drain = s_full + 5;
+    uint64_t* pair_bar = s_full + 6;              // [4 quarters][3]
+    constexpr int NBAR = 2 * STAGES + 6 + 12;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NBAR);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    int* k_issued = const_cast<int*>(abort_flag) + 1;   // [2] phase of the last load per slot, -1 none
-    int* v_issued = k_issued + 2;                       // [2]
-    // partial row maxima / sums exchanged by the two threads of a row: [tile even | odd | final][2 halves][128 rows]
-    float* red = reinterpret_cast<float*>(smem + C::QL_BYTES + 2 * C::K_SLOT + 2 * C::V_SLOT + 256);
+    int* issued = const_cast<int*>(abort_flag) + 1;    // [STAGES] phase of the last load, -1 none
+    float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);   // [2][2][128]
+    if ((smem - smem_raw) + C::BODY > C::SMEM) {   // dynamic shared memory less aligned than assumed
+        if (threadIdx.x == 0 && p.err) atomicCAS(p.err, 0, 0x205);
+        return;
+    }
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int bh = blockIdx.y;
     const int qb = p.causal ? p.n_qblocks - 1 - (int)blockIdx.x : (int)blockIdx.x;   // long rows first
     const int q0 = qb * BQ;
     const int bhkv = bh / p.group;
-    int kv_len = p.S;
-    if (p.causal) kv_len = min(p.S, q0 + BQ);
+    const int kv_len = p.causal ? min(p.S, q0 + BQ) : p.S;
     const int n_tiles = (kv_len + BKV - 1) / BKV;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < NBAR; i++) ptx::mbar_init(&bars[i], (i == 10 || i == 11) ? 32 * SOFT_WARPS : i >= 14 ? 64 : 1);
+        for (int i = 0; i < NBAR; i++) {
+            uint32_t cnt = 1;
+            if (&bars[i] == s_free || &bars[i] == p_full || &bars[i] == q_ready) cnt = 32 * SOFT_WARPS;
+            if (&bars[i] >= pair_bar) cnt = 64;
+            ptx::mbar_init(&bars[i], cnt);
+        }
+        for (int s = 0; s < STAGES; s++) issued[s] = -1;
         *abort_flag = 0;
-        k_issued[0] = k_issued[1] = v_issued[0] = v_issued[1] = -1;
         ptx::fence_mbar_init();
     }
     if (warp == 1) ptx::tmem_alloc(tmem_slot, 512);
@@ -124,27 +186,30 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
     ptx::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 0 || warp == 2 + SOFT_WARPS) {
-        // ---------------------------------------------------- TMA producers
-        // K and V tiles come from separate warps so that K loads run ahead:
-        // a K slot frees when its S tile is done, a V slot only after P.V.
-        const bool is_k = warp == 0;
+    if (warp == 0) {
+        // ---------------------------------------------------- producer
         if (lane == 0) {
-            for (int j = 0; j < n_tiles; j++) {
-                const int slot = j & 1;
-                const uint32_t par = ((j >> 1) & 1) ^ 1;
-                const uint8_t* tile = p.kv + ((size_t)bhkv * p.n_kv + j) * (C::K_SLOT + C::V_SLOT);
-                if (is_k) {
-                    if (!ptx::wait_bounded(&k_empty[slot], par, abort_flag, p.err, ERR_A_PROD, WAIT_NS)) break;
-                    ptx::mbar_expect_tx(&k_full[slot], C::K_SLOT);
-                    k_issued[slot] = (j >> 1) & 1;
-                    ptx::bulk_load(kbuf + slot * C::K_SLOT, tile, C::K_SLOT, &k_full[slot]);
-                } else {
-                    if (!ptx::wait_bounded(&v_empty[slot], par, abort_flag, p.err, ERR_A_PROD, WAIT_NS)) break;
-                    ptx::mbar_expect_tx(&v_full[slot], C::V_SLOT);
-                    v_issued[slot] = (j >> 1) & 1;
-                    ptx::bulk_load(vbuf + slot * C::V_SLOT, tile + C::K_SLOT, C::V_SLOT, &v_full[slot]);
+            int stage = 0;
+            uint32_t ph = 0;
+            bool ok = true;
+            auto push = [&](const uint8_t* src) {
+                if (!ok) return;
+                if (!(ok = ptx::wait_bounded(&empty[stage], ph ^ 1, abort_flag, p.err, ERR_A_PROD, WAIT_NS)))
+                    return;
+                ptx::mbar_expect_tx(&full[stage], CHUNK);
+                issued[stage] = (int)ph;
+                ptx::bulk_load(ring + stage * CHUNK, src, CHUNK, &full[stage]);
+                if (++stage == STAGES) {
+                    stage = 0;
+                    ph ^= 1;
                 }
+            };
+            auto tile = [&](int j) { return p.kv + ((size_t)bhkv * p.n_kv + j) * C::TILE_BYTES; };
+            for (int c = 0; c < C::K_CHUNKS; c++) push(tile(0) + c * CHUNK);
+            for (int j = 0; j < n_tiles && ok; j++) {
+                if (j + 1 < n_tiles)
+                    for (int c = 0; c < C::K_CHUNKS; c++) push(tile(j + 1) + c * CHUNK);
+                for (int c = 0; c < C::V_CHUNKS; c++) push(tile(j) + (C::K_CHUNKS + c) * CHUNK);
             }
         }
     } else if (warp == 1) {
@@ -152,56 +217,72 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
         if (lane == 0) {
             constexpr uint32_t idesc_s = ptx::idesc_tf32(BQ, BKV);
             constexpr uint32_t idesc_o = ptx::idesc_tf32(BQ, D);
+            int stage = 0;
+            uint32_t ph = 0;
             bool ok = ptx::wait_bounded(q_ready, 0, abort_flag, p.err, ERR_A_MMA, WAIT_NS);
             ptx::tc_fence_after();
-            // S_j = Q.K_j^T into S buffer j&1
-            auto issue_s = [&](int j) -> bool {
-                const int slot = j & 1;
-                if (!ptx::wait_bounded(&k_full[slot], (j >> 1) & 1, abort_flag, p.err, ERR_A_MMA, WAIT_NS))
-                    return false;
+            auto pop = [&]() -> uint8_t* {
+                if (!ok) return nullptr;
+                if (!(ok = ptx::wait_bounded(&full[stage], ph, abort_flag, p.err, ERR_A_MMA, WAIT_NS)))
+                    return nullptr;
                 ptx::tc_fence_after();
-                const uint8_t* kh = kbuf + slot * C::K_SLOT;
-                const uint32_t d_s = tmem + C::COL_S + slot * BKV;
-                // descriptors built once per tile; K steps advance the start address field
-                const uint64_t bh0 = ptx::smem_desc(kh, 1024, 2);
-                const uint64_t bl0 = ptx::smem_desc(kh + C::KH_BYTES, 1024, 2);
-                const uint64_t al0 = ptx::smem_desc(ql, 1024, 2);
-#pragma unroll
-                for (int kk = 0; kk < D / 8; kk++) {
-                    const uint64_t boff = (uint64_t)(((kk >> 2) * BKV * 128 + (kk & 3) * 32) >> 4);
-                    const uint64_t aoff = (uint64_t)(((kk >> 2) * BQ * 128 + (kk & 3) * 32) >> 4);
-                    const uint32_t a_hi = tmem + kk * 8;
-                    ptx::mma_tf32_ts(d_s, a_hi, bh0 + boff, idesc_s, kk > 0 ? 1u : 0u);
-                    ptx::mma_tf32_ts(d_s, a_hi, bl0 + boff, idesc_s, 1u);
-                    ptx::mma_tf32(d_s, al0 + aoff, bh0 + boff, idesc_s, 1u);
-                }
-                ptx::mma_commit(&k_empty[slot]);
-                ptx::mma_commit(&s_full[slot]);
-                return true;
+                return ring + stage * CHUNK;
             };
-            if (ok && n_tiles > 0) ok = issue_s(0);
+            auto release = [&]() {
+                ptx::mma_commit(&empty[stage]);
+                if (++stage == STAGES) {
+                    stage = 0;
+                    ph ^= 1;
+                }
+            };
+            auto issue_s = [&]() {
+                for (int c = 0; c < C::K_CHUNKS; c++) {
+                    uint8_t* buf = pop();
+                    if (!buf) return;
+                    const uint64_t ah = ptx::smem_desc(qh + c * BQ * 128, 1024, 2);
+                    const uint64_t al = ptx::smem_desc(ql + c * BQ * 128, 1024, 2);
+                    const uint64_t bh0 = ptx::smem_desc(buf, 1024, 2);
+                    const uint64_t bl0 = ptx::smem_desc(buf + CHUNK / 2, 1024, 2);
+#pragma unroll
+                    for (int kk = 0; kk < 4; kk++) {
+                        const uint64_t off = (uint64_t)((kk * 32) >> 4);
+                        ptx::mma_tf32(tmem + COL_S, ah + off, bh0 + off, idesc_s, (c | kk) ? 1u : 0u);
+                        ptx::mma_tf32(tmem + COL_S, ah + off, bl0 + off, idesc_s, 1u);
+                        ptx::mma_tf32(tmem + COL_S, al + off, bh0 + off, idesc_s, 1u);
+                    }
+                    release();
+                }
+                if (ok) ptx::mma_commit(s_full);
+            };
+            auto issue_pv = [&]() {
+                for (int c = 0; c < C::V_CHUNKS; c++) {
+                    uint8_t* buf = pop();
+                    if (!buf) return;
+                    const uint64_t bh0 = ptx::smem_desc(buf, 1024, 2);
+                    const uint64_t bl0 = ptx::smem_desc(buf + CHUNK / 2, 1024, 2);
+#pragma unroll
+                    for (int kk = 0; kk < C::V_KEYS / 8; kk++) {
+                        const uint64_t off = (uint64_t)((((kk >> 2) * D * 128) + (kk & 3) * 32) >> 4);
+                        const uint32_t kc = c * C::V_KEYS + kk * 8;
+                        ptx::mma_tf32_ts(tmem + COL_O, tmem + COL_PH + kc, bh0 + off, idesc_o, (c | kk) ? 1u : 0u);
+                        ptx::mma_tf32_ts(tmem + COL_O, tmem + COL_PH + kc, bl0 + off, idesc_o, 1u);
+                        ptx::mma_tf32_ts(tmem + COL_O, tmem + COL_PL + kc, bh0 + off, idesc_o, 1u);
+                    }
+                    release();
+                }
+                if (ok) ptx::mma_commit(pv_full);
+            };
+            if (ok && n_tiles > 0) issue_s();
             for (int j = 0; j < n_tiles && ok; j++) {
-                // S buffer (j+1)&1 was last read by softmax j-1, which finished before p_full j-1
-                if (j + 1 < n_tiles && !(ok = issue_s(j + 1))) break;
-                const int slot = j & 1;
+                if (j + 1 < n_tiles) {   // S_{j+1} once the softmax has read S_j out of TMEM
+                    if (!(ok = ptx::wait_bounded(s_free, j & 1, abort_flag, p.err, ERR_A_MMA, WAIT_NS))) break;
+                    ptx::tc_fence_after();
+                    issue_s();
+                }
+                if (!ok) break;
                 if (!(ok = ptx::wait_bounded(p_full, j & 1, abort_flag, p.err, ERR_A_MMA, WAIT_NS))) break;
                 ptx::tc_fence_after();
-                if (!(ok = ptx::wait_bounded(&v_full[slot], (j >> 1) & 1, abort_flag, p.err, ERR_A_MMA, WAIT_NS)))
-                    break;
-                ptx::tc_fence_after();
-                const uint8_t* vh = vbuf + slot * C::V_SLOT;
-                const uint32_t p_hi = tmem + C::COL_P + (j & 1) * 2 * BKV, p_lo = p_hi + BKV;
-                const uint64_t vh0 = ptx::smem_desc(vh, 1024, 2);
-                const uint64_t vl0 = ptx::smem_desc(vh + C::VH_BYTES, 1024, 2);
-#pragma unroll
-                for (int kk = 0; kk < BKV / 8; kk++) {
-                    const uint64_t off = (uint64_t)(((kk >> 2) * D * 128 + (kk & 3) * 32) >> 4);
-                    ptx::mma_tf32_ts(tmem + C::COL_O, p_hi + kk * 8, vh0 + off, idesc_o, kk > 0 ? 1u : 0u);
-                    ptx::mma_tf32_ts(tmem + C::COL_O, p_hi + kk * 8, vl0 + off, idesc_o, 1u);
-                    ptx::mma_tf32_ts(tmem + C::COL_O, p_lo + kk * 8, vh0 + off, idesc_o, 1u);
-                }
-                ptx::mma_commit(&v_empty[slot]);
-                ptx::mma_commit(pv_full);
+                issue_pv();
             }
             ptx::mma_commit(drain);
             volatile int no_abort = 0;
@@ -209,9 +290,7 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
         }
         __syncwarp();
     } else {
-        // ---------------------------------------------------- softmax rows (warps 2 .. 1+SOFT_WARPS)
-        // Two threads per query row (warps w and w+4 share TMEM lanes): each
-        // owns half of the row's scores and half of its output columns.
+        // ---------------------------------------------------- softmax rows (warps 2..9)
         const int quarter = warp & 3;
         const int half = (warp - 2) >> 2;
         const int row = quarter * 32 + lane;
@@ -219,42 +298,22 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
         const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
         constexpr int DH = D / 2, KH = BKV / 2;   // per-thread output columns / score columns
         const float* qrow = p.q + ((int64_t)bh * p.S + (q < p.S ? q : 0)) * D;
-        const float sl2 = p.scale * 1.4426950408889634f;   // scores in log2 units: exp(x) = 2^(x*log2 e)
-        // exchange with the row's other thread through an mbarrier (bounded wait, never a hang)
+        const float sl2 = p.scale * 1.4426950408889634f;   // scores in log2 units: exp(x) = 2^(x log2 e)
         auto pair_sync = [&](int which, uint32_t parity) -> bool {
             uint64_t* b = &pair_bar[quarter * 3 + which];
             ptx::mbar_arrive(b);
             return ptx::wait_bounded(b, parity, abort_flag, p.err, ERR_A_SOFT, WAIT_NS);
         };
-        // stage Q: hi -> TMEM [0, D), lo -> shared memory (128-byte swizzle)
-#pragma unroll 1
-        for (int c16 = half * (DH / 16); c16 < (half + 1) * (DH / 16); c16++) {
-            uint32_t hi[16];
-            float lo[16];
-#pragma unroll
-            for (int i = 0; i < 16; i += 4) {
-                float4 v = q < p.S ? *reinterpret_cast<const float4*>(qrow + c16 * 16 + i)
-                                   : make_float4(0.f, 0.f, 0.f, 0.f);
-                float x[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    float h = tf32_round(x[k]);
-                    hi[i + k] = __float_as_uint(h);
-                    lo[i + k] = x[k] - h;
-                }
-            }
-            ptx::tmem_st16(tmem + lane_off + c16 * 16, hi);
-            const int chunk = c16 >> 1;
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int unit = (c16 & 1) * 4 + u;   // 16-byte unit within the 128-byte row
-                uint8_t* dst = ql + chunk * BQ * 128 + row * 128 + ((unit ^ (row & 7)) << 4);
-                *reinterpret_cast<float4*>(dst) = make_float4(lo[4 * u], lo[4 * u + 1], lo[4 * u + 2], lo[4 * u + 3]);
-            }
+        // stage this thread's half of the Q row: hi and lo, 128-byte swizzled
+#pragma unroll 4
+        for (int d = half * DH; d < (half + 1) * DH; d += 4) {
+            float4 v = q < p.S ? *reinterpret_cast<const float4*>(qrow + d) : make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 h = make_float4(tf32_round(v.x), tf32_round(v.y), tf32_round(v.z), tf32_round(v.w));
+            const uint32_t off = (uint32_t)(d >> 5) * BQ * 128 + swz(row, d & 31);
+            *reinterpret_cast<float4*>(qh + off) = h;
+            *reinterpret_cast<float4*>(ql + off) = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
         }
-        ptx::tmem_st_wait();
         ptx::fence_proxy_async_smem();
-        ptx::tc_fence_before();
         ptx::mbar_arrive(q_ready);
 
         float m = -FLT_MAX, l = 0.0f;   // m in log2 units; -FLT_MAX as the reference's initial max
@@ -263,23 +322,23 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
         for (int i = 0; i < DH; i++) o[i] = 0.0f;
         bool ok = true;
         for (int j = 0; j < n_tiles; j++) {
-            const uint32_t s_col = C::COL_S + (j & 1) * BKV + half * KH;
-            if (!(ok = ptx::wait_bounded(&s_full[j & 1], (j >> 1) & 1, abort_flag, p.err, ERR_A_SOFT, WAIT_NS)))
-                break;
+            if (!(ok = ptx::wait_bounded(s_full, j & 1, abort_flag, p.err, ERR_A_SOFT, WAIT_NS))) break;
             ptx::tc_fence_after();
-            const int k0 = j * BKV + half * KH;
-            // every key of this half-tile valid for this row: no mask arithmetic
-            const bool full = k0 + KH <= p.S && (!p.causal || k0 + KH - 1 <= q);
             float sv[KH];
             {
                 uint32_t r[KH];
 #pragma unroll
                 for (int c16 = 0; c16 < KH / 16; c16++)
-                    ptx::tmem_ld16(tmem + lane_off + s_col + c16 * 16, *reinterpret_cast<uint32_t(*)[16]>(&r[c16 * 16]));
+                    ptx::tmem_ld16(tmem + lane_off + COL_S + half * KH + c16 * 16,
+                                   *reinterpret_cast<uint32_t(*)[16]>(&r[c16 * 16]));
                 ptx::tmem_ld_wait();
 #pragma unroll
                 for (int i = 0; i < KH; i++) sv[i] = __uint_as_float(r[i]) * sl2;
             }
+            ptx::tc_fence_before();
+            ptx::mbar_arrive(s_free);   // S may be overwritten by the next tile's MMAs
+            const int k0 = j * BKV + half * KH;
+            const bool full = k0 + KH <= p.S && (!p.causal || k0 + KH - 1 <= q);
             float mt = -INFINITY;
             if (full) {
 #pragma unroll
@@ -296,35 +355,25 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
             if (!(ok = pair_sync(j & 1, (j >> 1) & 1))) break;
             mt = fmaxf(mt, red[((j & 1) * 2 + (half ^ 1)) * BQ + row]);
             const float m_new = mt > m ? mt : m;
-            // P_j (relative to m_new) into P buffer j&1; that buffer's last reader,
-            // PV_{j-2}, finished before this thread's previous p_full arrive
-            const uint32_t p_hi = tmem + lane_off + C::COL_P + (j & 1) * 2 * BKV + half * KH;
             float lt = 0.0f;
 #pragma unroll
-            for (int c16 = 0; c16 < KH / 16; c16++) {
-                uint32_t ph[16], pl[16];
-#pragma unroll
-                for (int i = 0; i < 16; i++) {
-                    float pv = exp2f(sv[c16 * 16 + i] - m_new);   // masked: 2^-inf = 0
-                    lt += pv;
-                    float h = tf32_round(pv);
-                    ph[i] = __float_as_uint(h);
-                    pl[i] = __float_as_uint(pv - h);
-                }
-                ptx::tmem_st16(p_hi + c16 * 16, ph);
-                ptx::tmem_st16(p_hi + BKV + c16 * 16, pl);
+            for (int i = 0; i < KH; i++) {
+                sv[i] = exp2f(sv[i] - m_new);   // masked: 2^-inf = 0
+                lt += sv[i];
             }
-            if (j > 0) {   // O tile j-1 (relative to the old max): fold into registers, freeing the tile
+            if (j > 0) {   // O tile j-1 (relative to the old max): fold, freeing the tile and P
                 if (!(ok = ptx::wait_bounded(pv_full, (j - 1) & 1, abort_flag, p.err, ERR_A_SOFT, WAIT_NS))) break;
                 ptx::tc_fence_after();
-                uint32_t r[DH];
 #pragma unroll
-                for (int c16 = 0; c16 < DH / 16; c16++)
-                    ptx::tmem_ld16(tmem + lane_off + C::COL_O + half * DH + c16 * 16,
-                                   *reinterpret_cast<uint32_t(*)[16]>(&r[c16 * 16]));
-                ptx::tmem_ld_wait();
+                for (int g = 0; g < DH / 32; g++) {   // 32 columns per batch keeps registers in bounds
+                    uint32_t r[32];
+                    ptx::tmem_ld16(tmem + lane_off + COL_O + half * DH + g * 32, *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
+                    ptx::tmem_ld16(tmem + lane_off + COL_O + half * DH + g * 32 + 16,
+                                   *reinterpret_cast<uint32_t(*)[16]>(&r[16]));
+                    ptx::tmem_ld_wait();
 #pragma unroll
-                for (int i = 0; i < DH; i++) o[i] += __uint_as_float(r[i]);
+                    for (int i = 0; i < 32; i++) o[g * 32 + i] += __uint_as_float(r[i]);
+                }
             }
             if (m_new > m) {   // running max grew: rescale (corr would be 1 otherwise)
                 const float corr = exp2f(m - m_new);
@@ -334,6 +383,19 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
                 m = m_new;
             }
             l += lt;
+#pragma unroll
+            for (int c16 = 0; c16 < KH / 16; c16++) {
+                uint32_t ph[16], pl[16];
+#pragma unroll
+                for (int i = 0; i < 16; i++) {
+                    const float pv = sv[c16 * 16 + i];
+                    const float h = tf32_round(pv);
+                    ph[i] = __float_as_uint(h);
+                    pl[i] = __float_as_uint(pv - h);
+                }
+                ptx::tmem_st16(tmem + lane_off + COL_PH + half * KH + c16 * 16, ph);
+                ptx::tmem_st16(tmem + lane_off + COL_PL + half * KH + c16 * 16, pl);
+            }
             ptx::tmem_st_wait();
             ptx::tc_fence_before();
             ptx::mbar_arrive(p_full);
@@ -345,15 +407,17 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
                 uint32_t r[DH];
 #pragma unroll
                 for (int c16 = 0; c16 < DH / 16; c16++)
-                    ptx::tmem_ld16(tmem + lane_off + C::COL_O + half * DH + c16 * 16,
+                    ptx::tmem_ld16(tmem + lane_off + COL_O + half * DH + c16 * 16,
                                    *reinterpret_cast<uint32_t(*)[16]>(&r[c16 * 16]));
                 ptx::tmem_ld_wait();
 #pragma unroll
                 for (int i = 0; i < DH; i++) o[i] += __uint_as_float(r[i]);
             }
-            red[(4 + half) * BQ + row] = l;
+            // the exchange buffer of parity n_tiles&1 was last read for tile n_tiles-2
+            const int fb = n_tiles & 1;
+            red[(fb * 2 + half) * BQ + row] = l;
             const bool paired = pair_sync(2, 0);
-            l += red[(4 + (half ^ 1)) * BQ + row];
+            l += red[(fb * 2 + (half ^ 1)) * BQ + row];
             if (paired && q < p.S) {
                 const float inv = 1.0f / l;
                 float* orow = p.o + ((int64_t)bh * p.S + q) * D + half * DH;
@@ -367,56 +431,16 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
 
     __syncthreads();
     if (threadIdx.x == 0 && *abort_flag) {
+        // copies still in flight land before the CTA's shared memory goes away
         volatile int no_abort = 0;
-        for (int sl = 0; sl < 2; sl++) {
-            if (k_issued[sl] >= 0)
-                ptx::wait_bounded(&k_full[sl], (uint32_t)k_issued[sl], &no_abort, nullptr, 0, 100000000ull);
-            if (v_issued[sl] >= 0)
-                ptx::wait_bounded(&v_full[sl], (uint32_t)v_issued[sl], &no_abort, nullptr, 0, 100000000ull);
-        }
+        for (int s = 0; s < STAGES; s++)
+            if (issued[s] >= 0)
+                ptx::wait_bounded(&full[s], (uint32_t)issued[s], &no_abort, nullptr, 0, 100000000ull);
     }
     __syncthreads();
     if (warp == 1) {
         ptx::tc_fence_after();
         ptx::tmem_dealloc(tmem, 512);
-    }
-}
-
-// Packs K and V into per-tile images that are byte-for-byte the shared-memory
-// layout the MMA reads (K: [D/32 chunks][BKV keys][128 B], V^T: [BKV/32
-// chunks][D][128 B]; 16-byte units swizzled by row % 8 as the 128-byte
-// swizzle mode expects; hi then lo), so each tile is one contiguous bulk copy.
-// Keys past S are zero.
-template <int D>
-__global__ void pack_kv_kernel(const float* __restrict__ k, const float* __restrict__ v,
-                               uint8_t* __restrict__ out, int S, int n_kv) {
-    using C = AttnTcCfg<D>;
-    constexpr int BKV = C::BKV;
-    const int j = blockIdx.x, h = blockIdx.y;
-    const int k0 = j * BKV;
-    uint8_t* tile = out + ((size_t)h * n_kv + j) * (C::K_SLOT + C::V_SLOT);
-    const float* kb = k + (size_t)h * S * D;
-    const float* vb = v + (size_t)h * S * D;
-    for (int e = threadIdx.x; e < BKV * D; e += blockDim.x) {
-        const int r = e / D, d = e % D;   // key within tile, feature
-        const bool ok = k0 + r < S;
-        const float kx = ok ? kb[(size_t)(k0 + r) * D + d] : 0.0f;
-        const float vx = ok ? vb[(size_t)(k0 + r) * D + d] : 0.0f;
-        const float kh = tf32_round(kx), vh = tf32_round(vx);
-        // K image: chunk d/32, row r, unit (d%32)/4
-        {
-            const int c = d >> 5, w = d & 31;
-            const size_t off = (size_t)c * BKV * 128 + r * 128 + ((((w >> 2) ^ (r & 7))) << 4) + (w & 3) * 4;
-            *reinterpret_cast<float*>(tile + off) = kh;
-            *reinterpret_cast<float*>(tile + C::KH_BYTES + off) = kx - kh;
-        }
-        // V^T image: chunk r/32, row d, unit (r%32)/4
-        {
-            const int c = r >> 5, w = r & 31;
-            const size_t off = (size_t)c * D * 128 + d * 128 + ((((w >> 2) ^ (d & 7))) << 4) + (w & 3) * 4;
-            *reinterpret_cast<float*>(tile + C::K_SLOT + off) = vh;
-            *reinterpret_cast<float*>(tile + C::K_SLOT + C::VH_BYTES + off) = vx - vh;
-        }
     }
 }
 
@@ -430,17 +454,15 @@ Status launch_tc(const AttnTcParams& prm, int BH, cudaStream_t st) {
 
 }  // namespace
 
-// Shapes this kernel takes: no custom mask, head_dim 64 or 128, S a multiple
-// of 4 (TMA row stride of V^T), at least one full query block.
+// Shapes this kernel takes: no custom mask, head_dim 64 or 128, at least one
+// full 128-query block.
 bool attention_tc_applicable(int64_t S, int D, bool has_mask, int64_t BH) {
-    return !has_mask && (D == 64 || D == 128) && S % 4 == 0 && S >= 128 && BH <= 65535 && S < (1 << 30);
+    return !has_mask && (D == 64 || D == 128) && S >= 128 && BH <= 65535 && S < (1 << 30);
 }
 
 size_t attention_tc_workspace(int64_t BHkv, int64_t S, int D) {
-    const int bkv = D == 128 ? AttnTcCfg<128>::BKV : AttnTcCfg<64>::BKV;
-    const size_t tile = D == 128 ? AttnTcCfg<128>::K_SLOT + AttnTcCfg<128>::V_SLOT
-                                 : AttnTcCfg<64>::K_SLOT + AttnTcCfg<64>::V_SLOT;
-    return (size_t)BHkv * ((S + bkv - 1) / bkv) * tile;
+    const size_t tile = D == 128 ? AttnTcCfg<128>::TILE_BYTES : AttnTcCfg<64>::TILE_BYTES;
+    return (size_t)BHkv * ((S + BKV - 1) / BKV) * tile;
 }
 
 Status attention_tc_prepare() {
@@ -458,9 +480,9 @@ Status attention_tc_prepare() {
 Status launch_attention_tc(const float* q, const float* k, const float* v, float* o, int64_t BH, int64_t S,
                            int D, int group, int causal, Workspace ws, cudaStream_t st, int* launches) {
     const int64_t BHkv = BH / group;
-    if (ws.bytes < attention_tc_workspace(BHkv, S, D)) return Status::err(RT_ERR_ARGUMENT, "attention: workspace too small");
-    const int bkv = D == 128 ? AttnTcCfg<128>::BKV : AttnTcCfg<64>::BKV;
-    const int n_kv = (int)((S + bkv - 1) / bkv);
+    if (ws.bytes < attention_tc_workspace(BHkv, S, D))
+        return Status::err(RT_ERR_ARGUMENT, "attention: workspace too small");
+    const int n_kv = (int)((S + BKV - 1) / BKV);
     dim3 pgrid((unsigned)n_kv, (unsigned)BHkv);
     if (D == 64)
         pack_kv_kernel<64><<<pgrid, 256, 0, st>>>(k, v, reinterpret_cast<uint8_t*>(ws.base), (int)S, n_kv);
