@@ -46,13 +46,22 @@ int* kernel_error_flag();   // runtime.cu: device view of the host-mapped error 
 
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 16, STAGES = 4;
-constexpr int EPI_WARPS = 8, EPI_COLS = BN / 2;      // 2 warps per TMEM lane quarter
+constexpr int BM = 128, BK = 16;
+constexpr int EPI_WARPS = 8;                          // 2 warps per TMEM lane quarter
 constexpr int THREADS = 64 + 32 * EPI_WARPS;          // producer + MMA + epilogue
 constexpr int A_TILE = BM * BK * 4;                   // 8 KiB
-constexpr int B_TILE = BN * BK * 4;                   // 16 KiB
-constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;  // 48 KiB
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+
+// N tile 256 (4-stage ring of 48 KiB) or 128 (6 stages of 32 KiB); the host
+// picks per problem whichever fills the machine in fewer tile waves.
+template <int BN_>
+struct GCfg {
+    static constexpr int BN = BN_;
+    static constexpr int STAGES = BN_ == 256 ? 4 : 6;
+    static constexpr int EPI_COLS = BN_ / 2;
+    static constexpr int B_TILE = BN_ * BK * 4;
+    static constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;     // 2 s per wait
 constexpr int ERR_PRODUCER = 0x101, ERR_MMA = 0x102, ERR_EPILOGUE = 0x103, ERR_DRAIN = 0x104;
 
@@ -64,17 +73,26 @@ struct TcParams {
     int M, N, K, batches;
     int m_tiles, n_tiles, k_blocks, total_tiles;
     int kb_per_chunk, n_chunks;   // K accumulated in TMEM in chunks of kb_per_chunk blocks
+    int splits, kb_split;         // split-K: work item = (tile, split); split s covers K blocks [s*kb_split, ...)
+    int total_items;              // total_tiles * splits
     int* err;
 };
 
-__device__ __forceinline__ void tile_coords(const TcParams& p, int t, int& m_blk, int& n_blk, int& bz) {
+__device__ __forceinline__ void tile_coords(const TcParams& p, int item, int& m_blk, int& n_blk, int& bz,
+                                            int& kb_lo, int& kb_hi) {
+    const int t = item / p.splits, s = item % p.splits;
     n_blk = t % p.n_tiles;
     int rest = t / p.n_tiles;
     m_blk = rest % p.m_tiles;
     bz = rest / p.m_tiles;
+    kb_lo = s * p.kb_split;
+    kb_hi = min(p.k_blocks, kb_lo + p.kb_split);
 }
 
+template <int BN_>
 __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
+    constexpr int BN = GCfg<BN_>::BN, STAGES = GCfg<BN_>::STAGES, EPI_COLS = GCfg<BN_>::EPI_COLS;
+    constexpr int B_TILE = GCfg<BN_>::B_TILE, STAGE_BYTES = GCfg<BN_>::STAGE_BYTES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem =
         reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -119,10 +137,10 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
-                int m_blk, n_blk, bz;
-                tile_coords(p, t, m_blk, n_blk, bz);
-                for (int kb = 0; kb < p.k_blocks; kb++) {
+            for (int t = blockIdx.x; t < p.total_items && ok; t += gridDim.x) {
+                int m_blk, n_blk, bz, kb_lo, kb_hi;
+                tile_coords(p, t, m_blk, n_blk, bz, kb_lo, kb_hi);
+                for (int kb = kb_lo; kb < kb_hi; kb++) {
                     if (!ptx::wait_bounded(&empty[stage], phase ^ 1, abort_flag, p.err, ERR_PRODUCER,
                                            WAIT_LIMIT_NS)) {
                         ok = false;
@@ -151,8 +169,11 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
             uint32_t phase = 0;
             bool ok = true;
             int it = 0;   // accumulator hand-offs so far (one per K chunk)
-            for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
-                for (int c = 0; c < p.n_chunks && ok; c++, it++) {
+            for (int t = blockIdx.x; t < p.total_items && ok; t += gridDim.x) {
+                int m_blk, n_blk, bz, kb_lo, kb_hi;
+                tile_coords(p, t, m_blk, n_blk, bz, kb_lo, kb_hi);
+                const int n_chunks = (kb_hi - kb_lo + p.kb_per_chunk - 1) / p.kb_per_chunk;
+                for (int c = 0; c < n_chunks && ok; c++, it++) {
                     int b = it & 1;
                     uint32_t acc_phase = (it >> 1) & 1;
                     if (!ptx::wait_bounded(&acc_empty[b], acc_phase ^ 1, abort_flag, p.err, ERR_MMA,
@@ -162,8 +183,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
                     }
                     ptx::tc_fence_after();
                     const uint32_t d_tmem = tmem_base + b * BN;
-                    const int kb0 = c * p.kb_per_chunk;
-                    const int kb_end = min(p.k_blocks, kb0 + p.kb_per_chunk);
+                    const int kb0 = kb_lo + c * p.kb_per_chunk;
+                    const int kb_end = min(kb_hi, kb0 + p.kb_per_chunk);
                     for (int kb = kb0; kb < kb_end; kb++) {
                         if (!ptx::wait_bounded(&full[stage], phase, abort_flag, p.err, ERR_MMA, WAIT_LIMIT_NS)) {
                             ok = false;
@@ -201,17 +222,19 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
         __syncwarp();
     } else {
         // ------------------------------------------------ epilogue (warps 2..9)
-        // Thread = one tile row (TMEM lane) x 128 columns (half of BN).
+        // Thread = one tile row (TMEM lane) x BN/2 columns.
         const int quarter = warp & 3;
         const int half = (warp - 2) >> 2;
         const int row_in_tile = quarter * 32 + lane;
         int it = 0;
         bool ok = true;
-        for (int t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
-            int m_blk, n_blk, bz;
-            tile_coords(p, t, m_blk, n_blk, bz);
+        for (int t = blockIdx.x; t < p.total_items && ok; t += gridDim.x) {
+            int m_blk, n_blk, bz, kb_lo, kb_hi;
+            tile_coords(p, t, m_blk, n_blk, bz, kb_lo, kb_hi);
+            const int n_chunks = (kb_hi - kb_lo + p.kb_per_chunk - 1) / p.kb_per_chunk;
+            const bool first_split = kb_lo == 0;
             float acc[EPI_COLS];
-            for (int c = 0; c < p.n_chunks; c++, it++) {
+            for (int c = 0; c < n_chunks; c++, it++) {
                 int b = it & 1;
                 uint32_t acc_phase = (it >> 1) & 1;
                 if (!ptx::wait_bounded(&acc_full[b], acc_phase, abort_flag, p.err, ERR_EPILOGUE,
@@ -240,24 +263,29 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
             if (row >= p.M) continue;
             float* crow = p.c + ((int64_t)bz * p.M + row) * p.N;
             const int col0 = n_blk * BN + half * EPI_COLS;
+            const bool add_bias = p.bias && first_split;
             if ((p.N & 3) == 0 && col0 + EPI_COLS <= p.N) {
 #pragma unroll
                 for (int j = 0; j < EPI_COLS; j += 4) {
                     float4 v = make_float4(p.alpha * acc[j], p.alpha * acc[j + 1], p.alpha * acc[j + 2],
                                            p.alpha * acc[j + 3]);
-                    if (p.bias) {
+                    if (add_bias) {
                         float4 bb = *reinterpret_cast<const float4*>(p.bias + col0 + j);
                         v.x += bb.x; v.y += bb.y; v.z += bb.z; v.w += bb.w;
                     }
-                    *reinterpret_cast<float4*>(crow + col0 + j) = v;
+                    // two splits add into a zeroed C: 0+x+y == 0+y+x, so the
+                    // result does not depend on which split lands first
+                    if (p.splits > 1) atomicAdd(reinterpret_cast<float4*>(crow + col0 + j), v);
+                    else *reinterpret_cast<float4*>(crow + col0 + j) = v;
                 }
             } else {
 #pragma unroll
                 for (int j = 0; j < EPI_COLS; j++) {
                     if (col0 + j < p.N) {
                         float v = p.alpha * acc[j];
-                        if (p.bias) v += p.bias[col0 + j];
-                        crow[col0 + j] = v;
+                        if (add_bias) v += p.bias[col0 + j];
+                        if (p.splits > 1) atomicAdd(crow + col0 + j, v);
+                        else crow[col0 + j] = v;
                     }
                 }
             }
@@ -388,6 +416,15 @@ int k_chunk() {
     return v;
 }
 
+// RT_GEMM_SPLITK=0 turns the two-way split-K off.
+bool split_k_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("RT_GEMM_SPLITK");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
 bool b_is_constant(const GemmProblem& p) {
     return is_constant_range(p.b, (size_t)p.batches * p.N * p.K * 4);
 }
@@ -416,8 +453,10 @@ Status tc_gemm_prepare(const GemmProblem& p, cudaStream_t st) {
     if (!tc_gemm_applicable(p)) return Status::ok();
     static bool attr_set = false;
     if (!attr_set) {
-        RT_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           SMEM_BYTES));
+        RT_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           GCfg<256>::SMEM_BYTES));
+        RT_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           GCfg<128>::SMEM_BYTES));
         attr_set = true;
     }
     if (!b_is_constant(p)) return Status::ok();
@@ -458,6 +497,14 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
     memset(&prm, 0, sizeof prm);
     if (!(s = make_tmap(&prm.ta_hi, a_hi, p.K, p.M, p.batches, BM)).good()) return s;
     if (!(s = make_tmap(&prm.ta_lo, a_lo, p.K, p.M, p.batches, BM)).good()) return s;
+    // N tile: 256 -- measured faster than 128 at every BASELINE shape, N=768
+    // included (the 128-wide tile doubles A traffic per flop); short grids are
+    // filled by split-K below instead.  RT_GEMM_BN=128 selects the narrow tile.
+    static const int bn_force = [] {
+        const char* e = getenv("RT_GEMM_BN");
+        return e ? atoi(e) : 0;
+    }();
+    const int BN = bn_force == 128 ? 128 : 256;
     if (!(s = make_tmap(&prm.tb_hi, b_hi, p.K, p.N, p.batches, BN)).good()) return s;
     if (!(s = make_tmap(&prm.tb_lo, b_lo, p.K, p.N, p.batches, BN)).good()) return s;
     prm.c = p.c;
@@ -473,11 +520,23 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
     prm.kb_per_chunk = k_chunk() / BK;
     prm.n_chunks = (prm.k_blocks + prm.kb_per_chunk - 1) / prm.kb_per_chunk;
     int64_t total = (int64_t)prm.m_tiles * prm.n_tiles * p.batches;
-    if (total > INT32_MAX) return Status::err(RT_ERR_UNSUPPORTED, "gemm: too many tiles");
+    if (total > INT32_MAX / 2) return Status::err(RT_ERR_UNSUPPORTED, "gemm: too many tiles");
     prm.total_tiles = (int)total;
+    // Split K in two when the tiles alone fill well under 1.5 waves of the
+    // persistent grid (two addends keep the fp32 sum order-independent).
+    prm.splits = 1;
+    if (total < (int64_t)g_num_sms * 3 / 2 && prm.n_chunks >= 2 && split_k_enabled()) {
+        prm.splits = 2;
+        RT_CUDA_CHECK(cudaMemsetAsync(p.c, 0, (size_t)p.batches * p.M * p.N * 4, st));
+    }
+    prm.kb_split = ((prm.n_chunks + prm.splits - 1) / prm.splits) * prm.kb_per_chunk;
+    prm.total_items = prm.total_tiles * prm.splits;
     prm.err = kernel_error_flag();
-    int grid = prm.total_tiles < g_num_sms ? prm.total_tiles : g_num_sms;
-    tc_gemm_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(prm);
+    int grid = prm.total_items < g_num_sms ? prm.total_items : g_num_sms;
+    if (BN == 128)
+        tc_gemm_kernel<128><<<grid, THREADS, GCfg<128>::SMEM_BYTES, st>>>(prm);
+    else
+        tc_gemm_kernel<256><<<grid, THREADS, GCfg<256>::SMEM_BYTES, st>>>(prm);
     RT_LAUNCH_CHECK();
     *launches += 1;
     return Status::ok();
@@ -539,7 +598,8 @@ int noalloc_setup(int device, NoallocDevice** out) {
             cudaGetLastError();
             return RT_ERR_CUDA;
         }
-        if (cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) !=
+        if (cudaFuncSetAttribute(tc_gemm_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 GCfg<256>::SMEM_BYTES) !=
             cudaSuccess) {
             cudaGetLastError();
             return RT_ERR_CUDA;
@@ -587,7 +647,7 @@ extern "C" int rt_matmul_noalloc(const float* a, const float* b, const float* bi
     TcParams prm;
     memset(&prm, 0, sizeof prm);
     if (!make_tmap(&prm.ta_hi, a_hi, K, M, 1, BM).good() || !make_tmap(&prm.ta_lo, a_lo, K, M, 1, BM).good() ||
-        !make_tmap(&prm.tb_hi, b_hi, K, N, 1, BN).good() || !make_tmap(&prm.tb_lo, b_lo, K, N, 1, BN).good())
+        !make_tmap(&prm.tb_hi, b_hi, K, N, 1, 256).good() || !make_tmap(&prm.tb_lo, b_lo, K, N, 1, 256).good())
         return RT_ERR_CUDA;
     prm.c = c;
     prm.bias = bias;
@@ -597,16 +657,19 @@ extern "C" int rt_matmul_noalloc(const float* a, const float* b, const float* bi
     prm.K = K;
     prm.batches = 1;
     prm.m_tiles = (M + BM - 1) / BM;
-    prm.n_tiles = (N + BN - 1) / BN;
+    prm.n_tiles = (N + 255) / 256;
     prm.k_blocks = (K + BK - 1) / BK;
     prm.kb_per_chunk = k_chunk() / BK;
     prm.n_chunks = (prm.k_blocks + prm.kb_per_chunk - 1) / prm.kb_per_chunk;
     int64_t total = (int64_t)prm.m_tiles * prm.n_tiles;
     prm.total_tiles = (int)total;
+    prm.splits = 1;
+    prm.kb_split = prm.k_blocks;
+    prm.total_items = prm.total_tiles;
     prm.err = d->error;
     if (cudaMemsetAsync(d->error, 0, sizeof(int), st) != cudaSuccess) return RT_ERR_CUDA;
     int grid = prm.total_tiles < d->sms ? prm.total_tiles : d->sms;
-    tc_gemm_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(prm);
+    tc_gemm_kernel<256><<<grid, THREADS, GCfg<256>::SMEM_BYTES, st>>>(prm);
     if (cudaGetLastError() != cudaSuccess) return RT_ERR_CUDA;
     // synchronous: returns once C is written, and reports a kernel that gave up a wait
     if (cudaStreamSynchronize(st) != cudaSuccess) return RT_ERR_CUDA;
