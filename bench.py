@@ -75,60 +75,79 @@ def node_flops(n):
 
 
 class ClockSampler:
-    """nvidia-smi clock/throttle samples during the timed region."""
+    """SM clock and throttle reasons sampled during the timed region.
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NVML (nvidia_ml_py) polled every 10 ms from a thread; the nvidia-smi CLI
+    (`-lms 100`) is the fallback when NVML is unavailable."""
+
+    REASONS = {  # NVML clock-event reason bits
+        "sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
+    }
 
     def __init__(self, gpu_index):
         self.gpu = gpu_index
-        self.proc = None
-        self.lines = []
+        self.samples = []       # (sm_mhz, reasons_mask)
+        self.sm_max = None
+        self._stop = threading.Event()
+        self._thread = None
+
+    def _poll_nvml(self):
+        import pynvml
+        pynvml.nvmlInit()
+        h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+        self.sm_max = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+        get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self._stop.is_set():
+            self.samples.append((pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM), get_reasons(h)))
+            time.sleep(0.01)
+
+    def _poll_smi(self):
+        proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}",
+                                 "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.active",
+                                 "--format=csv,noheader,nounits", "-lms", "100"],
+                                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        while not self._stop.is_set():
+            line = proc.stdout.readline()
+            if not line:
+                break
+            f = [x.strip() for x in line.split(",")]
+            try:
+                self.sm_max = float(f[1])
+                self.samples.append((float(f[0]), int(f[2], 16)))
+            except (ValueError, IndexError):
+                pass
+        proc.terminate()
 
     def __enter__(self):
-        try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
-        except Exception:
-            self.proc = None
+        def run():
+            try:
+                self._poll_nvml()
+            except Exception:
+                try:
+                    self._poll_smi()
+                except Exception:
+                    pass
+        self._thread = threading.Thread(target=run, daemon=True)
+        self._thread.start()
+        time.sleep(0.05)
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *a):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        self._stop.set()
+        if self._thread:
+            self._thread.join(timeout=5)
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for l in self.lines:
-            f = [x.strip() for x in l.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for nm, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(nm)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.sm_max, "reasons": [], "samples": 0}
+        mask = 0
+        for _, m in self.samples:
+            mask |= m
+        reasons = sorted(k for k, bit in self.REASONS.items() if mask & bit)
+        return {"sm_mhz": statistics.median(s for s, _ in self.samples), "sm_max_mhz": self.sm_max,
+                "reasons": reasons, "samples": len(self.samples)}
 
 
 def cpu_reference_run(prog, consts, inputs, budget_s, threads):
@@ -154,8 +173,8 @@ def cpu_reference_run(prog, consts, inputs, budget_s, threads):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--config", default="gpt2", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-budget", type=float, default=15.0,
@@ -268,10 +287,14 @@ def main():
             "gpu_launches": launches * args.steps,
             "roofline": {"bound": "tensor", "kernel": "MATMUL/MATMUL_ADD nodes (sum)",
                          "achieved": round(achieved, 3), "peak": bf16, "unit": "TFLOP/s",
-                         "frac": round(achieved / bf16, 4), "traffic": None,
+                         "frac": round(achieved / bf16, 4),
+                         "traffic": GEMM_TRAFFIC.get(args.config),
+                         "traffic_source": "profiles/tc_gemm_kernel_gpt2_b8.md (ncu dram__bytes_read+write, mean per launch)"
+                         if args.config in GEMM_TRAFFIC else None,
                          "peak_basis": f"{basis} bf16 dense burst",
                          "peak_3xtf32_effective": round(tf32 / 3, 1),
                          "frac_3xtf32": round(achieved / (tf32 / 3), 4)},
+            "roofline_attention": attention_roofline(prog, per_node_ms, bf16),
             "clocks": clocks.summary(),
             "per_op_ms": summarize_ops(prog, per_node_ms),
         }
@@ -286,6 +309,23 @@ def main():
     ex.close()
     if world > 1:
         dist.destroy_process_group()
+
+
+# DRAM bytes per tc_gemm_kernel launch from the committed ncu capture of this
+# workload (mean of the captured launches), used as the roofline "traffic".
+GEMM_TRAFFIC = {"gpt2": round((70.07 + 56.24 + 240.86 + 14.03) / 2 * 1e6)}
+
+
+def attention_roofline(prog, per_node_ms, bf16):
+    ids = [i for i, n in enumerate(prog.nodes) if n.op == OP["ATTENTION"]]
+    if not ids:
+        return None
+    fl = sum(node_flops(prog.nodes[i]) for i in ids)
+    ms = sum(per_node_ms[i] for i in ids)
+    ach = fl / (ms / 1e3) / 1e12 if ms else 0.0
+    return {"bound": "tensor", "kernel": "ATTENTION nodes (pack + attn_tc_kernel)", "achieved": round(ach, 3),
+            "peak": bf16, "unit": "TFLOP/s", "frac": round(ach / bf16, 4),
+            "frac_3xtf32": round(ach / (bf16 / 6), 4)}
 
 
 def summarize_ops(prog, per_node_ms):

@@ -141,6 +141,7 @@ def _configs():
     # small programs with golden outputs (flash path: S > 256, ragged tiles)
     c["gpt2_mini_s300"] = (lambda: GPT2Body(2, 2, 128), 2, 300, 128, True)
     c["gpt2_mini_s64"] = (lambda: GPT2Body(2, 2, 128), 2, 64, 128, True)
+    c["gpt2_mini_s64_b1"] = (lambda: GPT2Body(2, 2, 128), 1, 64, 128, False)   # one shard of the batch above
     c["qwen3_mini_s272"] = (lambda: Qwen3Body(256, 512, 2, 4, 2, 128), 1, 272, 256, True)
     c["block_mini_causal_s300"] = (lambda: CustomBlock(128, 2, 512, True), 2, 300, 128, True)
     c["block_mini_s260"] = (lambda: CustomBlock(128, 2, 512, False), 1, 260, 128, True)
