@@ -138,6 +138,19 @@ int rt_reset_plans(void);
 int rt_synchronize(void);
 /* The library stream (a cudaStream_t), for callers that order work on it. */
 void* rt_stream(void);
+/* Declare [ptr, ptr+bytes) a graph output: plan-time layout fusion never
+ * folds away a node that writes into it.  The output of the last node of an
+ * array is always treated as a graph output; callers whose graphs return
+ * more than that register the other outputs here before the first execute
+ * (no counterpart in the reference, whose C side computes every node). */
+int rt_protect(const void* ptr, size_t bytes);
+int rt_unprotect_all(void);
+/* Plan-time layout fusion, as execute would apply it to this node array:
+ * flags[i] = 1 when node i (a SLICE / TRANSPOSE around attention) is folded
+ * into its consumer and not launched, 2 for an attention node launched with
+ * strided operands, 0 otherwise.  Returns the number of folded nodes.  Host
+ * only: needs no device and no rt_init.  RT_FUSE=0 turns folding off. */
+int rt_fusion_report(const OpNode* nodes, int n_nodes, int* flags);
 
 /* ---- allocation-free GEMM ------------------------------------------------ */
 /* No counterpart in the reference.  C[M,N] = alpha * A[M,K] . op(B) + bias

@@ -1,0 +1,413 @@
+// fusion.cu -- plan-time layout fusion over the OpNode array.
+//
+// The reference pipeline emits pure data-movement nodes around attention:
+// a merged QKV projection is split by SLICE (last dim), each head split by a
+// TRANSPOSE [B,S,H,D] -> [B,H,S,D] (runtime/ops.py:149-171, 310-329), and the
+// attention output is merged back by another TRANSPOSE.  The tensor-core
+// attention kernel can read Q/K/V and write O through strided views, so
+// those copies can be skipped -- but only when the node array proves it safe,
+// since the library sees pointers, not tensor names:
+//   * the skipped node's output is read by nobody but its one consumer and
+//     is not a graph output: callers register graph outputs with rt_protect
+//     (the Python executor does), and the last node's output is always kept;
+//   * the source the fused consumer reads instead is not written by any node
+//     between the skipped producer and the consumer;
+//   * for the output side, nothing between attention and the merge TRANSPOSE
+//     touches the merge's output region.
+// Every node's read and write extents are computed from its op, shape and
+// extras; a node whose read extent is not known blocks any fusion across it.
+// RT_FUSE=0 disables the pass.
+#include <stdio.h>
+#include <stdlib.h>
+
+#include <vector>
+
+#include "gemm.h"
+#include "rt_internal.h"
+
+namespace rt {
+
+
+namespace {
+
+struct Range {
+    uintptr_t lo = 0, hi = 0;
+};
+inline bool overlaps(Range a, Range b) { return a.lo < b.hi && b.lo < a.hi; }
+inline Range rng(const void* p, size_t bytes) {
+    Range r;
+    r.lo = reinterpret_cast<uintptr_t>(p);
+    r.hi = r.lo + bytes;
+    return r;
+}
+constexpr Range ALL{0, ~(uintptr_t)0};
+
+int64_t bcast_extent(const int* strides, const int* shape, int nd) {
+    int64_t e = 0;
+    for (int d = 0; d < nd; d++) e += (int64_t)(shape[d] - 1) * strides[d];
+    return e + 1;
+}
+
+Range write_range(const OpNode& n) { return rng(n.output, (size_t)total_elements(n) * n.elem_size); }
+
+// What a node reads; ALL when the extent is not derivable.
+void read_ranges(const OpNode& n, std::vector<Range>& out) {
+    out.clear();
+    const size_t numel = (size_t)total_elements(n), es = n.elem_size;
+    const size_t C = (size_t)last_dim(n);
+    auto in = [&](int i, size_t bytes) { out.push_back(rng(n.inputs[i], bytes)); };
+    switch (n.op) {
+        case RT_OP_RELU: case RT_OP_EXP: case RT_OP_TANH: case RT_OP_POW: case RT_OP_GELU:
+        case RT_OP_RSQRT: case RT_OP_SILU: case RT_OP_NEG: case RT_OP_COS: case RT_OP_SIN:
+        case RT_OP_SOFTMAX: case RT_OP_RESHAPE: case RT_OP_TRANSPOSE:
+            in(0, numel * es);
+            return;
+        case RT_OP_ADD: case RT_OP_SUB: case RT_OP_MUL: case RT_OP_DIV: {
+            const int mode = n.extra[0];
+            const bool add = n.op == RT_OP_ADD;
+            const int scalar = add ? 2 : 1, same = add ? 1 : 0, bc = add ? 3 : 2;
+            if (mode == scalar) { in(0, numel * 4); return; }
+            if (mode == same) { in(0, numel * 4); in(1, numel * 4); return; }
+            if (add && mode == 0) { in(0, numel * 4); in(1, C * 4); return; }
+            if (mode == bc) {
+                const int nd = n.extra[1];
+                if (nd < 1 || nd > 7) { out.push_back(ALL); return; }
+                const int* as = &n.extra[2];
+                const int* bs = &n.extra[2 + nd];
+                const int* sh = &n.extra[2 + 2 * nd];
+                in(0, (size_t)bcast_extent(as, sh, nd) * 4);
+                in(1, (size_t)bcast_extent(bs, sh, nd) * 4);
+                return;
+            }
+            out.push_back(ALL);
+            return;
+        }
+        case RT_OP_FUSED_BIAS_RELU:
+            in(0, numel * 4); in(1, C * 4);
+            return;
+        case RT_OP_GATED_ACT:
+            in(0, numel * 4);
+            if (n.extra[0]) { in(1, C * 4); in(2, numel * 4); } else in(1, numel * 4);
+            return;
+        case RT_OP_LAYERNORM:
+            in(0, numel * 4); in(1, C * 4); in(2, C * 4);
+            return;
+        case RT_OP_RMSNORM:
+            in(0, numel * 4); in(1, C * 4);
+            return;
+        case RT_OP_MATMUL: case RT_OP_MATMUL_ADD: {
+            GemmProblem g;
+            if (!decode_gemm(n, &g).good()) { out.push_back(ALL); return; }
+            in(0, (size_t)(g.batches * g.M * g.K) * 4);
+            in(1, (size_t)(n.extra[2] ? g.N * g.K : g.batches * g.N * g.K) * 4);
+            if (g.bias) in(2, (size_t)g.N * 4);
+            return;
+        }
+        case RT_OP_ATTENTION: {
+            const int group = n.extra[4] > 0 ? n.extra[4] : 1;
+            const size_t S = (size_t)n.extra[0];
+            in(0, numel * 4);
+            in(1, numel / group * 4);
+            in(2, numel / group * 4);
+            if (n.extra[3]) in(3, numel / (size_t)n.extra[1] * S * 4);   // mask [BH, S, S]
+            return;   // the planned scratch input is not used by this library's kernels
+        }
+        case RT_OP_SLICE:
+            in(0, (size_t)n.extra[0] * n.extra[1] * n.extra[4] * es);
+            return;
+        case RT_OP_CAT: {
+            const int dim = n.extra[0];
+            size_t outer = 1, inner = 1;
+            for (int i = 0; i < dim; i++) outer *= n.out_shape[i];
+            for (int i = dim + 1; i < n.n_dims; i++) inner *= n.out_shape[i];
+            for (int k = 0; k < n.n_inputs; k++) in(k, outer * (size_t)n.extra[1 + k] * inner * es);
+            return;
+        }
+        case RT_OP_MAX: case RT_OP_SUM: {
+            const int axis = n.extra[0];
+            size_t outer = 1, inner = 1;
+            for (int i = 0; i < axis && i < n.n_dims; i++) outer *= n.out_shape[i];
+            for (int i = axis; i < n.n_dims; i++) inner *= n.out_shape[i];
+            in(0, outer * (size_t)n.extra[1] * inner * 4);
+            return;
+        }
+        default:
+            out.push_back(ALL);   // e.g. EMBEDDING: table extent unknown
+            return;
+    }
+}
+
+struct Analysis {
+    const std::vector<OpNode>& nodes;
+    std::vector<std::vector<Range>> reads;
+    std::vector<Range> writes;
+
+    explicit Analysis(const std::vector<OpNode>& ns) : nodes(ns), reads(ns.size()), writes(ns.size()) {
+        for (size_t i = 0; i < ns.size(); i++) {
+            read_ranges(ns[i], reads[i]);
+            writes[i] = write_range(ns[i]);
+        }
+    }
+    int last_writer(Range r, int before) const {
+        for (int j = before - 1; j >= 0; j--)
+            if (overlaps(writes[j], r)) return j;
+        return -1;
+    }
+};
+
+bool aligned_view(const void* base, int64_t a, int64_t b, int64_t c) {
+    return aligned16(base) && a % 4 == 0 && b % 4 == 0 && c % 4 == 0;
+}
+
+// One candidate fusion around attention node `a`.
+struct Proposal {
+    int a = -1;
+    AttnViews views{};
+    std::vector<std::pair<int, int>> skips;       // (folded node, its consumer in the original schedule)
+    std::vector<std::pair<Range, int>> sources;   // range read through a view, chain start index
+    Range out{};                                  // what the fused attention writes
+    int out_skip = -1;                            // merge TRANSPOSE folded into the attention
+};
+
+// Pattern: operand written by a head-split TRANSPOSE [B,S,Hx,D] -> [B,Hx,S,D],
+// whose input is (optionally) a last-dim SLICE of a [B,S,W] projection.
+bool match_operand(const Analysis& an, int a, int which, int64_t B, int64_t Hx, int64_t S, int64_t D,
+                   Proposal& pr) {
+    const OpNode& att = an.nodes[a];
+    const void* x = att.inputs[which];
+    const Range R = rng(x, (size_t)(B * Hx * S * D) * 4);
+    const int t = an.last_writer(R, a);
+    if (t < 0) return false;
+    const OpNode& tr = an.nodes[t];
+    if (tr.op != RT_OP_TRANSPOSE || tr.n_dims != 4 || tr.elem_size != 4 || tr.output != x ||
+        an.writes[t].hi != R.hi || tr.extra[0] != B || tr.extra[1] != S || tr.extra[2] != 1 ||
+        tr.extra[3] != Hx || tr.extra[4] != D)
+        return false;
+    const Range Tin = rng(tr.inputs[0], (size_t)(R.hi - R.lo));
+    const float* base = static_cast<const float*>(tr.inputs[0]);
+    int64_t sb = S * Hx * D, sh = D, ss = Hx * D;
+    Range src = Tin;
+    int start = t;
+    int slice_skip = -1;
+    const int sidx = an.last_writer(Tin, t);
+    if (sidx >= 0) {
+        const OpNode& sl = an.nodes[sidx];
+        const int64_t W = sl.extra[1];
+        const float* sbase = static_cast<const float*>(sl.inputs[0]) + sl.extra[2];
+        if (sl.op == RT_OP_SLICE && sl.elem_size == 4 && sl.output == tr.inputs[0] && an.writes[sidx].hi == Tin.hi &&
+            sl.extra[0] == B * S && sl.extra[3] == Hx * D && sl.extra[4] == 1 && aligned_view(sbase, S * W, W, D)) {
+            base = sbase;
+            sb = S * W;
+            ss = W;
+            src = rng(sl.inputs[0], (size_t)(B * S * W) * 4);
+            start = sidx;
+            slice_skip = sidx;
+        }
+    }
+    if (!aligned_view(base, sb, ss, sh)) return false;
+    pr.skips.push_back({t, a});
+    if (slice_skip >= 0) pr.skips.push_back({slice_skip, t});
+    AttnViews& v = pr.views;
+    if (which == 0) { v.q = base; v.q_sb = sb; v.q_sh = sh; v.q_ss = ss; }
+    if (which == 1) { v.k = base; v.k_sb = sb; v.k_sh = sh; v.k_ss = ss; }
+    if (which == 2) { v.v = base; v.v_sb = sb; v.v_sh = sh; v.v_ss = ss; }
+    pr.sources.push_back({src, start});
+    return true;
+}
+
+// Pattern: attention output consumed by a head-merge TRANSPOSE [B,H,S,D] -> [B,S,H,D].
+void match_output(const Analysis& an, int a, int64_t B, int64_t H, int64_t S, int64_t D, Proposal& pr) {
+    const OpNode& att = an.nodes[a];
+    for (size_t j = a + 1; j < an.nodes.size(); j++) {
+        const OpNode& tr = an.nodes[j];
+        if (tr.op == RT_OP_TRANSPOSE && tr.inputs[0] == att.output) {
+            if (tr.n_dims == 4 && tr.elem_size == 4 && tr.extra[0] == B && tr.extra[1] == H && tr.extra[2] == 1 &&
+                tr.extra[3] == S && tr.extra[4] == D && aligned_view(tr.output, S * H * D, H * D, D)) {
+                pr.out_skip = (int)j;
+                pr.out = an.writes[j];
+                pr.views.o = static_cast<float*>(tr.output);
+                pr.views.o_sb = S * H * D;
+                pr.views.o_sh = D;
+                pr.views.o_ss = H * D;
+            }
+            return;
+        }
+        if (overlaps(an.writes[j], an.writes[a])) return;
+    }
+}
+
+// The node array as it would execute with the proposals applied: skipped
+// nodes neither read nor write; a fused attention reads its view sources.
+struct Effective {
+    std::vector<std::vector<Range>> reads;
+    std::vector<Range> writes;
+    std::vector<bool> skipped;
+};
+
+Effective effective(const Analysis& an, const std::vector<Proposal>& props) {
+    Effective e;
+    const size_t n = an.nodes.size();
+    e.reads = an.reads;
+    e.writes = an.writes;
+    e.skipped.assign(n, false);
+    for (const Proposal& p : props) {
+        for (auto& k : p.skips) e.skipped[k.first] = true;
+        if (p.out_skip >= 0) e.skipped[p.out_skip] = true;
+    }
+    for (const Proposal& p : props) {
+        std::vector<Range> r;
+        const std::vector<Range>& orig = an.reads[p.a];
+        // operands not fused keep their contiguous ranges (orig[0..2] = q, k, v)
+        const void* ptrs[3] = {p.views.q, p.views.k, p.views.v};
+        const void* origp[3] = {an.nodes[p.a].inputs[0], an.nodes[p.a].inputs[1], an.nodes[p.a].inputs[2]};
+        for (int i = 0; i < 3 && i < (int)orig.size(); i++)
+            if (ptrs[i] == origp[i]) r.push_back(orig[i]);
+        for (size_t i = 3; i < orig.size(); i++) r.push_back(orig[i]);
+        for (auto& sr : p.sources) r.push_back(sr.first);
+        e.reads[p.a] = r;
+        e.writes[p.a] = p.out;
+    }
+    for (size_t j = 0; j < n; j++)
+        if (e.skipped[j]) {
+            e.reads[j].clear();
+            e.writes[j] = Range{};
+        }
+    return e;
+}
+
+bool eff_reads(const Effective& e, int j, Range r) {
+    for (const Range& x : e.reads[j])
+        if (overlaps(x, r)) return true;
+    return false;
+}
+
+// A folded node's output is dead: in the original schedule nobody but its
+// fused consumer reads it before the memory is rewritten, and if it is never
+// rewritten it is not a graph output (rt_protect ranges, the last node's output).
+bool dead_output(const Analysis& an, int k, int consumer, const std::vector<Range>& protect) {
+    const Range r = an.writes[k];
+    for (size_t j = k + 1; j < an.nodes.size(); j++) {
+        bool rd = false;
+        for (const Range& x : an.reads[j]) rd |= overlaps(x, r);
+        if (rd && (int)j != consumer) {
+            if (getenv("RT_FUSE_DEBUG")) fprintf(stderr, "[fusion]   node %d output read by node %zu\n", k, j);
+            return false;
+        }
+        if (overlaps(an.writes[j], r)) return true;   // recycled: the planner only reuses dead memory
+    }
+    // never rewritten: k would leave the final contents here, which matter
+    // if they are a graph output (registered, or the last node's output)
+    for (const Range& pr : protect)
+        if (overlaps(pr, r)) {
+            if (getenv("RT_FUSE_DEBUG")) fprintf(stderr, "[fusion]   node %d output is a graph output\n", k);
+            return false;
+        }
+    return true;
+}
+
+static bool dbg() {
+    static const bool on = getenv("RT_FUSE_DEBUG") != nullptr;
+    return on;
+}
+#define FAIL(msg)                                                               \
+    do {                                                                        \
+        if (dbg()) fprintf(stderr, "[fusion] attention %d: %s\n", p.a, msg);   \
+        return false;                                                           \
+    } while (0)
+
+bool valid(const Analysis& an, const Effective& e, const Proposal& p, const std::vector<Range>& protect) {
+    // view sources intact from the start of their chain to the attention
+    for (auto& sr : p.sources) {
+        for (int j = sr.second + 1; j < p.a; j++)
+            if (overlaps(e.writes[j], sr.first)) FAIL("source overwritten before the attention");
+        if (overlaps(p.out, sr.first)) FAIL("output overlaps a source");
+    }
+    for (auto& k : p.skips)
+        if (!dead_output(an, k.first, k.second, protect)) FAIL("a folded node's output is still needed");
+    if (p.out_skip >= 0) {
+        // nothing between the attention and the folded merge touches either buffer
+        for (int j = p.a + 1; j < p.out_skip; j++)
+            if (overlaps(e.writes[j], p.out) || eff_reads(e, j, p.out) || eff_reads(e, j, an.writes[p.a]))
+                FAIL("merge buffer touched between attention and merge");
+        for (int i = 0; i < 3; i++) {   // nor does the output overlap an unfused operand
+            const Range in = an.reads[p.a][i];
+            if (overlaps(in, p.out)) FAIL("merge output overlaps an operand");
+        }
+        if (!dead_output(an, p.a, p.out_skip, protect)) FAIL("attention output still needed");
+    }
+    return true;
+}
+
+bool fusion_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("RT_FUSE");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+}  // namespace
+
+std::vector<PlanItem> plan_fusions(const std::vector<OpNode>& nodes,
+                                   const std::vector<std::pair<uintptr_t, size_t>>& protected_ranges) {
+    std::vector<PlanItem> items(nodes.size());
+    Analysis an(nodes);
+    std::vector<Range> protect;
+    for (auto& pr : protected_ranges) protect.push_back(Range{pr.first, pr.first + pr.second});
+    // last entry: the final node's output (a graph output unless recycled)
+    protect.push_back(nodes.empty() ? Range{} : an.writes.back());
+    // candidates per attention node, most ambitious first
+    std::vector<std::vector<Proposal>> cands;
+    for (size_t a = 0; a < nodes.size(); a++) {
+        const OpNode& n = nodes[a];
+        if (n.op != RT_OP_ATTENTION || !attention_takes_views(n)) continue;
+        AttnViews dv;
+        if (!attention_default_views(n, &dv)) continue;
+        items[a].views = true;
+        items[a].attn = dv;
+        if (!fusion_enabled() || n.n_dims != 4) continue;
+        const int64_t B = n.out_shape[0], H = n.out_shape[1], S = n.out_shape[2], D = n.out_shape[3];
+        const int group = n.extra[4] > 0 ? n.extra[4] : 1;
+        Proposal pr;
+        pr.a = (int)a;
+        pr.views = dv;
+        pr.out = an.writes[a];
+        match_operand(an, (int)a, 0, B, H, S, D, pr);
+        match_operand(an, (int)a, 1, B, H / group, S, D, pr);
+        match_operand(an, (int)a, 2, B, H / group, S, D, pr);
+        std::vector<Proposal> c;
+        Proposal with_out = pr;
+        match_output(an, (int)a, B, H, S, D, with_out);
+        if (with_out.out_skip >= 0) c.push_back(with_out);
+        if (!pr.skips.empty()) c.push_back(pr);
+        if (!c.empty()) cands.push_back(c);
+    }
+    // choose the first candidate of every node; when one is invalid under the
+    // combined effect of all current choices, fall back to its next candidate
+    std::vector<size_t> pick(cands.size(), 0);
+    for (int iter = 0; iter < 256; iter++) {
+        std::vector<Proposal> cur;
+        std::vector<size_t> owner;
+        for (size_t i = 0; i < cands.size(); i++)
+            if (pick[i] < cands[i].size()) {
+                cur.push_back(cands[i][pick[i]]);
+                owner.push_back(i);
+            }
+        Effective e = effective(an, cur);
+        int bad = -1;
+        for (size_t i = 0; i < cur.size() && bad < 0; i++)
+            if (!valid(an, e, cur[i], protect)) bad = (int)i;
+        if (bad < 0) {
+            for (const Proposal& p : cur) {
+                items[p.a].attn = p.views;
+                for (auto& k : p.skips) items[k.first].skip = true;
+                if (p.out_skip >= 0) items[p.out_skip].skip = true;
+            }
+            break;
+        }
+        pick[owner[bad]]++;
+    }
+    return items;
+}
+
+}  // namespace rt

@@ -198,8 +198,8 @@ Status launch_simt(const AttnParams& p, int64_t BH, cudaStream_t st) {
 bool attention_tc_applicable(int64_t S, int D, bool has_mask, int64_t BH);
 size_t attention_tc_workspace(int64_t BHkv, int64_t S, int D);
 Status attention_tc_prepare();
-Status launch_attention_tc(const float* q, const float* k, const float* v, float* o, int64_t BH, int64_t S,
-                           int D, int group, int causal, Workspace ws, cudaStream_t st, int* launches);
+Status launch_attention_tc(const AttnViews& vw, int64_t BH, int64_t S, int D, int group, int causal,
+                           Workspace ws, cudaStream_t st, int* launches);
 
 namespace {
 
@@ -260,13 +260,54 @@ Status launch_attention(const OpNode& n, cudaStream_t st, Workspace ws, int* lau
     Status s = decode_attention(n, &p, &BH, &has_mask);
     if (!s.good()) return s;
     if (use_tc(p, BH, has_mask) && ws.bytes >= attention_tc_workspace(BH / p.group, p.S, p.D))
-        return launch_attention_tc(p.q, p.k, p.v, p.o, BH, p.S, p.D, p.group, p.causal, ws, st, launches);
+    {
+        AttnViews vw;
+        attention_default_views(n, &vw);
+        return launch_attention_tc(vw, BH, p.S, p.D, p.group, p.causal, ws, st, launches);
+    }
     *launches += 1;
     if (p.D <= 16) return launch_simt<16>(p, BH, st);
     if (p.D <= 32) return launch_simt<32>(p, BH, st);
     if (p.D <= 64) return launch_simt<64>(p, BH, st);
     if (p.D <= 128) return launch_simt<128>(p, BH, st);
     return Status::err(RT_ERR_UNSUPPORTED, "attention: head_dim > 128");
+}
+
+bool attention_default_views(const OpNode& n, AttnViews* v) {
+    AttnParams p;
+    int64_t BH;
+    bool m;
+    if (!decode_attention(n, &p, &BH, &m).good()) return false;
+    const int64_t H = n.n_dims >= 4 ? n.out_shape[n.n_dims - 3] : BH;
+    const int64_t S = p.S, D = p.D, Hkv = H / p.group;
+    v->q = p.q;
+    v->k = p.k;
+    v->v = p.v;
+    v->o = p.o;
+    v->q_sb = H * S * D; v->q_sh = S * D; v->q_ss = D;
+    v->o_sb = H * S * D; v->o_sh = S * D; v->o_ss = D;
+    v->k_sb = Hkv * S * D; v->k_sh = S * D; v->k_ss = D;
+    v->v_sb = Hkv * S * D; v->v_sh = S * D; v->v_ss = D;
+    v->H = (int)H;
+    return H % p.group == 0;
+}
+
+bool attention_takes_views(const OpNode& n) {
+    AttnParams p;
+    int64_t BH;
+    bool m;
+    if (!decode_attention(n, &p, &BH, &m).good()) return false;
+    return n.n_dims >= 4 && use_tc(p, BH, m);
+}
+
+Status launch_attention_views(const OpNode& n, const AttnViews& vw, cudaStream_t st, Workspace ws, int* launches) {
+    AttnParams p;
+    int64_t BH;
+    bool m;
+    Status s = decode_attention(n, &p, &BH, &m);
+    if (!s.good()) return s;
+    if (!use_tc(p, BH, m)) return Status::err(RT_ERR_ARGUMENT, "attention: strided views need the tensor-core path");
+    return launch_attention_tc(vw, BH, p.S, p.D, p.group, p.causal, ws, st, launches);
 }
 
 }  // namespace rt

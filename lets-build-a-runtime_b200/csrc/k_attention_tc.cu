@@ -65,6 +65,9 @@ struct AttnTcParams {
     int n_kv;            // key tiles per head
     const float* q;
     float* o;
+    int64_t q_sb, q_sh, q_ss;   // element strides of Q: batch, head, sequence (features contiguous)
+    int64_t o_sb, o_sh, o_ss;   // same for O
+    int H;                      // query heads per batch element
     int S, group, causal, n_qblocks;
     float scale;
     int* err;
@@ -87,20 +90,27 @@ __device__ __forceinline__ uint32_t swz(int row, int w) {
 // each chunk, byte-for-byte the shared-memory image the MMAs read.  Keys
 // past S are zero.  Every store is a whole 16-byte unit; V is transposed
 // through shared memory 32 keys at a time so its global reads stay coalesced.
+struct KvViews {
+    const float* k;
+    const float* v;
+    int64_t k_sb, k_sh, k_ss, v_sb, v_sh, v_ss;   // element strides: batch, head, sequence
+    int Hkv;                                      // kv heads per batch element
+};
+
 template <int D>
-__global__ void __launch_bounds__(256) pack_kv_kernel(const float* __restrict__ k, const float* __restrict__ v,
-                                                      uint8_t* __restrict__ out, int S, int n_kv) {
+__global__ void __launch_bounds__(256) pack_kv_kernel(KvViews kv, uint8_t* __restrict__ out, int S, int n_kv) {
     using C = AttnTcCfg<D>;
     __shared__ float sv[32][D + 1];
     const int j = blockIdx.x, h = blockIdx.y;
     const int k0 = j * BKV;
     uint8_t* tile = out + ((size_t)h * n_kv + j) * C::TILE_BYTES;
-    const float* kb = k + (size_t)h * S * D;
-    const float* vb = v + (size_t)h * S * D;
+    const int bb = h / kv.Hkv, hh = h % kv.Hkv;
+    const float* kb = kv.k + bb * kv.k_sb + hh * kv.k_sh;
+    const float* vb = kv.v + bb * kv.v_sb + hh * kv.v_sh;
     // K: unit = 4 consecutive features of one key
     for (int u = threadIdx.x; u < BKV * D / 4; u += blockDim.x) {
         const int r = u / (D / 4), d = (u % (D / 4)) * 4;
-        float4 x = k0 + r < S ? *reinterpret_cast<const float4*>(kb + (size_t)(k0 + r) * D + d)
+        float4 x = k0 + r < S ? *reinterpret_cast<const float4*>(kb + (int64_t)(k0 + r) * kv.k_ss + d)
                               : make_float4(0.f, 0.f, 0.f, 0.f);
         float4 hi = make_float4(tf32_round(x.x), tf32_round(x.y), tf32_round(x.z), tf32_round(x.w));
         uint8_t* kc = tile + (size_t)(d >> 5) * CHUNK + swz(r, d & 31);
@@ -113,7 +123,7 @@ __global__ void __launch_bounds__(256) pack_kv_kernel(const float* __restrict__ 
         for (int u = threadIdx.x; u < 32 * D / 4; u += blockDim.x) {
             const int r = u / (D / 4), d = (u % (D / 4)) * 4;
             const int key = k0 + kb32 + r;
-            float4 x = key < S ? *reinterpret_cast<const float4*>(vb + (size_t)key * D + d)
+            float4 x = key < S ? *reinterpret_cast<const float4*>(vb + (int64_t)key * kv.v_ss + d)
                                : make_float4(0.f, 0.f, 0.f, 0.f);
             sv[r][d] = x.x; sv[r][d + 1] = x.y; sv[r][d + 2] = x.z; sv[r][d + 3] = x.w;
         }
@@ -297,7 +307,7 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
         const int q = q0 + row;
         const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
         constexpr int DH = D / 2, KH = BKV / 2;   // per-thread output columns / score columns
-        const float* qrow = p.q + ((int64_t)bh * p.S + (q < p.S ? q : 0)) * D;
+        const float* qrow = p.q + (bh / p.H) * p.q_sb + (bh % p.H) * p.q_sh + (int64_t)(q < p.S ? q : 0) * p.q_ss;
         const float sl2 = p.scale * 1.4426950408889634f;   // scores in log2 units: exp(x) = 2^(x log2 e)
         auto pair_sync = [&](int which, uint32_t parity) -> bool {
             uint64_t* b = &pair_bar[quarter * 3 + which];
@@ -420,7 +430,7 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
             l += red[(fb * 2 + (half ^ 1)) * BQ + row];
             if (paired && q < p.S) {
                 const float inv = 1.0f / l;
-                float* orow = p.o + ((int64_t)bh * p.S + q) * D + half * DH;
+                float* orow = p.o + (bh / p.H) * p.o_sb + (bh % p.H) * p.o_sh + (int64_t)q * p.o_ss + half * DH;
 #pragma unroll
                 for (int i = 0; i < DH; i += 4)
                     *reinterpret_cast<float4*>(orow + i) =
@@ -477,25 +487,29 @@ Status attention_tc_prepare() {
     return Status::ok();
 }
 
-Status launch_attention_tc(const float* q, const float* k, const float* v, float* o, int64_t BH, int64_t S,
-                           int D, int group, int causal, Workspace ws, cudaStream_t st, int* launches) {
+Status launch_attention_tc(const AttnViews& vw, int64_t BH, int64_t S, int D, int group, int causal,
+                           Workspace ws, cudaStream_t st, int* launches) {
     const int64_t BHkv = BH / group;
     if (ws.bytes < attention_tc_workspace(BHkv, S, D))
         return Status::err(RT_ERR_ARGUMENT, "attention: workspace too small");
     const int n_kv = (int)((S + BKV - 1) / BKV);
     dim3 pgrid((unsigned)n_kv, (unsigned)BHkv);
+    KvViews kv{vw.k, vw.v, vw.k_sb, vw.k_sh, vw.k_ss, vw.v_sb, vw.v_sh, vw.v_ss, vw.H / group};
     if (D == 64)
-        pack_kv_kernel<64><<<pgrid, 256, 0, st>>>(k, v, reinterpret_cast<uint8_t*>(ws.base), (int)S, n_kv);
+        pack_kv_kernel<64><<<pgrid, 256, 0, st>>>(kv, reinterpret_cast<uint8_t*>(ws.base), (int)S, n_kv);
     else
-        pack_kv_kernel<128><<<pgrid, 256, 0, st>>>(k, v, reinterpret_cast<uint8_t*>(ws.base), (int)S, n_kv);
+        pack_kv_kernel<128><<<pgrid, 256, 0, st>>>(kv, reinterpret_cast<uint8_t*>(ws.base), (int)S, n_kv);
     RT_LAUNCH_CHECK();
     *launches += 1;
     AttnTcParams prm;
     memset(&prm, 0, sizeof prm);
     prm.kv = reinterpret_cast<const uint8_t*>(ws.base);
     prm.n_kv = n_kv;
-    prm.q = q;
-    prm.o = o;
+    prm.q = vw.q;
+    prm.o = vw.o;
+    prm.q_sb = vw.q_sb; prm.q_sh = vw.q_sh; prm.q_ss = vw.q_ss;
+    prm.o_sb = vw.o_sb; prm.o_sh = vw.o_sh; prm.o_ss = vw.o_ss;
+    prm.H = vw.H;
     prm.S = (int)S;
     prm.group = group;
     prm.causal = causal;

@@ -6,6 +6,7 @@
 #include <string.h>
 
 #include <string>
+#include <vector>
 
 #include "b200exec.h"
 
@@ -80,6 +81,30 @@ Status launch_gemm(const OpNode& n, cudaStream_t st, Workspace ws, int* launches
 Status prepare_gemm(const OpNode& n, cudaStream_t st);   // constant splits, before capture
 
 Status launch_attention(const OpNode& n, cudaStream_t st, Workspace ws, int* launches);
+// Strided operands of a fused attention: element (b, h, s, d) of X lives at
+// X + b*X_sb + h*X_sh + s*X_ss + d.  Produced by the plan's layout fusion.
+struct AttnViews {
+    const float* q;
+    const float* k;
+    const float* v;
+    float* o;
+    int64_t q_sb, q_sh, q_ss, k_sb, k_sh, k_ss, v_sb, v_sh, v_ss, o_sb, o_sh, o_ss;
+    int H;   // query heads per batch element
+};
+// Contiguous [B, H, S, D] views of an ATTENTION node's operands (4-D nodes only).
+bool attention_default_views(const OpNode& n, AttnViews* v);
+// Whether the tensor-core kernel (which takes strided views) runs this node.
+bool attention_takes_views(const OpNode& n);
+Status launch_attention_views(const OpNode& n, const AttnViews& v, cudaStream_t st, Workspace ws, int* launches);
+
+// Per-node outcome of the plan-time layout fusion (fusion.cu).
+struct PlanItem {
+    bool skip = false;    // producer folded into its consumer: not launched
+    bool views = false;   // attention launched with `attn` (strided operands)
+    AttnViews attn{};
+};
+std::vector<PlanItem> plan_fusions(const std::vector<OpNode>& nodes,
+                                   const std::vector<std::pair<uintptr_t, size_t>>& protected_ranges);
 size_t attention_workspace_bytes(const OpNode& n);
 Status prepare_attention(const OpNode& n);
 Status launch_elementwise(const OpNode& n, cudaStream_t st, int* launches);

@@ -11,6 +11,7 @@
 // does when it patches input pointers (runtime/executor/compiled.py:77-82);
 // with device staging buffers for graph inputs those pointers never change.
 #include <stdio.h>
+#include <stdlib.h>
 
 #include <map>
 #include <memory>
@@ -24,6 +25,7 @@
 namespace rt {
 
 int g_num_sms = 148;
+
 
 namespace {
 
@@ -41,6 +43,7 @@ struct Plan {
     size_t ws_total = 0;
     cudaGraphExec_t exec = nullptr;
     int launches = 0;
+    std::vector<PlanItem> items;   // per node: skipped by layout fusion / strided attention
 };
 
 struct State {
@@ -52,6 +55,7 @@ struct State {
     std::unordered_map<uint64_t, std::vector<std::unique_ptr<Plan>>> plans;
     int last_error = RT_OK;
     std::string last_msg;
+    std::vector<std::pair<uintptr_t, size_t>> protect;   // graph outputs (rt_protect)
     volatile int* kerr_host = nullptr;   // host-mapped error word written by kernels
     int* kerr_dev = nullptr;
 };
@@ -276,10 +280,18 @@ Status launch_node(const OpNode& n, cudaStream_t st, Workspace ws, int* launches
     }
 }
 
+Status launch_item(Plan& p, size_t i, cudaStream_t st, int* launches) {
+    Workspace ws{p.ws + p.ws_offset[i], p.ws_bytes[i]};
+    if (i < p.items.size()) {
+        if (p.items[i].skip) return Status::ok();
+        if (p.items[i].views) return launch_attention_views(p.nodes[i], p.items[i].attn, st, ws, launches);
+    }
+    return launch_node(p.nodes[i], st, ws, launches);
+}
+
 Status launch_all(Plan& p, cudaStream_t st, int* launches) {
     for (size_t i = 0; i < p.nodes.size(); i++) {
-        Workspace ws{p.ws + p.ws_offset[i], p.ws_bytes[i]};
-        Status s = launch_node(p.nodes[i], st, ws, launches);
+        Status s = launch_item(p, i, st, launches);
         if (!s.good()) {
             s.msg = "node " + std::to_string(i) + " (op " + std::to_string(p.nodes[i].op) + "): " + s.msg;
             return s;
@@ -301,6 +313,13 @@ Status build_plan(const OpNode* nodes, int n, bool capture, Plan** out) {
     for (int i = 0; i < n; i++) {
         Status s = validate_node(nodes[i], i);
         if (!s.good()) return s;
+    }
+    plan->items = plan_fusions(plan->nodes, S().protect);
+    if (getenv("RT_FUSE_VERBOSE")) {
+        int skipped = 0, viewed = 0;
+        for (auto& it : plan->items) { skipped += it.skip; viewed += it.views; }
+        fprintf(stderr, "[b200exec] plan of %d nodes: %d skipped by layout fusion, %d strided attention\n", n,
+                skipped, viewed);
     }
     size_t total = 0;
     for (int i = 0; i < n; i++) {
@@ -692,8 +711,7 @@ int rt_profile(const OpNode* nodes, int n, int reps, float* ms_per_node) {
         cudaEventRecord(ev[0], st);
         int launches = 0;
         for (int i = 0; i < n && s.good(); i++) {
-            Workspace ws{p->ws + p->ws_offset[i], p->ws_bytes[i]};
-            s = launch_node(p->nodes[i], st, ws, &launches);
+            s = launch_item(*p, (size_t)i, st, &launches);
             cudaEventRecord(ev[i + 1], st);
         }
         if (cudaEventSynchronize(ev[n]) != cudaSuccess) s = Status::err(RT_ERR_CUDA, "profile sync");
@@ -728,6 +746,40 @@ int rt_synchronize(void) {
 }
 
 void* rt_stream(void) { return S().stream; }
+
+int rt_protect(const void* ptr, size_t bytes) {
+    RT_GUARD;
+    if (!ptr) return fail(RT_ERR_NULL_POINTER, "rt_protect: NULL");
+    S().protect.push_back({reinterpret_cast<uintptr_t>(ptr), bytes});
+    if (S().initialized) {   // plans built without this range may have folded it away
+        cudaStreamSynchronize(S().stream);
+        clear_plans();
+    }
+    return RT_OK;
+}
+
+int rt_unprotect_all(void) {
+    RT_GUARD;
+    S().protect.clear();
+    if (S().initialized) {
+        cudaStreamSynchronize(S().stream);
+        clear_plans();
+    }
+    return RT_OK;
+}
+
+int rt_fusion_report(const OpNode* nodes, int n, int* skipped) {
+    if (n < 0 || (n > 0 && !nodes)) return -RT_ERR_ARGUMENT;
+    std::vector<OpNode> v(nodes, nodes + n);
+    std::vector<PlanItem> items = plan_fusions(v, S().protect);
+    int count = 0;
+    for (int i = 0; i < n; i++) {
+        int f = items[i].skip ? 1 : (items[i].views ? 2 : 0);
+        if (skipped) skipped[i] = f;
+        count += items[i].skip;
+    }
+    return count;
+}
 
 int rt_last_error(void) { return S().last_error; }
 const char* rt_last_error_message(void) { return S().last_msg.c_str(); }

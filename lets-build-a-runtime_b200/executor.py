@@ -68,6 +68,8 @@ def load_library(path: str | Path | None = None) -> ctypes.CDLL:
         "rt_kernel_launches": ([ctypes.POINTER(COpNode), i], i),
         "rt_profile": ([ctypes.POINTER(COpNode), i, i, ctypes.POINTER(ctypes.c_float)], i),
         "rt_reset_plans": ([], i), "rt_synchronize": ([], i), "rt_stream": ([], vp),
+        "rt_fusion_report": ([ctypes.POINTER(COpNode), i, ctypes.POINTER(ctypes.c_int)], i),
+        "rt_protect": ([vp, sz], i), "rt_unprotect_all": ([], i),
         "rt_last_error": ([], i), "rt_last_error_message": ([], ctypes.c_char_p),
         "rt_clear_error": ([], None),
     }
@@ -182,6 +184,9 @@ class CudaCompiledExecutor:
             self._h2d[k] = RtCopy(self._in_dev[name], self._in_host[name].ctypes.data,
                                   self._in_host[name].nbytes)
         self._d2h = (RtCopy * max(1, len(self._out_host)))()
+        # graph outputs must be materialised: keep layout fusion away from them
+        for name, spec in program.outputs.items():
+            check(lib, lib.rt_protect(resolve(spec["ref"]), self._out_host[name].nbytes), "protect")
         for k, (name, spec) in enumerate(program.outputs.items()):
             self._d2h[k] = RtCopy(self._out_host[name].ctypes.data, resolve(spec["ref"]),
                                   self._out_host[name].nbytes)
