@@ -167,6 +167,7 @@ struct Proposal {
     std::vector<std::pair<Range, int>> sources;   // range read through a view, chain start index
     Range out{};                                  // what the fused attention writes
     int out_skip = -1;                            // merge TRANSPOSE folded into the attention
+    std::vector<std::pair<int, int>> redirect;    // (node, input slot) now reading `out` instead of the merge's output
 };
 
 // Pattern: operand written by a head-split TRANSPOSE [B,S,Hx,D] -> [B,Hx,S,D],
@@ -236,6 +237,44 @@ void match_output(const Analysis& an, int a, int64_t B, int64_t H, int64_t S, in
     }
 }
 
+// Variant: the attention writes the merged [B,S,H,D] layout into its own
+// output buffer and the merge's readers are redirected there.
+bool match_output_inplace(const Analysis& an, int a, int64_t B, int64_t H, int64_t S, int64_t D, Proposal& pr) {
+    Proposal tmp = pr;
+    match_output(an, a, B, H, S, D, tmp);
+    if (tmp.out_skip < 0) return false;
+    const int u = tmp.out_skip;
+    const OpNode& tr = an.nodes[u];
+    const Range U = an.writes[u];
+    // readers of U until it is rewritten: each must read exactly U through one input slot
+    std::vector<std::pair<int, int>> red;
+    for (size_t j = u + 1; j < an.nodes.size(); j++) {
+        bool rd = false;
+        for (const Range& x : an.reads[j]) rd |= overlaps(x, U);
+        if (rd) {
+            int slot = -1, hits = 0;
+            for (int i = 0; i < an.nodes[j].n_inputs; i++)
+                if (an.nodes[j].inputs[i] == tr.output) { slot = i; hits++; }
+            if (hits != 1 || an.reads[j].size() <= (size_t)slot || an.reads[j][slot].hi - an.reads[j][slot].lo !=
+                                                                         U.hi - U.lo)
+                return false;
+            for (size_t i = 0; i < an.reads[j].size(); i++)
+                if ((int)i != slot && overlaps(an.reads[j][i], U)) return false;
+            red.push_back({(int)j, slot});
+        }
+        if (overlaps(an.writes[j], U)) break;
+    }
+    if (red.empty()) return false;
+    pr.out_skip = u;
+    pr.out = an.writes[a];
+    pr.views.o = static_cast<float*>(an.nodes[a].output);
+    pr.views.o_sb = S * H * D;
+    pr.views.o_sh = D;
+    pr.views.o_ss = H * D;
+    pr.redirect = red;
+    return true;
+}
+
 // The node array as it would execute with the proposals applied: skipped
 // nodes neither read nor write; a fused attention reads its view sources.
 struct Effective {
@@ -266,6 +305,10 @@ Effective effective(const Analysis& an, const std::vector<Proposal>& props) {
         for (auto& sr : p.sources) r.push_back(sr.first);
         e.reads[p.a] = r;
         e.writes[p.a] = p.out;
+        for (auto& rd : p.redirect) {   // redirected readers see the attention's buffer
+            const int j = rd.first, slot = rd.second;
+            e.reads[j][slot] = rng(an.nodes[p.a].output, (size_t)(an.reads[j][slot].hi - an.reads[j][slot].lo));
+        }
     }
     for (size_t j = 0; j < n; j++)
         if (e.skipped[j]) {
@@ -324,7 +367,29 @@ bool valid(const Analysis& an, const Effective& e, const Proposal& p, const std:
     }
     for (auto& k : p.skips)
         if (!dead_output(an, k.first, k.second, protect)) FAIL("a folded node's output is still needed");
-    if (p.out_skip >= 0) {
+    if (p.out_skip >= 0 && !p.redirect.empty()) {
+        // the merged result stays in the attention's buffer until its last reader
+        const int last = p.redirect.back().first;
+        for (int j = p.a + 1; j < last; j++)
+            if (overlaps(e.writes[j], p.out)) FAIL("merged output overwritten before its readers");
+        // the attention buffer's original reader was the merge only
+        if (!dead_output(an, p.a, p.out_skip, protect)) FAIL("attention output still needed");
+        // the merge's output: read only by the redirected nodes, never a graph output
+        const Range U = an.writes[p.out_skip];
+        for (size_t j = p.out_skip + 1; j < an.nodes.size(); j++) {
+            bool redirected = false;
+            for (auto& rd : p.redirect) redirected |= rd.first == (int)j;
+            if (!redirected && eff_reads(e, (int)j, U)) FAIL("merge output read elsewhere");
+            if (overlaps(an.writes[j], U)) break;
+        }
+        bool rewritten = false;
+        for (size_t j = p.out_skip + 1; j < an.nodes.size(); j++) rewritten |= overlaps(an.writes[j], U);
+        if (!rewritten)
+            for (const Range& pr : protect)
+                if (overlaps(pr, U)) FAIL("merge output is a graph output");
+        for (auto& sr : p.sources)
+            if (overlaps(sr.first, p.out)) FAIL("output overlaps a source");
+    } else if (p.out_skip >= 0) {
         // nothing between the attention and the folded merge touches either buffer
         for (int j = p.a + 1; j < p.out_skip; j++)
             if (overlaps(e.writes[j], p.out) || eff_reads(e, j, p.out) || eff_reads(e, j, an.writes[p.a]))
@@ -379,6 +444,8 @@ std::vector<PlanItem> plan_fusions(const std::vector<OpNode>& nodes,
         Proposal with_out = pr;
         match_output(an, (int)a, B, H, S, D, with_out);
         if (with_out.out_skip >= 0) c.push_back(with_out);
+        Proposal inplace = pr;
+        if (match_output_inplace(an, (int)a, B, H, S, D, inplace)) c.push_back(inplace);
         if (!pr.skips.empty()) c.push_back(pr);
         if (!c.empty()) cands.push_back(c);
     }
@@ -402,6 +469,10 @@ std::vector<PlanItem> plan_fusions(const std::vector<OpNode>& nodes,
                 items[p.a].attn = p.views;
                 for (auto& k : p.skips) items[k.first].skip = true;
                 if (p.out_skip >= 0) items[p.out_skip].skip = true;
+                for (auto& rd : p.redirect) {
+                    items[rd.first].redirect_slot = rd.second;
+                    items[rd.first].redirect_ptr = an.nodes[p.a].output;
+                }
             }
             break;
         }

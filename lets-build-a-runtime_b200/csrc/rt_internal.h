@@ -102,6 +102,8 @@ struct PlanItem {
     bool skip = false;    // producer folded into its consumer: not launched
     bool views = false;   // attention launched with `attn` (strided operands)
     AttnViews attn{};
+    int redirect_slot = -1;        // input slot now reading `redirect_ptr` (a folded producer's source)
+    void* redirect_ptr = nullptr;
 };
 std::vector<PlanItem> plan_fusions(const std::vector<OpNode>& nodes,
                                    const std::vector<std::pair<uintptr_t, size_t>>& protected_ranges);

@@ -285,6 +285,11 @@ Status launch_item(Plan& p, size_t i, cudaStream_t st, int* launches) {
     if (i < p.items.size()) {
         if (p.items[i].skip) return Status::ok();
         if (p.items[i].views) return launch_attention_views(p.nodes[i], p.items[i].attn, st, ws, launches);
+        if (p.items[i].redirect_slot >= 0) {
+            OpNode n = p.nodes[i];
+            n.inputs[p.items[i].redirect_slot] = p.items[i].redirect_ptr;
+            return launch_node(n, st, ws, launches);
+        }
     }
     return launch_node(p.nodes[i], st, ws, launches);
 }

@@ -42,11 +42,11 @@ def report(prog, arr):
     return n, list(flags)
 
 
-def test_gpt2_head_split_copies_fold_into_attention():
+def test_gpt2_head_split_and_merge_copies_fold_into_attention():
     prog = Program.load(GOLDEN / "gpt2_b8.json")
     arr, _ = bind(prog)
     n, flags = report(prog, arr)
-    assert n == 12
+    assert n == 14   # per layer: 3 slices + 3 head splits + the head merge
     folded_ops = {prog.nodes[i].op for i, f in enumerate(flags) if f == 1}
     assert folded_ops == {OP["SLICE"], OP["TRANSPOSE"]}
     assert [prog.nodes[i].op for i, f in enumerate(flags) if f == 2] == [OP["ATTENTION"]] * 2
