@@ -1,13 +1,31 @@
 // k_gemm_tc.cu -- MATMUL / MATMUL_ADD on the 5th-generation tensor cores.
 //
-// fp32 accuracy from tf32 tensor cores by the 3xTF32 split: every operand
-// x is written as hi + lo with hi = x rounded to tf32 (cvt.rna.tf32.f32,
-// low 13 mantissa bits zero) and lo = x - hi (exact in fp32), and
+// fp32 accuracy from reduced-precision tensor cores.  Every operand x is
+// written as hi + lo with hi = x rounded to tf32 (cvt.rna.tf32.f32, low 13
+// mantissa bits zero) and lo = x - hi (exact in fp32, |lo| <= 2^-11 |x|), and
 //     A.B ~= A_hi.B_hi + A_hi.B_lo + A_lo.B_hi
-// (the dropped A_lo.B_lo term is ~2^-22 relative).  Constant B operands
-// (weights) are split once per plan and cached; A (activations) is split per
-// launch by a bandwidth-bound pre-pass into the node's workspace.  Both split
-// operands are stored K-major.
+// (the dropped A_lo.B_lo term is ~2^-22 relative).  Two ways to issue it:
+//
+//  * tf32 + bf16 cross terms (default): A_hi.B_hi is one kind::tf32 MMA (a
+//    product of two tf32 values is exact in fp32); the two cross terms only
+//    need ~8 significant bits each, so they run as ONE kind::f16 (bf16) MMA
+//    over a doubled K: A' = [bf16(A_hi) | bf16(A_lo)], B' = [bf16(B_lo) |
+//    bf16(B_hi)].  Rounding the cross operands to bf16 costs ~2^-19 of
+//    |a||b| per product.  bf16 MMAs run at twice the tf32 rate, so a K block
+//    takes 4 MMA instructions instead of 6 (1.5x less tensor time).
+//  * 3xTF32 (RT_GEMM_3XTF32=1): three kind::tf32 MMAs, hi.hi + hi.lo + lo.hi.
+//
+// Both schemes store two planes per operand, K-major, 4 bytes per element:
+// plane 0 = hi (tf32 in fp32 words); plane 1 = lo (fp32) for 3xTF32, or the
+// "cross" plane for the default: per row and per K block of 16 (width w =
+// min(16, K - 16*kb)), 2w bf16 values [first(0..w-1) | second(0..w-1)] in the
+// block's 64 bytes, first/second = hi/lo for A and lo/hi for B.  The same
+// 64-byte TMA box serves both; a short last block lands its second half where
+// the first MMA still reads it and the rest is TMA zero fill.
+//
+// Constant B operands (weights) are split once per plan and cached; A
+// (activations) is split per launch by a bandwidth-bound pre-pass into the
+// node's workspace.
 //
 // The tensor core's fp32 accumulation does not round like IEEE adds, and its
 // error grows with the number of MMAs summed into one accumulator (measured
@@ -17,13 +35,13 @@
 // level of OpenBLAS sgemm (1.6e-5 at K=16384) at no measurable cost.
 //
 // Kernel: persistent, one CTA per SM, 320 threads in three roles:
-//   warp 0     TMA producer: per K-block, four tile loads (A_hi, A_lo,
-//              B_hi, B_lo; 64-byte swizzle, 16 fp32 of K per row) into a
+//   warp 0     TMA producer: per K-block, four tile loads (A plane 0/1,
+//              B plane 0/1; 64-byte swizzle, 64 bytes of K per row) into a
 //              4-stage shared-memory ring;
 //   warp 1     allocates 512 TMEM columns (two 128x256 fp32 accumulators)
-//              and issues the tcgen05.mma (kind::tf32, M=128, N=256, K=8)
-//              from one thread; tcgen05.commit frees ring stages and
-//              publishes each finished K chunk;
+//              and issues the tcgen05.mma (M=128, N=256) from one thread;
+//              tcgen05.commit frees ring stages and publishes each finished
+//              K chunk;
 //   warps 2-9  epilogue: tcgen05.ld of the accumulator (warp w reads TMEM
 //              lanes 32*(w%4)..+31 = tile rows, one half of the columns),
 //              sums the chunks in registers, then alpha / bias and one
@@ -33,6 +51,7 @@
 // (bounded), frees TMEM and returns.
 #include <cuda.h>
 #include <cudaTypedefs.h>
+#include <cuda_bf16.h>
 #include <stdlib.h>
 
 #include <mutex>
@@ -89,7 +108,7 @@ __device__ __forceinline__ void tile_coords(const TcParams& p, int item, int& m_
     kb_hi = min(p.k_blocks, kb_lo + p.kb_split);
 }
 
-template <int BN_>
+template <int BN_, bool CROSS>
 __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
     constexpr int BN = GCfg<BN_>::BN, STAGES = GCfg<BN_>::STAGES, EPI_COLS = GCfg<BN_>::EPI_COLS;
     constexpr int B_TILE = GCfg<BN_>::B_TILE, STAGE_BYTES = GCfg<BN_>::STAGE_BYTES;
@@ -165,6 +184,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {
             constexpr uint32_t idesc = ptx::idesc_tf32(BM, BN);
+            constexpr uint32_t idesc_x = ptx::idesc_bf16(BM, BN);
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
@@ -192,17 +212,31 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
                         }
                         ptx::tc_fence_after();
                         uint8_t* st = smem + stage * STAGE_BYTES;
+                        const uint32_t acc0 = kb > kb0 ? 1u : 0u;
+                        if (CROSS) {
+                            // hi.hi: two tf32 K=8 steps (+32 bytes each inside the 64-byte atom)
 #pragma unroll
-                        for (int kk = 0; kk < BK / 8; kk++) {
-                            // K advance inside the 64-byte swizzle atom: +32 bytes per 8 fp32
-                            uint64_t a_hi = ptx::smem_desc(st + kk * 32, 512, 4);
-                            uint64_t a_lo = ptx::smem_desc(st + A_TILE + kk * 32, 512, 4);
-                            uint64_t b_hi = ptx::smem_desc(st + 2 * A_TILE + kk * 32, 512, 4);
-                            uint64_t b_lo = ptx::smem_desc(st + 2 * A_TILE + B_TILE + kk * 32, 512, 4);
-                            uint32_t acc = (kb > kb0 || kk > 0) ? 1u : 0u;
-                            ptx::mma_tf32(d_tmem, a_hi, b_hi, idesc, acc);
-                            ptx::mma_tf32(d_tmem, a_hi, b_lo, idesc, 1u);
-                            ptx::mma_tf32(d_tmem, a_lo, b_hi, idesc, 1u);
+                            for (int kk = 0; kk < 2; kk++)
+                                ptx::mma_tf32(d_tmem, ptx::smem_desc(st + kk * 32, 512, 4),
+                                              ptx::smem_desc(st + 2 * A_TILE + kk * 32, 512, 4), idesc,
+                                              (acc0 | kk) ? 1u : 0u);
+                            // cross terms: two bf16 K=16 steps over the doubled K
+#pragma unroll
+                            for (int kk = 0; kk < 2; kk++)
+                                ptx::mma_bf16(d_tmem, ptx::smem_desc(st + A_TILE + kk * 32, 512, 4),
+                                              ptx::smem_desc(st + 2 * A_TILE + B_TILE + kk * 32, 512, 4),
+                                              idesc_x, 1u);
+                        } else {
+#pragma unroll
+                            for (int kk = 0; kk < BK / 8; kk++) {
+                                uint64_t a_hi = ptx::smem_desc(st + kk * 32, 512, 4);
+                                uint64_t a_lo = ptx::smem_desc(st + A_TILE + kk * 32, 512, 4);
+                                uint64_t b_hi = ptx::smem_desc(st + 2 * A_TILE + kk * 32, 512, 4);
+                                uint64_t b_lo = ptx::smem_desc(st + 2 * A_TILE + B_TILE + kk * 32, 512, 4);
+                                ptx::mma_tf32(d_tmem, a_hi, b_hi, idesc, (acc0 | kk) ? 1u : 0u);
+                                ptx::mma_tf32(d_tmem, a_hi, b_lo, idesc, 1u);
+                                ptx::mma_tf32(d_tmem, a_lo, b_hi, idesc, 1u);
+                            }
                         }
                         ptx::mma_commit(&empty[stage]);
                         if (++stage == STAGES) {
@@ -307,6 +341,259 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
     }
 }
 
+// ---- CTA-pair kernel: 256 x 256 tiles on tcgen05 cta_group::2 -------------
+// A cluster of two CTAs on two SMs computes one 256x256 tile per work item:
+// each CTA loads its own 128 rows of A and 128 rows of B (a 128x256 operand
+// slice per SM instead of 128x384), so shared-memory traffic per flop drops
+// by a third -- the 1-CTA kernel is bound by shared-memory bandwidth (TMA
+// writes plus MMA operand reads), not by the tensor pipe.
+//   * both CTAs' copies complete on the LEADER's (rank 0) full barrier, whose
+//     producer posts the expected bytes of both;
+//   * the leader's MMA thread issues M=256 MMAs over the pair; its commits
+//     arrive on the empty / accumulator-full barriers of both CTAs;
+//   * each CTA's epilogue drains its own TMEM (its 128 rows) and releases the
+//     accumulator on the leader's barrier (one arrival per warp).
+constexpr int P_STAGES = 6;
+constexpr int P_TILE = 128 * BK * 4;                   // 8 KiB: one plane of 128 rows
+constexpr int P_STAGE_BYTES = 4 * P_TILE;              // A hi / A plane1 / B hi / B plane1
+constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
+constexpr int P_EPI_COLS = 128;
+
+template <bool CROSS>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    tc_gemm_pair_kernel(const __grid_constant__ TcParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem =
+        reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P_STAGES * P_STAGE_BYTES);
+    uint64_t* full = bars;                          // [P_STAGES] (leader's are used)
+    uint64_t* empty = bars + P_STAGES;              // [P_STAGES]
+    uint64_t* acc_full = bars + 2 * P_STAGES;       // [2]
+    uint64_t* acc_empty = bars + 2 * P_STAGES + 2;  // [2]   (leader's are used)
+    uint64_t* drain = bars + 2 * P_STAGES + 4;      // [1]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * P_STAGES + 5);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    int* issued_phase = const_cast<int*>(abort_flag) + 1;   // [P_STAGES]
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = ptx::cluster_ctarank();
+    const bool leader = rank == 0;
+    const int cluster = blockIdx.x >> 1, n_clusters = gridDim.x >> 1;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < P_STAGES; s++) {
+            ptx::mbar_init(&full[s], 1);
+            ptx::mbar_init(&empty[s], 1);
+            issued_phase[s] = -1;
+        }
+        for (int b = 0; b < 2; b++) {
+            ptx::mbar_init(&acc_full[b], 1);
+            ptx::mbar_init(&acc_empty[b], 2 * EPI_WARPS);
+        }
+        ptx::mbar_init(drain, 1);
+        *abort_flag = 0;
+        ptx::fence_mbar_init();
+        ptx::prefetch_tmap(&p.ta_hi);
+        ptx::prefetch_tmap(&p.ta_lo);
+        ptx::prefetch_tmap(&p.tb_hi);
+        ptx::prefetch_tmap(&p.tb_lo);
+    }
+    if (warp == 1) ptx::tmem_alloc_pair(tmem_slot, 512);
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::cluster_sync();   // barriers of both CTAs initialised, TMEM of both allocated
+    ptx::tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------ TMA producer (both CTAs)
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (int t = cluster; t < p.total_items && ok; t += n_clusters) {
+                int m_blk, n_blk, bz, kb_lo, kb_hi;
+                tile_coords(p, t, m_blk, n_blk, bz, kb_lo, kb_hi);
+                const int arow = m_blk * 256 + (int)rank * 128, brow = n_blk * 256 + (int)rank * 128;
+                for (int kb = kb_lo; kb < kb_hi; kb++) {
+                    if (!ptx::wait_bounded(&empty[stage], phase ^ 1, abort_flag, p.err, ERR_PRODUCER,
+                                           WAIT_LIMIT_NS)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* st = smem + stage * P_STAGE_BYTES;
+                    const uint32_t bar = ptx::mapa_shared(ptx::smem_u32(&full[stage]), 0);
+                    if (leader) {
+                        ptx::mbar_expect_tx(&full[stage], 2 * P_STAGE_BYTES);
+                        issued_phase[stage] = (int)phase;
+                    }
+                    const int k0 = kb * BK;
+                    ptx::tma_load_3d_pair(st, &p.ta_hi, bar, k0, arow, bz);
+                    ptx::tma_load_3d_pair(st + P_TILE, &p.ta_lo, bar, k0, arow, bz);
+                    ptx::tma_load_3d_pair(st + 2 * P_TILE, &p.tb_hi, bar, k0, brow, bz);
+                    ptx::tma_load_3d_pair(st + 3 * P_TILE, &p.tb_lo, bar, k0, brow, bz);
+                    if (++stage == P_STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------ MMA issuer (leader only)
+        if (leader && lane == 0) {
+            constexpr uint32_t idesc = ptx::idesc_tf32(256, 256);
+            constexpr uint32_t idesc_x = ptx::idesc_bf16(256, 256);
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            int it = 0;
+            for (int t = cluster; t < p.total_items && ok; t += n_clusters) {
+                int m_blk, n_blk, bz, kb_lo, kb_hi;
+                tile_coords(p, t, m_blk, n_blk, bz, kb_lo, kb_hi);
+                const int n_chunks = (kb_hi - kb_lo + p.kb_per_chunk - 1) / p.kb_per_chunk;
+                for (int c = 0; c < n_chunks && ok; c++, it++) {
+                    const int b = it & 1;
+                    const uint32_t acc_phase = (it >> 1) & 1;
+                    if (!ptx::wait_bounded(&acc_empty[b], acc_phase ^ 1, abort_flag, p.err, ERR_MMA,
+                                           WAIT_LIMIT_NS)) {
+                        ok = false;
+                        break;
+                    }
+                    ptx::tc_fence_after();
+                    const uint32_t d_tmem = tmem_base + b * 256;
+                    const int kb0 = kb_lo + c * p.kb_per_chunk;
+                    const int kb_end = min(kb_hi, kb0 + p.kb_per_chunk);
+                    for (int kb = kb0; kb < kb_end; kb++) {
+                        if (!ptx::wait_bounded(&full[stage], phase, abort_flag, p.err, ERR_MMA, WAIT_LIMIT_NS)) {
+                            ok = false;
+                            break;
+                        }
+                        ptx::tc_fence_after();
+                        uint8_t* st = smem + stage * P_STAGE_BYTES;
+                        const uint32_t acc0 = kb > kb0 ? 1u : 0u;
+                        if (CROSS) {
+#pragma unroll
+                            for (int kk = 0; kk < 2; kk++)
+                                ptx::mma_tf32_pair(d_tmem, ptx::smem_desc(st + kk * 32, 512, 4),
+                                                   ptx::smem_desc(st + 2 * P_TILE + kk * 32, 512, 4), idesc,
+                                                   (acc0 | kk) ? 1u : 0u);
+#pragma unroll
+                            for (int kk = 0; kk < 2; kk++)
+                                ptx::mma_bf16_pair(d_tmem, ptx::smem_desc(st + P_TILE + kk * 32, 512, 4),
+                                                   ptx::smem_desc(st + 3 * P_TILE + kk * 32, 512, 4), idesc_x,
+                                                   1u);
+                        } else {
+#pragma unroll
+                            for (int kk = 0; kk < 2; kk++) {
+                                uint64_t a_hi = ptx::smem_desc(st + kk * 32, 512, 4);
+                                uint64_t a_lo = ptx::smem_desc(st + P_TILE + kk * 32, 512, 4);
+                                uint64_t b_hi = ptx::smem_desc(st + 2 * P_TILE + kk * 32, 512, 4);
+                                uint64_t b_lo = ptx::smem_desc(st + 3 * P_TILE + kk * 32, 512, 4);
+                                ptx::mma_tf32_pair(d_tmem, a_hi, b_hi, idesc, (acc0 | kk) ? 1u : 0u);
+                                ptx::mma_tf32_pair(d_tmem, a_hi, b_lo, idesc, 1u);
+                                ptx::mma_tf32_pair(d_tmem, a_lo, b_hi, idesc, 1u);
+                            }
+                        }
+                        ptx::mma_commit_pair(&empty[stage], 0x3);
+                        if (++stage == P_STAGES) {
+                            stage = 0;
+                            phase ^= 1;
+                        }
+                    }
+                    if (!ok) break;
+                    ptx::mma_commit_pair(&acc_full[b], 0x3);
+                }
+            }
+            ptx::mma_commit_pair(drain, 0x1);
+            volatile int no_abort = 0;
+            ptx::wait_bounded(drain, 0, &no_abort, p.err, ERR_DRAIN, WAIT_LIMIT_NS);
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------ epilogue (warps 2..9, both CTAs)
+        const int quarter = warp & 3;
+        const int half = (warp - 2) >> 2;
+        const int row_in_tile = quarter * 32 + lane;
+        const uint32_t acc_empty_leader0 = ptx::mapa_shared(ptx::smem_u32(&acc_empty[0]), 0);
+        int it = 0;
+        bool ok = true;
+        for (int t = cluster; t < p.total_items && ok; t += n_clusters) {
+            int m_blk, n_blk, bz, kb_lo, kb_hi;
+            tile_coords(p, t, m_blk, n_blk, bz, kb_lo, kb_hi);
+            const int n_chunks = (kb_hi - kb_lo + p.kb_per_chunk - 1) / p.kb_per_chunk;
+            const bool first_split = kb_lo == 0;
+            float acc[P_EPI_COLS];
+            for (int c = 0; c < n_chunks; c++, it++) {
+                const int b = it & 1;
+                const uint32_t acc_phase = (it >> 1) & 1;
+                if (!ptx::wait_bounded(&acc_full[b], acc_phase, abort_flag, p.err, ERR_EPILOGUE,
+                                       WAIT_LIMIT_NS)) {
+                    ok = false;
+                    break;
+                }
+                ptx::tc_fence_after();
+                const uint32_t tbase =
+                    tmem_base + ((uint32_t)(quarter * 32) << 16) + b * 256 + half * P_EPI_COLS;
+#pragma unroll
+                for (int q = 0; q < P_EPI_COLS / 16; q++) {
+                    uint32_t r[16];
+                    ptx::tmem_ld16(tbase + q * 16, r);
+                    ptx::tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 16; j++)
+                        acc[q * 16 + j] =
+                            c == 0 ? __uint_as_float(r[j]) : acc[q * 16 + j] + __uint_as_float(r[j]);
+                }
+                ptx::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) ptx::mbar_arrive_cluster(acc_empty_leader0 + b * 8);
+            }
+            if (!ok) break;
+            const int64_t row = (int64_t)m_blk * 256 + rank * 128 + row_in_tile;
+            if (row >= p.M) continue;
+            float* crow = p.c + ((int64_t)bz * p.M + row) * p.N;
+            const int col0 = n_blk * 256 + half * P_EPI_COLS;
+            const bool add_bias = p.bias && first_split;
+            if ((p.N & 3) == 0 && col0 + P_EPI_COLS <= p.N) {
+#pragma unroll
+                for (int j = 0; j < P_EPI_COLS; j += 4) {
+                    float4 v = make_float4(p.alpha * acc[j], p.alpha * acc[j + 1], p.alpha * acc[j + 2],
+                                           p.alpha * acc[j + 3]);
+                    if (add_bias) {
+                        float4 bb = *reinterpret_cast<const float4*>(p.bias + col0 + j);
+                        v.x += bb.x; v.y += bb.y; v.z += bb.z; v.w += bb.w;
+                    }
+                    if (p.splits > 1) atomicAdd(reinterpret_cast<float4*>(crow + col0 + j), v);
+                    else *reinterpret_cast<float4*>(crow + col0 + j) = v;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < P_EPI_COLS; j++) {
+                    if (col0 + j < p.N) {
+                        float v = p.alpha * acc[j];
+                        if (add_bias) v += p.bias[col0 + j];
+                        if (p.splits > 1) atomicAdd(crow + col0 + j, v);
+                        else crow[col0 + j] = v;
+                    }
+                }
+            }
+        }
+    }
+
+    __syncthreads();
+    if (threadIdx.x == 0 && leader && *abort_flag) {
+        volatile int no_abort = 0;
+        for (int s = 0; s < P_STAGES; s++)
+            if (issued_phase[s] >= 0)
+                ptx::wait_bounded(&full[s], (uint32_t)issued_phase[s], &no_abort, nullptr, 0, 100000000ull);
+    }
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::cluster_sync();   // the peer's copies, MMA reads and remote arrivals are over
+    ptx::tc_fence_after();
+    if (warp == 1) ptx::tmem_dealloc_pair(tmem_base, 512);
+}
+
 // ---- operand split: hi = tf32(x) (round to nearest), lo = x - hi ----------
 __device__ __forceinline__ float tf32_hi(float x) {
     uint32_t r;
@@ -314,34 +601,74 @@ __device__ __forceinline__ float tf32_hi(float x) {
     return __uint_as_float(r);
 }
 
-__global__ void split_kernel(const float* __restrict__ x, float* __restrict__ hi, float* __restrict__ lo,
-                             int64_t n, bool vec) {
+__device__ __forceinline__ uint16_t bf16_bits(float x) {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(x));
+}
+
+// Plane-1 writer for element k of a row whose plane-1 row starts at `row1`
+// (2K bf16 slots).  mode 0: lo as fp32; mode 1 (A): cross [hi | lo];
+// mode 2 (B): cross [lo | hi].  See the file comment for the block layout.
+__device__ __forceinline__ void put_plane1(float* row1, int64_t k, int64_t K, float h, float l, int mode) {
+    if (mode == 0) {
+        row1[k] = l;
+        return;
+    }
+    const int64_t kb = k >> 4;
+    const int j = (int)(k & 15);
+    const int w = (int)min((int64_t)16, K - kb * 16);
+    uint16_t* blk = reinterpret_cast<uint16_t*>(row1) + kb * 32;
+    blk[j] = bf16_bits(mode == 1 ? h : l);
+    blk[w + j] = bf16_bits(mode == 1 ? l : h);
+}
+
+// [rows][K] -> planes of the same layout.  Vector path: 4 consecutive k of
+// one row per thread (K % 4 == 0 keeps them in one 16-wide block).
+__global__ void split_kernel(const float* __restrict__ x, float* __restrict__ hi, float* __restrict__ p1,
+                             int64_t n, int64_t K, int mode, bool vec) {
     int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
     int64_t stride = (int64_t)gridDim.x * blockDim.x;
     if (vec) {
         for (int64_t i = tid; i < n / 4; i += stride) {
             float4 v = reinterpret_cast<const float4*>(x)[i];
             float4 h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
+            float4 l = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
             reinterpret_cast<float4*>(hi)[i] = h;
-            reinterpret_cast<float4*>(lo)[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+            if (mode == 0) {
+                reinterpret_cast<float4*>(p1)[i] = l;
+                continue;
+            }
+            const int64_t e = i * 4, row = e / K, k = e - row * K;
+            const int64_t kb = k >> 4;
+            const int j = (int)(k & 15);
+            const int w = (int)min((int64_t)16, K - kb * 16);
+            uint16_t* blk = reinterpret_cast<uint16_t*>(p1 + row * K) + kb * 32;
+            const float4 f = mode == 1 ? h : l, g = mode == 1 ? l : h;
+            uint2 fu, gu;
+            fu.x = (uint32_t)bf16_bits(f.x) | ((uint32_t)bf16_bits(f.y) << 16);
+            fu.y = (uint32_t)bf16_bits(f.z) | ((uint32_t)bf16_bits(f.w) << 16);
+            gu.x = (uint32_t)bf16_bits(g.x) | ((uint32_t)bf16_bits(g.y) << 16);
+            gu.y = (uint32_t)bf16_bits(g.z) | ((uint32_t)bf16_bits(g.w) << 16);
+            *reinterpret_cast<uint2*>(blk + j) = fu;       // 8-byte aligned: j, w multiples of 4
+            *reinterpret_cast<uint2*>(blk + w + j) = gu;
         }
     } else {
         for (int64_t i = tid; i < n; i += stride) {
+            const int64_t row = i / K, k = i - row * K;
             float h = tf32_hi(x[i]);
             hi[i] = h;
-            lo[i] = x[i] - h;
+            put_plane1(p1 + row * K, k, K, h, x[i] - h, mode);
         }
     }
 }
 
-// [batches][K][N] -> split of the transpose, [batches][N][K]
+// [batches][K][N] -> planes of the transpose, [batches][N][K]
 __global__ void split_transpose_kernel(const float* __restrict__ x, float* __restrict__ hi,
-                                       float* __restrict__ lo, int K, int N) {
+                                       float* __restrict__ p1, int K, int N, int mode) {
     __shared__ float tile[32][33];
     int64_t bz = blockIdx.z;
     const float* xb = x + bz * (int64_t)K * N;
     float* hb = hi + bz * (int64_t)K * N;
-    float* lb = lo + bz * (int64_t)K * N;
+    float* pb = p1 + bz * (int64_t)K * N;
     int k0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
     for (int r = threadIdx.y; r < 32; r += blockDim.y) {
         int k = k0 + r, n = n0 + threadIdx.x;
@@ -354,22 +681,22 @@ __global__ void split_transpose_kernel(const float* __restrict__ x, float* __res
             float v = tile[threadIdx.x][r];
             float h = tf32_hi(v);
             hb[(int64_t)n * K + k] = h;
-            lb[(int64_t)n * K + k] = v - h;
+            put_plane1(pb + (int64_t)n * K, k, K, h, v - h, mode);
         }
     }
 }
 
-Status run_split(const float* x, float* hi, float* lo, int64_t batches, int64_t rows, int64_t K, bool trans,
-                 cudaStream_t st) {
+Status run_split(const float* x, float* hi, float* p1, int64_t batches, int64_t rows, int64_t K, bool trans,
+                 int mode, cudaStream_t st) {
     if (!trans) {
         int64_t n = batches * rows * K;
-        bool vec = aligned16(x) && n % 4 == 0;
+        bool vec = aligned16(x) && K % 4 == 0;
         int grid = grid_for(vec ? n / 4 : n, 256, 16);
-        split_kernel<<<grid, 256, 0, st>>>(x, hi, lo, n, vec);
+        split_kernel<<<grid, 256, 0, st>>>(x, hi, p1, n, K, mode, vec);
     } else {
         // x is [batches][K][rows]; output [batches][rows][K]
         dim3 grid((unsigned)((rows + 31) / 32), (unsigned)((K + 31) / 32), (unsigned)batches);
-        split_transpose_kernel<<<grid, dim3(32, 8), 0, st>>>(x, hi, lo, (int)K, (int)rows);
+        split_transpose_kernel<<<grid, dim3(32, 8), 0, st>>>(x, hi, p1, (int)K, (int)rows, mode);
     }
     RT_LAUNCH_CHECK();
     return Status::ok();
@@ -425,6 +752,54 @@ bool split_k_enabled() {
     return on;
 }
 
+// Cross-term scheme (default) or RT_GEMM_3XTF32=1 for three tf32 MMAs.
+bool cross_scheme() {
+    static const bool on = [] {
+        const char* e = getenv("RT_GEMM_3XTF32");
+        return !(e && e[0] == '1');
+    }();
+    return on;
+}
+int a_mode() { return cross_scheme() ? 1 : 0; }
+int b_mode() { return cross_scheme() ? 2 : 0; }
+SplitKey b_key(const GemmProblem& p) {
+    return SplitKey{p.b, p.batches, p.N, p.K, (p.trans_b ? 0 : 1) | (cross_scheme() ? 2 : 0)};
+}
+
+// RT_GEMM_PAIR=0 keeps every GEMM on the one-CTA kernel.
+bool pair_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("RT_GEMM_PAIR");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+// CTA pairs the device keeps resident at once (one pair per two SMs unless
+// the GPC layout leaves some SMs unpaired).
+int pair_clusters() {
+    static int n = [] {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * (g_num_sms / 2));
+        cfg.blockDim = dim3(THREADS);
+        cfg.dynamicSmemBytes = P_SMEM_BYTES;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = 2;
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        int c = 0;
+        if (cudaOccupancyMaxActiveClusters(&c, tc_gemm_pair_kernel<true>, &cfg) != cudaSuccess || c <= 0) {
+            cudaGetLastError();
+            c = g_num_sms / 2;
+        }
+        return c;
+    }();
+    return n;
+}
+
 bool b_is_constant(const GemmProblem& p) {
     return is_constant_range(p.b, (size_t)p.batches * p.N * p.K * 4);
 }
@@ -453,19 +828,28 @@ Status tc_gemm_prepare(const GemmProblem& p, cudaStream_t st) {
     if (!tc_gemm_applicable(p)) return Status::ok();
     static bool attr_set = false;
     if (!attr_set) {
-        RT_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           GCfg<256>::SMEM_BYTES));
-        RT_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           GCfg<128>::SMEM_BYTES));
+        RT_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_kernel<256, true>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, GCfg<256>::SMEM_BYTES));
+        RT_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_kernel<128, true>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, GCfg<128>::SMEM_BYTES));
+        RT_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_pair_kernel<true>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES));
+        RT_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_pair_kernel<false>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES));
+        RT_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_kernel<256, false>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, GCfg<256>::SMEM_BYTES));
+        RT_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_kernel<128, false>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, GCfg<128>::SMEM_BYTES));
         attr_set = true;
+        pair_clusters();   // occupancy query outside any stream capture
     }
     if (!b_is_constant(p)) return Status::ok();
-    SplitKey key{p.b, p.batches, p.N, p.K, p.trans_b ? 0 : 1};
+    SplitKey key = b_key(p);
     if (find_constant_split(key)) return Status::ok();
     SplitOperand s;
     Status r = create_constant_split(key, (size_t)p.batches * p.N * p.K, &s);
     if (!r.good()) return r;
-    return run_split(p.b, s.hi, s.lo, p.batches, p.N, p.K, !p.trans_b, st);
+    return run_split(p.b, s.hi, s.lo, p.batches, p.N, p.K, !p.trans_b, b_mode(), st);
 }
 
 Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* launches) {
@@ -475,11 +859,11 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
     float* a_hi = reinterpret_cast<float*>(ws.base);
     float* a_lo = reinterpret_cast<float*>(ws.base + abytes);
     const float *b_hi, *b_lo;
-    Status s = run_split(p.a, a_hi, a_lo, p.batches, p.M, p.K, false, st);
+    Status s = run_split(p.a, a_hi, a_lo, p.batches, p.M, p.K, false, a_mode(), st);
     if (!s.good()) return s;
     *launches += 1;
     if (b_is_constant(p)) {
-        const SplitOperand* so = find_constant_split(SplitKey{p.b, p.batches, p.N, p.K, p.trans_b ? 0 : 1});
+        const SplitOperand* so = find_constant_split(b_key(p));
         if (!so) return Status::err(RT_ERR_ARGUMENT, "gemm: constant operand not prepared");
         b_hi = so->hi;
         b_lo = so->lo;
@@ -487,7 +871,7 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
         const size_t bbytes = round256(b_split_bytes(p));
         float* bh = reinterpret_cast<float*>(ws.base + 2 * abytes);
         float* bl = reinterpret_cast<float*>(ws.base + 2 * abytes + bbytes);
-        s = run_split(p.b, bh, bl, p.batches, p.N, p.K, !p.trans_b, st);
+        s = run_split(p.b, bh, bl, p.batches, p.N, p.K, !p.trans_b, b_mode(), st);
         if (!s.good()) return s;
         *launches += 1;
         b_hi = bh;
@@ -505,8 +889,11 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
         return e ? atoi(e) : 0;
     }();
     const int BN = bn_force == 128 ? 128 : 256;
-    if (!(s = make_tmap(&prm.tb_hi, b_hi, p.K, p.N, p.batches, BN)).good()) return s;
-    if (!(s = make_tmap(&prm.tb_lo, b_lo, p.K, p.N, p.batches, BN)).good()) return s;
+    // CTA pairs (256x256 tiles) whenever A has more than one 128-row block.
+    const bool pair = BN == 256 && p.M > BM && pair_enabled();
+    const int b_box = pair ? 128 : BN;
+    if (!(s = make_tmap(&prm.tb_hi, b_hi, p.K, p.N, p.batches, b_box)).good()) return s;
+    if (!(s = make_tmap(&prm.tb_lo, b_lo, p.K, p.N, p.batches, b_box)).good()) return s;
     prm.c = p.c;
     prm.bias = p.bias;
     prm.alpha = p.alpha;
@@ -514,7 +901,8 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
     prm.N = (int)p.N;
     prm.K = (int)p.K;
     prm.batches = (int)p.batches;
-    prm.m_tiles = (int)((p.M + BM - 1) / BM);
+    const int tile_m = pair ? 2 * BM : BM;
+    prm.m_tiles = (int)((p.M + tile_m - 1) / tile_m);
     prm.n_tiles = (int)((p.N + BN - 1) / BN);
     prm.k_blocks = (int)((p.K + BK - 1) / BK);
     prm.kb_per_chunk = k_chunk() / BK;
@@ -522,21 +910,32 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
     int64_t total = (int64_t)prm.m_tiles * prm.n_tiles * p.batches;
     if (total > INT32_MAX / 2) return Status::err(RT_ERR_UNSUPPORTED, "gemm: too many tiles");
     prm.total_tiles = (int)total;
+    // persistent workers: CTAs, or CTA pairs
+    const int workers = pair ? pair_clusters() : g_num_sms;
     // Split K in two when the tiles alone fill well under 1.5 waves of the
     // persistent grid (two addends keep the fp32 sum order-independent).
     prm.splits = 1;
-    if (total < (int64_t)g_num_sms * 3 / 2 && prm.n_chunks >= 2 && split_k_enabled()) {
+    if (total < (int64_t)workers * 3 / 2 && prm.n_chunks >= 2 && split_k_enabled()) {
         prm.splits = 2;
         RT_CUDA_CHECK(cudaMemsetAsync(p.c, 0, (size_t)p.batches * p.M * p.N * 4, st));
     }
     prm.kb_split = ((prm.n_chunks + prm.splits - 1) / prm.splits) * prm.kb_per_chunk;
     prm.total_items = prm.total_tiles * prm.splits;
     prm.err = kernel_error_flag();
-    int grid = prm.total_items < g_num_sms ? prm.total_items : g_num_sms;
-    if (BN == 128)
-        tc_gemm_kernel<128><<<grid, THREADS, GCfg<128>::SMEM_BYTES, st>>>(prm);
+    const int grid = prm.total_items < workers ? prm.total_items : workers;
+    const bool cross = cross_scheme();
+    if (pair && cross)
+        tc_gemm_pair_kernel<true><<<2 * grid, THREADS, P_SMEM_BYTES, st>>>(prm);
+    else if (pair)
+        tc_gemm_pair_kernel<false><<<2 * grid, THREADS, P_SMEM_BYTES, st>>>(prm);
+    else if (BN == 128 && cross)
+        tc_gemm_kernel<128, true><<<grid, THREADS, GCfg<128>::SMEM_BYTES, st>>>(prm);
+    else if (BN == 128)
+        tc_gemm_kernel<128, false><<<grid, THREADS, GCfg<128>::SMEM_BYTES, st>>>(prm);
+    else if (cross)
+        tc_gemm_kernel<256, true><<<grid, THREADS, GCfg<256>::SMEM_BYTES, st>>>(prm);
     else
-        tc_gemm_kernel<256><<<grid, THREADS, GCfg<256>::SMEM_BYTES, st>>>(prm);
+        tc_gemm_kernel<256, false><<<grid, THREADS, GCfg<256>::SMEM_BYTES, st>>>(prm);
     RT_LAUNCH_CHECK();
     *launches += 1;
     return Status::ok();
@@ -598,7 +997,7 @@ int noalloc_setup(int device, NoallocDevice** out) {
             cudaGetLastError();
             return RT_ERR_CUDA;
         }
-        if (cudaFuncSetAttribute(tc_gemm_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (cudaFuncSetAttribute(tc_gemm_kernel<256, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  GCfg<256>::SMEM_BYTES) !=
             cudaSuccess) {
             cudaGetLastError();
@@ -641,8 +1040,8 @@ extern "C" int rt_matmul_noalloc(const float* a, const float* b, const float* bi
     float* a_lo = a_hi + a_elems;
     float* b_hi = a_lo + a_elems;
     float* b_lo = b_hi + b_elems;
-    if (!run_split(a, a_hi, a_lo, 1, M, K, false, st).good()) return RT_ERR_CUDA;
-    if (!run_split(b, b_hi, b_lo, 1, N, K, !trans_b, st).good()) return RT_ERR_CUDA;
+    if (!run_split(a, a_hi, a_lo, 1, M, K, false, 1, st).good()) return RT_ERR_CUDA;
+    if (!run_split(b, b_hi, b_lo, 1, N, K, !trans_b, 2, st).good()) return RT_ERR_CUDA;
 
     TcParams prm;
     memset(&prm, 0, sizeof prm);
@@ -669,7 +1068,7 @@ extern "C" int rt_matmul_noalloc(const float* a, const float* b, const float* bi
     prm.err = d->error;
     if (cudaMemsetAsync(d->error, 0, sizeof(int), st) != cudaSuccess) return RT_ERR_CUDA;
     int grid = prm.total_tiles < d->sms ? prm.total_tiles : d->sms;
-    tc_gemm_kernel<256><<<grid, THREADS, GCfg<256>::SMEM_BYTES, st>>>(prm);
+    tc_gemm_kernel<256, true><<<grid, THREADS, GCfg<256>::SMEM_BYTES, st>>>(prm);
     if (cudaGetLastError() != cudaSuccess) return RT_ERR_CUDA;
     // synchronous: returns once C is written, and reports a kernel that gave up a wait
     if (cudaStreamSynchronize(st) != cudaSuccess) return RT_ERR_CUDA;
@@ -680,10 +1079,10 @@ extern "C" int rt_matmul_noalloc(const float* a, const float* b, const float* bi
 
 namespace rt {
 
-// Shared with the attention kernel: the 3xTF32 operand split and tensor maps.
+// Plain hi/lo split (3xTF32 form) and fp32 tensor maps for other kernels.
 Status split_operand(const float* x, float* hi, float* lo, int64_t batches, int64_t rows, int64_t K,
                      bool transpose, cudaStream_t st) {
-    return run_split(x, hi, lo, batches, rows, K, transpose, st);
+    return run_split(x, hi, lo, batches, rows, K, transpose, 0, st);
 }
 
 Status encode_tmap_f32_3d(CUtensorMap* m, const float* base, int64_t d0, int64_t d1, int64_t d2, int box0,
