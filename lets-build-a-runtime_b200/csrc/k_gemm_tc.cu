@@ -353,8 +353,11 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
 //     arrive on the empty / accumulator-full barriers of both CTAs;
 //   * each CTA's epilogue drains its own TMEM (its 128 rows) and releases the
 //     accumulator on the leader's barrier (one arrival per warp).
-constexpr int P_STAGES = 6;
-constexpr int P_TILE = 128 * BK * 4;                   // 8 KiB: one plane of 128 rows
+// K block of 32 fp32 = one 128-byte swizzle row: half the TMA requests per
+// byte of the 64-byte rows (the request path to L2 limits the 1-CTA kernel).
+constexpr int P_BK = 32;
+constexpr int P_STAGES = 3;
+constexpr int P_TILE = 128 * P_BK * 4;                 // 16 KiB: one plane of 128 rows
 constexpr int P_STAGE_BYTES = 4 * P_TILE;              // A hi / A plane1 / B hi / B plane1
 constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
 constexpr int P_EPI_COLS = 128;
@@ -426,7 +429,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                         ptx::mbar_expect_tx(&full[stage], 2 * P_STAGE_BYTES);
                         issued_phase[stage] = (int)phase;
                     }
-                    const int k0 = kb * BK;
+                    const int k0 = kb * P_BK;
                     ptx::tma_load_3d_pair(st, &p.ta_hi, bar, k0, arow, bz);
                     ptx::tma_load_3d_pair(st + P_TILE, &p.ta_lo, bar, k0, arow, bz);
                     ptx::tma_load_3d_pair(st + 2 * P_TILE, &p.tb_hi, bar, k0, brow, bz);
@@ -471,24 +474,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                         ptx::tc_fence_after();
                         uint8_t* st = smem + stage * P_STAGE_BYTES;
                         const uint32_t acc0 = kb > kb0 ? 1u : 0u;
+                        // K advance inside the 128-byte swizzle atom: +32 bytes per step
                         if (CROSS) {
 #pragma unroll
-                            for (int kk = 0; kk < 2; kk++)
-                                ptx::mma_tf32_pair(d_tmem, ptx::smem_desc(st + kk * 32, 512, 4),
-                                                   ptx::smem_desc(st + 2 * P_TILE + kk * 32, 512, 4), idesc,
+                            for (int kk = 0; kk < 4; kk++)
+                                ptx::mma_tf32_pair(d_tmem, ptx::smem_desc(st + kk * 32, 1024, 2),
+                                                   ptx::smem_desc(st + 2 * P_TILE + kk * 32, 1024, 2), idesc,
                                                    (acc0 | kk) ? 1u : 0u);
 #pragma unroll
-                            for (int kk = 0; kk < 2; kk++)
-                                ptx::mma_bf16_pair(d_tmem, ptx::smem_desc(st + P_TILE + kk * 32, 512, 4),
-                                                   ptx::smem_desc(st + 3 * P_TILE + kk * 32, 512, 4), idesc_x,
+                            for (int kk = 0; kk < 4; kk++)
+                                ptx::mma_bf16_pair(d_tmem, ptx::smem_desc(st + P_TILE + kk * 32, 1024, 2),
+                                                   ptx::smem_desc(st + 3 * P_TILE + kk * 32, 1024, 2), idesc_x,
                                                    1u);
                         } else {
 #pragma unroll
-                            for (int kk = 0; kk < 2; kk++) {
-                                uint64_t a_hi = ptx::smem_desc(st + kk * 32, 512, 4);
-                                uint64_t a_lo = ptx::smem_desc(st + P_TILE + kk * 32, 512, 4);
-                                uint64_t b_hi = ptx::smem_desc(st + 2 * P_TILE + kk * 32, 512, 4);
-                                uint64_t b_lo = ptx::smem_desc(st + 3 * P_TILE + kk * 32, 512, 4);
+                            for (int kk = 0; kk < 4; kk++) {
+                                uint64_t a_hi = ptx::smem_desc(st + kk * 32, 1024, 2);
+                                uint64_t a_lo = ptx::smem_desc(st + P_TILE + kk * 32, 1024, 2);
+                                uint64_t b_hi = ptx::smem_desc(st + 2 * P_TILE + kk * 32, 1024, 2);
+                                uint64_t b_lo = ptx::smem_desc(st + 3 * P_TILE + kk * 32, 1024, 2);
                                 ptx::mma_tf32_pair(d_tmem, a_hi, b_hi, idesc, (acc0 | kk) ? 1u : 0u);
                                 ptx::mma_tf32_pair(d_tmem, a_hi, b_lo, idesc, 1u);
                                 ptx::mma_tf32_pair(d_tmem, a_lo, b_hi, idesc, 1u);
@@ -716,15 +720,17 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-Status make_tmap(CUtensorMap* m, const float* base, int64_t K, int64_t rows, int64_t batches, int box_rows) {
+Status make_tmap(CUtensorMap* m, const float* base, int64_t K, int64_t rows, int64_t batches, int box_rows,
+                 int box_k = BK) {
     auto fn = encode_fn();
     if (!fn) return Status::err(RT_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
     cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)rows, (cuuint64_t)batches};
     cuuint64_t strides[2] = {(cuuint64_t)K * 4, (cuuint64_t)(rows * K * 4)};
-    cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)box_rows, 1};
+    cuuint32_t box[3] = {(cuuint32_t)box_k, (cuuint32_t)box_rows, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    box_k * 4 == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
         return Status::err(RT_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
@@ -732,12 +738,12 @@ Status make_tmap(CUtensorMap* m, const float* base, int64_t K, int64_t rows, int
 }
 
 // K accumulated per TMEM chunk (see the file comment).  RT_GEMM_KCHUNK (a
-// multiple of 16) overrides the default of 128.
+// multiple of 32) overrides the default of 128.
 int k_chunk() {
     static int v = [] {
         const char* e = getenv("RT_GEMM_KCHUNK");
         int k = e ? atoi(e) : 128;
-        if (k < BK || k % BK) k = 128;
+        if (k < 32 || k % 32) k = 128;
         return k;
     }();
     return v;
@@ -879,8 +885,6 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
     }
     TcParams prm;
     memset(&prm, 0, sizeof prm);
-    if (!(s = make_tmap(&prm.ta_hi, a_hi, p.K, p.M, p.batches, BM)).good()) return s;
-    if (!(s = make_tmap(&prm.ta_lo, a_lo, p.K, p.M, p.batches, BM)).good()) return s;
     // N tile: 256 -- measured faster than 128 at every BASELINE shape, N=768
     // included (the 128-wide tile doubles A traffic per flop); short grids are
     // filled by split-K below instead.  RT_GEMM_BN=128 selects the narrow tile.
@@ -892,8 +896,11 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
     // CTA pairs (256x256 tiles) whenever A has more than one 128-row block.
     const bool pair = BN == 256 && p.M > BM && pair_enabled();
     const int b_box = pair ? 128 : BN;
-    if (!(s = make_tmap(&prm.tb_hi, b_hi, p.K, p.N, p.batches, b_box)).good()) return s;
-    if (!(s = make_tmap(&prm.tb_lo, b_lo, p.K, p.N, p.batches, b_box)).good()) return s;
+    const int bk = pair ? P_BK : BK;
+    if (!(s = make_tmap(&prm.ta_hi, a_hi, p.K, p.M, p.batches, BM, bk)).good()) return s;
+    if (!(s = make_tmap(&prm.ta_lo, a_lo, p.K, p.M, p.batches, BM, bk)).good()) return s;
+    if (!(s = make_tmap(&prm.tb_hi, b_hi, p.K, p.N, p.batches, b_box, bk)).good()) return s;
+    if (!(s = make_tmap(&prm.tb_lo, b_lo, p.K, p.N, p.batches, b_box, bk)).good()) return s;
     prm.c = p.c;
     prm.bias = p.bias;
     prm.alpha = p.alpha;
@@ -904,8 +911,8 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
     const int tile_m = pair ? 2 * BM : BM;
     prm.m_tiles = (int)((p.M + tile_m - 1) / tile_m);
     prm.n_tiles = (int)((p.N + BN - 1) / BN);
-    prm.k_blocks = (int)((p.K + BK - 1) / BK);
-    prm.kb_per_chunk = k_chunk() / BK;
+    prm.k_blocks = (int)((p.K + bk - 1) / bk);
+    prm.kb_per_chunk = k_chunk() / bk > 0 ? k_chunk() / bk : 1;
     prm.n_chunks = (prm.k_blocks + prm.kb_per_chunk - 1) / prm.kb_per_chunk;
     int64_t total = (int64_t)prm.m_tiles * prm.n_tiles * p.batches;
     if (total > INT32_MAX / 2) return Status::err(RT_ERR_UNSUPPORTED, "gemm: too many tiles");
