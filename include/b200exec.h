@@ -142,14 +142,19 @@ void* rt_stream(void);
  * folds away a node that writes into it.  The output of the last node of an
  * array is always treated as a graph output; callers whose graphs return
  * more than that register the other outputs here before the first execute
- * (no counterpart in the reference, whose C side computes every node). */
+ * (no counterpart in the reference, whose C side computes every node).
+ * A registration lasts until rt_unprotect_all or until the rt_alloc memory
+ * holding `ptr` is released with rt_free. */
 int rt_protect(const void* ptr, size_t bytes);
 int rt_unprotect_all(void);
-/* Plan-time layout fusion, as execute would apply it to this node array:
- * flags[i] = 1 when node i (a SLICE / TRANSPOSE around attention) is folded
- * into its consumer and not launched, 2 for an attention node launched with
- * strided operands, 0 otherwise.  Returns the number of folded nodes.  Host
- * only: needs no device and no rt_init.  RT_FUSE=0 turns folding off. */
+/* Plan-time fusion, as execute would apply it to this node array:
+ * flags[i] = 1 when node i is folded into another node and not launched (a
+ * SLICE / TRANSPOSE around attention, a GELU after a GEMM), 2 for an
+ * attention node launched with strided operands, 3 for a GEMM that applies a
+ * folded activation and/or writes the split A operand of a later GEMM in its
+ * epilogue, 4 for a GEMM whose A operand arrives that way (no split pass),
+ * 0 otherwise.  Returns the number of folded nodes.  Host only: needs no
+ * device and no rt_init.  RT_FUSE=0 turns all fusion off. */
 int rt_fusion_report(const OpNode* nodes, int n_nodes, int* flags);
 
 /* ---- allocation-free GEMM ------------------------------------------------ */

@@ -16,7 +16,8 @@
 //     touches the merge's output region.
 // Every node's read and write extents are computed from its op, shape and
 // extras; a node whose read extent is not known blocks any fusion across it.
-// RT_FUSE=0 disables the pass.
+// RT_FUSE=0 disables the pass (RT_FUSE_GEMM=0 only the GEMM epilogue chains;
+// RT_FUSE_HANDOFF=1 turns on the split-operand hand-off between GEMMs).
 #include <stdio.h>
 #include <stdlib.h>
 
@@ -403,6 +404,80 @@ bool valid(const Analysis& an, const Effective& e, const Proposal& p, const std:
     return true;
 }
 
+// GEMM epilogue fusion on the schedule left by layout fusion:
+//   GEMM g -> GELU u: g applies the GELU and writes u's output; u is skipped.
+//   ... -> GEMM k reading u's output as its A operand: g writes k's split A
+//   planes (carry buffer) instead, k skips its split pass (opt-in,
+//   RT_FUSE_HANDOFF=1: the plane stores currently cost the first GEMM more
+//   than the second one saves).
+// Conditions mirror the layout folds: g's output is read by u alone and is
+// not a graph output; nothing between g and u touches u's output, which g
+// now writes earlier (and g's own operands do not overlap it); for the
+// hand-off, u's output is read by k alone, through A only.  Chains share one
+// carry buffer, so their [g, k] spans must not overlap.
+void plan_gemm_chains(const Analysis& an, const Effective& e, std::vector<PlanItem>& items,
+                      const std::vector<Range>& protect, size_t* carry_bytes) {
+    const int n = (int)an.nodes.size();
+    auto is_gemm = [](const OpNode& x) { return x.op == RT_OP_MATMUL || x.op == RT_OP_MATMUL_ADD; };
+    auto next_reader = [&](int from, Range r) {
+        for (int j = from + 1; j < n; j++) {
+            if (e.skipped[j]) continue;
+            if (eff_reads(e, j, r)) return j;
+            if (overlaps(e.writes[j], r)) return -1;
+        }
+        return -1;
+    };
+    size_t carry = 0;
+    int carry_busy_until = -1;
+    for (int g = 0; g < n; g++) {
+        const OpNode& gn = an.nodes[g];
+        if (e.skipped[g] || items[g].views || !is_gemm(gn) || !gemm_fusable(gn)) continue;
+        const Range W = an.writes[g];
+        const int u = next_reader(g, W);
+        if (u < 0) continue;
+        const OpNode& un = an.nodes[u];
+        if (un.op != RT_OP_GELU || un.inputs[0] != gn.output || un.elem_size != 4 || items[u].redirect_slot >= 0 ||
+            an.writes[u].hi - an.writes[u].lo != W.hi - W.lo)
+            continue;
+        if (!dead_output(an, g, u, protect)) continue;
+        const Range U = an.writes[u];
+        bool ok = true;
+        for (int j = g + 1; j < u && ok; j++)
+            if (!e.skipped[j] && (overlaps(e.writes[j], U) || eff_reads(e, j, U))) ok = false;
+        for (const Range& r : e.reads[g])
+            if (overlaps(r, U)) ok = false;
+        if (!ok) continue;
+        items[u].skip = true;
+        items[g].epi_act = 1;
+        items[g].epi_out = un.output;
+        if (dbg()) fprintf(stderr, "[fusion] gemm %d: GELU %d folded into the epilogue\n", g, u);
+
+        const char* hv = getenv("RT_FUSE_HANDOFF");   // read per plan
+        if (!(hv && hv[0] == '1')) continue;
+        const int k = next_reader(u, U);
+        if (k < 0 || g <= carry_busy_until) continue;
+        const OpNode& kn = an.nodes[k];
+        if (!is_gemm(kn) || kn.inputs[0] != un.output || items[k].redirect_slot >= 0 || !gemm_fusable(kn)) continue;
+        GemmProblem gp, kp;
+        if (!decode_gemm(gn, &gp).good() || !decode_gemm(kn, &kp).good()) continue;
+        if ((uintptr_t)(kp.batches * kp.M * kp.K * 4) != U.hi - U.lo || kp.K != gp.N || kp.K % 4 != 0 ||
+            kp.batches * kp.M != gp.batches * gp.M)
+            continue;
+        bool only_a = true;
+        for (size_t i = 1; i < e.reads[k].size(); i++) only_a &= !overlaps(e.reads[k][i], U);
+        if (!only_a || !dead_output(an, u, k, protect)) continue;
+        const int64_t plane = (int64_t)(((U.hi - U.lo) + 255) & ~(uintptr_t)255);
+        items[g].carry_off = 0;
+        items[g].carry_plane_bytes = plane;
+        items[k].presplit_off = 0;
+        items[k].carry_plane_bytes = plane;
+        if ((size_t)(2 * plane) > carry) carry = (size_t)(2 * plane);
+        carry_busy_until = k;
+        if (dbg()) fprintf(stderr, "[fusion] gemm %d: writes the split A operand of gemm %d\n", g, k);
+    }
+    if (carry_bytes) *carry_bytes = carry;
+}
+
 bool fusion_enabled() {
     static const bool on = [] {
         const char* e = getenv("RT_FUSE");
@@ -414,8 +489,10 @@ bool fusion_enabled() {
 }  // namespace
 
 std::vector<PlanItem> plan_fusions(const std::vector<OpNode>& nodes,
-                                   const std::vector<std::pair<uintptr_t, size_t>>& protected_ranges) {
+                                   const std::vector<std::pair<uintptr_t, size_t>>& protected_ranges,
+                                   size_t* carry_bytes) {
     std::vector<PlanItem> items(nodes.size());
+    if (carry_bytes) *carry_bytes = 0;
     Analysis an(nodes);
     std::vector<Range> protect;
     for (auto& pr : protected_ranges) protect.push_back(Range{pr.first, pr.first + pr.second});
@@ -474,6 +551,11 @@ std::vector<PlanItem> plan_fusions(const std::vector<OpNode>& nodes,
                     items[rd.first].redirect_ptr = an.nodes[p.a].output;
                 }
             }
+            static const bool gemm_chains = [] {
+                const char* v = getenv("RT_FUSE_GEMM");
+                return !(v && v[0] == '0');
+            }();
+            if (fusion_enabled() && gemm_chains) plan_gemm_chains(an, e, items, protect, carry_bytes);
             break;
         }
         pick[owner[bad]]++;

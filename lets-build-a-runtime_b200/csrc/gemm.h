@@ -24,7 +24,8 @@ Status launch_simt_gemm(const GemmProblem& p, cudaStream_t st);
 bool tc_gemm_applicable(const GemmProblem& p);
 size_t tc_gemm_workspace_bytes(const GemmProblem& p);
 Status tc_gemm_prepare(const GemmProblem& p, cudaStream_t st);
-Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* launches);
+Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* launches,
+                      const GemmFusion* f = nullptr);
 
 }  // namespace rt
 

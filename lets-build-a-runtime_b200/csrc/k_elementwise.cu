@@ -18,14 +18,13 @@
 // using CUDA's IEEE-accurate library functions (no fast-math intrinsics).
 #include "rt_internal.h"
 
+#include "dev_math.h"
+
 namespace rt {
 namespace {
 
 enum UnaryKind { U_RELU, U_EXP, U_TANH, U_POW, U_GELU, U_RSQRT, U_SILU, U_NEG, U_COS, U_SIN };
 
-__device__ __forceinline__ float gelu_tanh(float x) {
-    return 0.5f * x * (1.0f + tanhf(0.7978845608f * (x + 0.044715f * x * x * x)));
-}
 __device__ __forceinline__ float silu(float v) { return v / (1.0f + expf(-v)); }
 
 template <int K>

@@ -162,11 +162,17 @@ Status prepare_gemm(const OpNode& n, cudaStream_t st) {
     return tc_gemm_prepare(p, st);
 }
 
-Status launch_gemm(const OpNode& n, cudaStream_t st, Workspace ws, int* launches) {
+bool gemm_fusable(const OpNode& n) {
+    GemmProblem p;
+    return decode_gemm(n, &p).good() && tc_gemm_applicable(p);
+}
+
+Status launch_gemm(const OpNode& n, cudaStream_t st, Workspace ws, int* launches, const GemmFusion* f) {
     GemmProblem p;
     Status s = decode_gemm(n, &p);
     if (!s.good()) return s;
-    if (tc_gemm_applicable(p)) return tc_gemm_launch(p, st, ws, launches);
+    if (tc_gemm_applicable(p)) return tc_gemm_launch(p, st, ws, launches, f);
+    if (f) return Status::err(RT_ERR_ARGUMENT, "gemm: fused epilogue needs the tensor-core path");
     *launches += 1;
     return launch_simt_gemm(p, st);
 }

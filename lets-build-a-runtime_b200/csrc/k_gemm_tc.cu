@@ -56,6 +56,7 @@
 
 #include <mutex>
 
+#include "dev_math.h"
 #include "gemm.h"
 #include "sm100_ptx.h"
 
@@ -94,8 +95,99 @@ struct TcParams {
     int kb_per_chunk, n_chunks;   // K accumulated in TMEM in chunks of kb_per_chunk blocks
     int splits, kb_split;         // split-K: work item = (tile, split); split s covers K blocks [s*kb_split, ...)
     int total_items;              // total_tiles * splits
+    int act;                      // 1: tanh-GELU after alpha and bias
+    float* plane_hi;              // non-null: write the result as split A planes (hi, plane 1) of a
+    uint8_t* plane_x;             //   later GEMM instead of C (row-major [batches*M][N])
+    int plane_mode;               //   plane 1: 0 = lo (fp32), 1 = cross (bf16 [hi | lo] per 16 block)
     int* err;
 };
+
+__device__ __forceinline__ float tf32_hi(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+__device__ __forceinline__ uint16_t bf16_bits(float x) {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(x));
+}
+
+// One epilogue row: COLS consecutive columns from col0 of output row `row`
+// (within batch bz): alpha, bias (first split only), optional GELU, then C
+// (plain store, or float4 atomics under split-K) or, for PLANES kernels, the
+// split A planes (a separate instantiation: the plane code's registers would
+// otherwise cost every GEMM's epilogue).
+template <int COLS, bool PLANES>
+__device__ __forceinline__ void store_row(const TcParams& p, int64_t row, int bz, int col0, const float* acc,
+                                          bool first_split) {
+    const bool add_bias = p.bias && first_split;
+    const int64_t r = (int64_t)bz * p.M + row;
+    if (PLANES) {
+        // N % 4 == 0 here (it is the K of the consuming GEMM); splits == 1
+        float* hrow = p.plane_hi + r * p.N;
+        uint16_t* xrow = reinterpret_cast<uint16_t*>(p.plane_x + r * p.N * 4);
+#pragma unroll
+        for (int j = 0; j < COLS; j += 4) {
+            const int col = col0 + j;
+            if (col >= p.N) break;
+            float h[4], l[4];
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                float v = p.alpha * acc[j + e];
+                if (add_bias) v += p.bias[col + e];
+                if (p.act == 1) v = gelu_tanh(v);
+                h[e] = tf32_hi(v);
+                l[e] = v - h[e];
+            }
+            *reinterpret_cast<float4*>(hrow + col) = make_float4(h[0], h[1], h[2], h[3]);
+            if (p.plane_mode == 1) {
+                // cross: bf16 [hi(0..w-1) | lo(0..w-1)] per 16-column block of width w
+                const int kb = col >> 4, jj = col & 15, w = min(16, p.N - kb * 16);
+                uint16_t* blk = xrow + kb * 32;
+                uint2 f, g;
+                f.x = (uint32_t)bf16_bits(h[0]) | ((uint32_t)bf16_bits(h[1]) << 16);
+                f.y = (uint32_t)bf16_bits(h[2]) | ((uint32_t)bf16_bits(h[3]) << 16);
+                g.x = (uint32_t)bf16_bits(l[0]) | ((uint32_t)bf16_bits(l[1]) << 16);
+                g.y = (uint32_t)bf16_bits(l[2]) | ((uint32_t)bf16_bits(l[3]) << 16);
+                *reinterpret_cast<uint2*>(blk + jj) = f;
+                *reinterpret_cast<uint2*>(blk + w + jj) = g;
+            } else {
+                *reinterpret_cast<float4*>(reinterpret_cast<float*>(xrow) + col) =
+                    make_float4(l[0], l[1], l[2], l[3]);
+            }
+        }
+        return;
+    }
+    float* crow = p.c + r * p.N;
+    if ((p.N & 3) == 0 && col0 + COLS <= p.N) {
+#pragma unroll
+        for (int j = 0; j < COLS; j += 4) {
+            float4 v = make_float4(p.alpha * acc[j], p.alpha * acc[j + 1], p.alpha * acc[j + 2],
+                                   p.alpha * acc[j + 3]);
+            if (add_bias) {
+                float4 bb = *reinterpret_cast<const float4*>(p.bias + col0 + j);
+                v.x += bb.x; v.y += bb.y; v.z += bb.z; v.w += bb.w;
+            }
+            if (p.act == 1) {
+                v.x = gelu_tanh(v.x); v.y = gelu_tanh(v.y); v.z = gelu_tanh(v.z); v.w = gelu_tanh(v.w);
+            }
+            // two splits add into a zeroed C: 0+x+y == 0+y+x, so the
+            // result does not depend on which split lands first
+            if (p.splits > 1) atomicAdd(reinterpret_cast<float4*>(crow + col0 + j), v);
+            else *reinterpret_cast<float4*>(crow + col0 + j) = v;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < COLS; j++) {
+            if (col0 + j < p.N) {
+                float v = p.alpha * acc[j];
+                if (add_bias) v += p.bias[col0 + j];
+                if (p.act == 1) v = gelu_tanh(v);
+                if (p.splits > 1) atomicAdd(crow + col0 + j, v);
+                else crow[col0 + j] = v;
+            }
+        }
+    }
+}
 
 __device__ __forceinline__ void tile_coords(const TcParams& p, int item, int& m_blk, int& n_blk, int& bz,
                                             int& kb_lo, int& kb_hi) {
@@ -108,7 +200,7 @@ __device__ __forceinline__ void tile_coords(const TcParams& p, int item, int& m_
     kb_hi = min(p.k_blocks, kb_lo + p.kb_split);
 }
 
-template <int BN_, bool CROSS>
+template <int BN_, bool CROSS, bool PLANES>
 __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
     constexpr int BN = GCfg<BN_>::BN, STAGES = GCfg<BN_>::STAGES, EPI_COLS = GCfg<BN_>::EPI_COLS;
     constexpr int B_TILE = GCfg<BN_>::B_TILE, STAGE_BYTES = GCfg<BN_>::STAGE_BYTES;
@@ -259,7 +351,6 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
         // Thread = one tile row (TMEM lane) x BN/2 columns.
         const int quarter = warp & 3;
         const int half = (warp - 2) >> 2;
-        const int row_in_tile = quarter * 32 + lane;
         int it = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < p.total_items && ok; t += gridDim.x) {
@@ -271,8 +362,10 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
             for (int c = 0; c < n_chunks; c++, it++) {
                 int b = it & 1;
                 uint32_t acc_phase = (it >> 1) & 1;
-                if (!ptx::wait_bounded(&acc_full[b], acc_phase, abort_flag, p.err, ERR_EPILOGUE,
-                                       WAIT_LIMIT_NS)) {
+                // warp-uniform outcome: the stores below are warp-collective
+                const bool got = ptx::wait_bounded(&acc_full[b], acc_phase, abort_flag, p.err, ERR_EPILOGUE,
+                                                   WAIT_LIMIT_NS);
+                if (!__all_sync(0xffffffffu, got)) {
                     ok = false;
                     break;
                 }
@@ -293,36 +386,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
                 ptx::mbar_arrive(&acc_empty[b]);
             }
             if (!ok) break;
-            int64_t row = (int64_t)m_blk * BM + row_in_tile;
-            if (row >= p.M) continue;
-            float* crow = p.c + ((int64_t)bz * p.M + row) * p.N;
-            const int col0 = n_blk * BN + half * EPI_COLS;
-            const bool add_bias = p.bias && first_split;
-            if ((p.N & 3) == 0 && col0 + EPI_COLS <= p.N) {
-#pragma unroll
-                for (int j = 0; j < EPI_COLS; j += 4) {
-                    float4 v = make_float4(p.alpha * acc[j], p.alpha * acc[j + 1], p.alpha * acc[j + 2],
-                                           p.alpha * acc[j + 3]);
-                    if (add_bias) {
-                        float4 bb = *reinterpret_cast<const float4*>(p.bias + col0 + j);
-                        v.x += bb.x; v.y += bb.y; v.z += bb.z; v.w += bb.w;
-                    }
-                    // two splits add into a zeroed C: 0+x+y == 0+y+x, so the
-                    // result does not depend on which split lands first
-                    if (p.splits > 1) atomicAdd(reinterpret_cast<float4*>(crow + col0 + j), v);
-                    else *reinterpret_cast<float4*>(crow + col0 + j) = v;
-                }
-            } else {
-#pragma unroll
-                for (int j = 0; j < EPI_COLS; j++) {
-                    if (col0 + j < p.N) {
-                        float v = p.alpha * acc[j];
-                        if (add_bias) v += p.bias[col0 + j];
-                        if (p.splits > 1) atomicAdd(crow + col0 + j, v);
-                        else crow[col0 + j] = v;
-                    }
-                }
-            }
+            const int64_t row = (int64_t)m_blk * BM + quarter * 32 + lane;
+            if (row < p.M) store_row<EPI_COLS, PLANES>(p, row, bz, n_blk * BN + half * EPI_COLS, acc, first_split);
         }
     }
 
@@ -360,9 +425,10 @@ constexpr int P_STAGES = 3;
 constexpr int P_TILE = 128 * P_BK * 4;                 // 16 KiB: one plane of 128 rows
 constexpr int P_STAGE_BYTES = 4 * P_TILE;              // A hi / A plane1 / B hi / B plane1
 constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
+static_assert(P_SMEM_BYTES <= 232448, "shared memory budget");
 constexpr int P_EPI_COLS = 128;
 
-template <bool CROSS>
+template <bool CROSS, bool PLANES>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     tc_gemm_pair_kernel(const __grid_constant__ TcParams p) {
     extern __shared__ uint8_t smem_raw[];
@@ -517,7 +583,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         // ------------------------------------------------ epilogue (warps 2..9, both CTAs)
         const int quarter = warp & 3;
         const int half = (warp - 2) >> 2;
-        const int row_in_tile = quarter * 32 + lane;
         const uint32_t acc_empty_leader0 = ptx::mapa_shared(ptx::smem_u32(&acc_empty[0]), 0);
         int it = 0;
         bool ok = true;
@@ -530,8 +595,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             for (int c = 0; c < n_chunks; c++, it++) {
                 const int b = it & 1;
                 const uint32_t acc_phase = (it >> 1) & 1;
-                if (!ptx::wait_bounded(&acc_full[b], acc_phase, abort_flag, p.err, ERR_EPILOGUE,
-                                       WAIT_LIMIT_NS)) {
+                // warp-uniform outcome: the stores below are warp-collective
+                const bool got = ptx::wait_bounded(&acc_full[b], acc_phase, abort_flag, p.err, ERR_EPILOGUE,
+                                                   WAIT_LIMIT_NS);
+                if (!__all_sync(0xffffffffu, got)) {
                     ok = false;
                     break;
                 }
@@ -553,34 +620,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                 if (lane == 0) ptx::mbar_arrive_cluster(acc_empty_leader0 + b * 8);
             }
             if (!ok) break;
-            const int64_t row = (int64_t)m_blk * 256 + rank * 128 + row_in_tile;
-            if (row >= p.M) continue;
-            float* crow = p.c + ((int64_t)bz * p.M + row) * p.N;
-            const int col0 = n_blk * 256 + half * P_EPI_COLS;
-            const bool add_bias = p.bias && first_split;
-            if ((p.N & 3) == 0 && col0 + P_EPI_COLS <= p.N) {
-#pragma unroll
-                for (int j = 0; j < P_EPI_COLS; j += 4) {
-                    float4 v = make_float4(p.alpha * acc[j], p.alpha * acc[j + 1], p.alpha * acc[j + 2],
-                                           p.alpha * acc[j + 3]);
-                    if (add_bias) {
-                        float4 bb = *reinterpret_cast<const float4*>(p.bias + col0 + j);
-                        v.x += bb.x; v.y += bb.y; v.z += bb.z; v.w += bb.w;
-                    }
-                    if (p.splits > 1) atomicAdd(reinterpret_cast<float4*>(crow + col0 + j), v);
-                    else *reinterpret_cast<float4*>(crow + col0 + j) = v;
-                }
-            } else {
-#pragma unroll
-                for (int j = 0; j < P_EPI_COLS; j++) {
-                    if (col0 + j < p.N) {
-                        float v = p.alpha * acc[j];
-                        if (add_bias) v += p.bias[col0 + j];
-                        if (p.splits > 1) atomicAdd(crow + col0 + j, v);
-                        else crow[col0 + j] = v;
-                    }
-                }
-            }
+            const int64_t row = (int64_t)m_blk * 256 + rank * 128 + quarter * 32 + lane;
+            if (row < p.M) store_row<P_EPI_COLS, PLANES>(p, row, bz, n_blk * 256 + half * P_EPI_COLS, acc, first_split);
         }
     }
 
@@ -599,15 +640,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 }
 
 // ---- operand split: hi = tf32(x) (round to nearest), lo = x - hi ----------
-__device__ __forceinline__ float tf32_hi(float x) {
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-    return __uint_as_float(r);
-}
-
-__device__ __forceinline__ uint16_t bf16_bits(float x) {
-    return __bfloat16_as_ushort(__float2bfloat16_rn(x));
-}
 
 // Plane-1 writer for element k of a row whose plane-1 row starts at `row1`
 // (2K bf16 slots).  mode 0: lo as fp32; mode 1 (A): cross [hi | lo];
@@ -772,6 +804,42 @@ SplitKey b_key(const GemmProblem& p) {
     return SplitKey{p.b, p.batches, p.N, p.K, (p.trans_b ? 0 : 1) | (cross_scheme() ? 2 : 0)};
 }
 
+// Every kernel instantiation with its dynamic shared memory size.
+template <class F>
+cudaError_t for_each_kernel(F f) {
+    const void* ks[] = {
+        (const void*)tc_gemm_pair_kernel<true, false>, (const void*)tc_gemm_pair_kernel<false, false>,
+        (const void*)tc_gemm_pair_kernel<true, true>,  (const void*)tc_gemm_pair_kernel<false, true>,
+        (const void*)tc_gemm_kernel<256, true, false>, (const void*)tc_gemm_kernel<256, false, false>,
+        (const void*)tc_gemm_kernel<256, true, true>,  (const void*)tc_gemm_kernel<256, false, true>,
+        (const void*)tc_gemm_kernel<128, true, false>, (const void*)tc_gemm_kernel<128, false, false>,
+        (const void*)tc_gemm_kernel<128, true, true>,  (const void*)tc_gemm_kernel<128, false, true>};
+    const int smem[] = {P_SMEM_BYTES, P_SMEM_BYTES, P_SMEM_BYTES, P_SMEM_BYTES,
+                        GCfg<256>::SMEM_BYTES, GCfg<256>::SMEM_BYTES, GCfg<256>::SMEM_BYTES, GCfg<256>::SMEM_BYTES,
+                        GCfg<128>::SMEM_BYTES, GCfg<128>::SMEM_BYTES, GCfg<128>::SMEM_BYTES, GCfg<128>::SMEM_BYTES};
+    for (int i = 0; i < 12; i++) {
+        cudaError_t e = f(ks[i], smem[i]);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+template <bool CROSS, bool PLANES>
+void launch_tc_t(bool pair, int BN, int grid, const TcParams& prm, cudaStream_t st) {
+    if (pair)
+        tc_gemm_pair_kernel<CROSS, PLANES><<<2 * grid, THREADS, P_SMEM_BYTES, st>>>(prm);
+    else if (BN == 128)
+        tc_gemm_kernel<128, CROSS, PLANES><<<grid, THREADS, GCfg<128>::SMEM_BYTES, st>>>(prm);
+    else
+        tc_gemm_kernel<256, CROSS, PLANES><<<grid, THREADS, GCfg<256>::SMEM_BYTES, st>>>(prm);
+}
+void launch_tc(bool pair, int BN, bool cross, bool planes, int grid, const TcParams& prm, cudaStream_t st) {
+    if (cross && planes) launch_tc_t<true, true>(pair, BN, grid, prm, st);
+    else if (cross) launch_tc_t<true, false>(pair, BN, grid, prm, st);
+    else if (planes) launch_tc_t<false, true>(pair, BN, grid, prm, st);
+    else launch_tc_t<false, false>(pair, BN, grid, prm, st);
+}
+
 // RT_GEMM_PAIR=0 keeps every GEMM on the one-CTA kernel.
 bool pair_enabled() {
     static const bool on = [] {
@@ -797,7 +865,7 @@ int pair_clusters() {
         cfg.attrs = &attr;
         cfg.numAttrs = 1;
         int c = 0;
-        if (cudaOccupancyMaxActiveClusters(&c, tc_gemm_pair_kernel<true>, &cfg) != cudaSuccess || c <= 0) {
+        if (cudaOccupancyMaxActiveClusters(&c, tc_gemm_pair_kernel<true, false>, &cfg) != cudaSuccess || c <= 0) {
             cudaGetLastError();
             c = g_num_sms / 2;
         }
@@ -834,18 +902,9 @@ Status tc_gemm_prepare(const GemmProblem& p, cudaStream_t st) {
     if (!tc_gemm_applicable(p)) return Status::ok();
     static bool attr_set = false;
     if (!attr_set) {
-        RT_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_kernel<256, true>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, GCfg<256>::SMEM_BYTES));
-        RT_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_kernel<128, true>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, GCfg<128>::SMEM_BYTES));
-        RT_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_pair_kernel<true>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES));
-        RT_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_pair_kernel<false>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES));
-        RT_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_kernel<256, false>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, GCfg<256>::SMEM_BYTES));
-        RT_CUDA_CHECK(cudaFuncSetAttribute(tc_gemm_kernel<128, false>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, GCfg<128>::SMEM_BYTES));
+        RT_CUDA_CHECK(for_each_kernel([](const void* k, int smem) {
+            return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        }));
         attr_set = true;
         pair_clusters();   // occupancy query outside any stream capture
     }
@@ -858,16 +917,27 @@ Status tc_gemm_prepare(const GemmProblem& p, cudaStream_t st) {
     return run_split(p.b, s.hi, s.lo, p.batches, p.N, p.K, !p.trans_b, b_mode(), st);
 }
 
-Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* launches) {
+Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* launches,
+                      const GemmFusion* f) {
     if (p.M == 0) return Status::ok();
     if (ws.bytes < tc_gemm_workspace_bytes(p)) return Status::err(RT_ERR_ARGUMENT, "gemm: workspace too small");
+    if (f && f->plane_hi && p.N % 4 != 0) return Status::err(RT_ERR_ARGUMENT, "gemm: split-plane output needs N % 4 == 0");
     const size_t abytes = round256(a_split_bytes(p));
-    float* a_hi = reinterpret_cast<float*>(ws.base);
-    float* a_lo = reinterpret_cast<float*>(ws.base + abytes);
+    const float *a_hi, *a_lo;
     const float *b_hi, *b_lo;
-    Status s = run_split(p.a, a_hi, a_lo, p.batches, p.M, p.K, false, a_mode(), st);
-    if (!s.good()) return s;
-    *launches += 1;
+    Status s;
+    if (f && f->pre_hi) {   // A split by the producing GEMM's epilogue
+        a_hi = f->pre_hi;
+        a_lo = static_cast<const float*>(f->pre_x);
+    } else {
+        float* ah = reinterpret_cast<float*>(ws.base);
+        float* al = reinterpret_cast<float*>(ws.base + abytes);
+        s = run_split(p.a, ah, al, p.batches, p.M, p.K, false, a_mode(), st);
+        if (!s.good()) return s;
+        *launches += 1;
+        a_hi = ah;
+        a_lo = al;
+    }
     if (b_is_constant(p)) {
         const SplitOperand* so = find_constant_split(b_key(p));
         if (!so) return Status::err(RT_ERR_ARGUMENT, "gemm: constant operand not prepared");
@@ -901,9 +971,13 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
     if (!(s = make_tmap(&prm.ta_lo, a_lo, p.K, p.M, p.batches, BM, bk)).good()) return s;
     if (!(s = make_tmap(&prm.tb_hi, b_hi, p.K, p.N, p.batches, b_box, bk)).good()) return s;
     if (!(s = make_tmap(&prm.tb_lo, b_lo, p.K, p.N, p.batches, b_box, bk)).good()) return s;
-    prm.c = p.c;
+    prm.c = f && f->out ? f->out : p.c;
     prm.bias = p.bias;
     prm.alpha = p.alpha;
+    prm.act = f ? f->act : 0;
+    prm.plane_hi = f ? f->plane_hi : nullptr;
+    prm.plane_x = f ? static_cast<uint8_t*>(f->plane_x) : nullptr;
+    prm.plane_mode = a_mode();
     prm.M = (int)p.M;
     prm.N = (int)p.N;
     prm.K = (int)p.K;
@@ -921,28 +995,18 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
     const int workers = pair ? pair_clusters() : g_num_sms;
     // Split K in two when the tiles alone fill well under 1.5 waves of the
     // persistent grid (two addends keep the fp32 sum order-independent).
+    // (Not with a fused activation or split-plane output: both need the full sum.)
     prm.splits = 1;
-    if (total < (int64_t)workers * 3 / 2 && prm.n_chunks >= 2 && split_k_enabled()) {
+    const bool whole_sum = prm.act != 0 || prm.plane_hi != nullptr;
+    if (total < (int64_t)workers * 3 / 2 && prm.n_chunks >= 2 && split_k_enabled() && !whole_sum) {
         prm.splits = 2;
-        RT_CUDA_CHECK(cudaMemsetAsync(p.c, 0, (size_t)p.batches * p.M * p.N * 4, st));
+        RT_CUDA_CHECK(cudaMemsetAsync(prm.c, 0, (size_t)p.batches * p.M * p.N * 4, st));
     }
     prm.kb_split = ((prm.n_chunks + prm.splits - 1) / prm.splits) * prm.kb_per_chunk;
     prm.total_items = prm.total_tiles * prm.splits;
     prm.err = kernel_error_flag();
     const int grid = prm.total_items < workers ? prm.total_items : workers;
-    const bool cross = cross_scheme();
-    if (pair && cross)
-        tc_gemm_pair_kernel<true><<<2 * grid, THREADS, P_SMEM_BYTES, st>>>(prm);
-    else if (pair)
-        tc_gemm_pair_kernel<false><<<2 * grid, THREADS, P_SMEM_BYTES, st>>>(prm);
-    else if (BN == 128 && cross)
-        tc_gemm_kernel<128, true><<<grid, THREADS, GCfg<128>::SMEM_BYTES, st>>>(prm);
-    else if (BN == 128)
-        tc_gemm_kernel<128, false><<<grid, THREADS, GCfg<128>::SMEM_BYTES, st>>>(prm);
-    else if (cross)
-        tc_gemm_kernel<256, true><<<grid, THREADS, GCfg<256>::SMEM_BYTES, st>>>(prm);
-    else
-        tc_gemm_kernel<256, false><<<grid, THREADS, GCfg<256>::SMEM_BYTES, st>>>(prm);
+    launch_tc(pair, BN, cross_scheme(), prm.plane_hi != nullptr, grid, prm, st);
     RT_LAUNCH_CHECK();
     *launches += 1;
     return Status::ok();
@@ -1004,7 +1068,7 @@ int noalloc_setup(int device, NoallocDevice** out) {
             cudaGetLastError();
             return RT_ERR_CUDA;
         }
-        if (cudaFuncSetAttribute(tc_gemm_kernel<256, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (cudaFuncSetAttribute(tc_gemm_kernel<256, true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  GCfg<256>::SMEM_BYTES) !=
             cudaSuccess) {
             cudaGetLastError();
@@ -1075,7 +1139,7 @@ extern "C" int rt_matmul_noalloc(const float* a, const float* b, const float* bi
     prm.err = d->error;
     if (cudaMemsetAsync(d->error, 0, sizeof(int), st) != cudaSuccess) return RT_ERR_CUDA;
     int grid = prm.total_tiles < d->sms ? prm.total_tiles : d->sms;
-    tc_gemm_kernel<256, true><<<grid, THREADS, GCfg<256>::SMEM_BYTES, st>>>(prm);
+    tc_gemm_kernel<256, true, false><<<grid, THREADS, GCfg<256>::SMEM_BYTES, st>>>(prm);
     if (cudaGetLastError() != cudaSuccess) return RT_ERR_CUDA;
     // synchronous: returns once C is written, and reports a kernel that gave up a wait
     if (cudaStreamSynchronize(st) != cudaSuccess) return RT_ERR_CUDA;

@@ -77,7 +77,19 @@ bool is_constant_range(const void* p, size_t bytes);
 // ---- kernel families: each returns a Status; `ws` is the node's scratch.
 // Planning hooks report scratch bytes a node needs beyond its arena buffers.
 size_t gemm_workspace_bytes(const OpNode& n);
-Status launch_gemm(const OpNode& n, cudaStream_t st, Workspace ws, int* launches);
+// Epilogue / prologue fusion of one GEMM launch (from a PlanItem).
+struct GemmFusion {
+    int act = 0;                    // 1: tanh-GELU after alpha and bias
+    float* out = nullptr;           // write C here instead of the node's output
+    float* plane_hi = nullptr;      // write the result as split A planes of a later GEMM
+    void* plane_x = nullptr;
+    const float* pre_hi = nullptr;  // this GEMM's A, already split
+    const void* pre_x = nullptr;
+};
+Status launch_gemm(const OpNode& n, cudaStream_t st, Workspace ws, int* launches,
+                   const GemmFusion* f = nullptr);
+// Whether a GEMM node can take a GemmFusion (tensor-core path).
+bool gemm_fusable(const OpNode& n);
 Status prepare_gemm(const OpNode& n, cudaStream_t st);   // constant splits, before capture
 
 Status launch_attention(const OpNode& n, cudaStream_t st, Workspace ws, int* launches);
@@ -104,9 +116,20 @@ struct PlanItem {
     AttnViews attn{};
     int redirect_slot = -1;        // input slot now reading `redirect_ptr` (a folded producer's source)
     void* redirect_ptr = nullptr;
+    // GEMM epilogue fusion: a GEMM that applies the folded activation node's
+    // op and writes its output (`epi_out`), or -- when that output only feeds
+    // the A operand of a later GEMM -- writes the split A planes of that GEMM
+    // into the plan's carry buffer at `carry_off` (hi, then plane 1).
+    int epi_act = 0;               // 0 none, 1 tanh-GELU
+    void* epi_out = nullptr;
+    int64_t carry_off = -1;        // producer: write A planes here (byte offset into the carry buffer)
+    int64_t presplit_off = -1;     // consumer: A planes are already here; no split pre-pass
+    int64_t carry_plane_bytes = 0; // bytes of one plane
 };
+// `carry_bytes` receives the carry buffer size the items need (0 if none).
 std::vector<PlanItem> plan_fusions(const std::vector<OpNode>& nodes,
-                                   const std::vector<std::pair<uintptr_t, size_t>>& protected_ranges);
+                                   const std::vector<std::pair<uintptr_t, size_t>>& protected_ranges,
+                                   size_t* carry_bytes = nullptr);
 size_t attention_workspace_bytes(const OpNode& n);
 Status prepare_attention(const OpNode& n);
 Status launch_elementwise(const OpNode& n, cudaStream_t st, int* launches);

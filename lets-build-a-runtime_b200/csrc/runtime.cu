@@ -44,6 +44,8 @@ struct Plan {
     cudaGraphExec_t exec = nullptr;
     int launches = 0;
     std::vector<PlanItem> items;   // per node: skipped by layout fusion / strided attention
+    char* carry = nullptr;         // split A planes handed from one GEMM's epilogue to the next GEMM
+    size_t carry_bytes = 0;
 };
 
 struct State {
@@ -285,6 +287,23 @@ Status launch_item(Plan& p, size_t i, cudaStream_t st, int* launches) {
     if (i < p.items.size()) {
         if (p.items[i].skip) return Status::ok();
         if (p.items[i].views) return launch_attention_views(p.nodes[i], p.items[i].attn, st, ws, launches);
+        const PlanItem& it = p.items[i];
+        if (it.epi_act || it.epi_out || it.carry_off >= 0 || it.presplit_off >= 0) {
+            GemmFusion f;
+            f.act = it.epi_act;
+            f.out = static_cast<float*>(it.epi_out);
+            if (it.carry_off >= 0) {
+                f.plane_hi = reinterpret_cast<float*>(p.carry + it.carry_off);
+                f.plane_x = p.carry + it.carry_off + it.carry_plane_bytes;
+            }
+            if (it.presplit_off >= 0) {
+                f.pre_hi = reinterpret_cast<const float*>(p.carry + it.presplit_off);
+                f.pre_x = p.carry + it.presplit_off + it.carry_plane_bytes;
+            }
+            OpNode n = p.nodes[i];
+            if (it.redirect_slot >= 0) n.inputs[it.redirect_slot] = it.redirect_ptr;
+            return launch_gemm(n, st, ws, launches, &f);
+        }
         if (p.items[i].redirect_slot >= 0) {
             OpNode n = p.nodes[i];
             n.inputs[p.items[i].redirect_slot] = p.items[i].redirect_ptr;
@@ -308,8 +327,10 @@ Status launch_all(Plan& p, cudaStream_t st, int* launches) {
 void free_plan(Plan& p) {
     if (p.exec) cudaGraphExecDestroy(p.exec);
     if (p.ws) cudaFree(p.ws);
+    if (p.carry) cudaFree(p.carry);
     p.exec = nullptr;
     p.ws = nullptr;
+    p.carry = nullptr;
 }
 
 Status build_plan(const OpNode* nodes, int n, bool capture, Plan** out) {
@@ -319,7 +340,7 @@ Status build_plan(const OpNode* nodes, int n, bool capture, Plan** out) {
         Status s = validate_node(nodes[i], i);
         if (!s.good()) return s;
     }
-    plan->items = plan_fusions(plan->nodes, S().protect);
+    plan->items = plan_fusions(plan->nodes, S().protect, &plan->carry_bytes);
     if (getenv("RT_FUSE_VERBOSE")) {
         int skipped = 0, viewed = 0;
         for (auto& it : plan->items) { skipped += it.skip; viewed += it.views; }
@@ -328,7 +349,12 @@ Status build_plan(const OpNode* nodes, int n, bool capture, Plan** out) {
     }
     size_t total = 0;
     for (int i = 0; i < n; i++) {
-        size_t b = (node_workspace(nodes[i]) + 255) & ~(size_t)255;
+        // sized for the node as launched: a redirected input can change the
+        // GEMM's choice of path (A overlapping C needs the split pre-pass)
+        OpNode eff = nodes[i];
+        if (i < (int)plan->items.size() && plan->items[i].redirect_slot >= 0)
+            eff.inputs[plan->items[i].redirect_slot] = plan->items[i].redirect_ptr;
+        size_t b = (node_workspace(eff) + 255) & ~(size_t)255;
         plan->ws_offset.push_back(total);
         plan->ws_bytes.push_back(b);
         total += b;
@@ -346,6 +372,14 @@ Status build_plan(const OpNode* nodes, int n, bool capture, Plan** out) {
         if (e != cudaSuccess) {
             cudaGetLastError();
             return Status::err(RT_ERR_OOM, "workspace allocation failed");
+        }
+    }
+    if (plan->carry_bytes) {
+        cudaError_t e = cudaMalloc(&plan->carry, plan->carry_bytes);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            free_plan(*plan);
+            return Status::err(RT_ERR_OOM, "carry buffer allocation failed");
         }
     }
     cudaStream_t st = S().stream;
@@ -563,6 +597,18 @@ int rt_free(void* dev) {
         cudaStreamSynchronize(S().stream);
         clear_plans();
     }
+    // graph outputs registered inside this memory go with it (a later
+    // allocation at the same address belongs to another graph)
+    const uintptr_t lo = it->first, hi = lo + it->second.bytes;
+    auto& pr = S().protect;
+    const size_t before = pr.size();
+    for (size_t k = 0; k < pr.size();)
+        if (pr[k].first >= lo && pr[k].first < hi) pr.erase(pr.begin() + k);
+        else k++;
+    if (pr.size() != before) {
+        cudaStreamSynchronize(S().stream);
+        clear_plans();   // plans were made with the old protections
+    }
     cudaFree(dev);
     S().allocs.erase(it);
     return RT_OK;
@@ -779,7 +825,12 @@ int rt_fusion_report(const OpNode* nodes, int n, int* skipped) {
     std::vector<PlanItem> items = plan_fusions(v, S().protect);
     int count = 0;
     for (int i = 0; i < n; i++) {
-        int f = items[i].skip ? 1 : (items[i].views ? 2 : 0);
+        const PlanItem& it = items[i];
+        int f = it.skip ? 1
+                : it.views ? 2
+                : it.presplit_off >= 0 ? 4
+                : (it.epi_act || it.epi_out || it.carry_off >= 0) ? 3
+                                                                    : 0;
         if (skipped) skipped[i] = f;
         count += items[i].skip;
     }

@@ -46,10 +46,62 @@ def test_gpt2_head_split_and_merge_copies_fold_into_attention():
     prog = Program.load(GOLDEN / "gpt2_b8.json")
     arr, _ = bind(prog)
     n, flags = report(prog, arr)
-    assert n == 14   # per layer: 3 slices + 3 head splits + the head merge
-    folded_ops = {prog.nodes[i].op for i, f in enumerate(flags) if f == 1}
-    assert folded_ops == {OP["SLICE"], OP["TRANSPOSE"]}
+    # per layer: 3 slices + 3 head splits + the head merge + the MLP's GELU
+    assert n == 16
+    folded = [prog.nodes[i].op for i, f in enumerate(flags) if f == 1]
+    assert sorted(set(folded)) == sorted({OP["SLICE"], OP["TRANSPOSE"], OP["GELU"]})
+    assert folded.count(OP["GELU"]) == 2
     assert [prog.nodes[i].op for i, f in enumerate(flags) if f == 2] == [OP["ATTENTION"]] * 2
+
+
+def test_gemm_gelu_gemm_chain_hands_over_split_operand(monkeypatch):
+    """MLP up-projection -> GELU -> down-projection: the GELU runs in the first
+    GEMM's epilogue, which (RT_FUSE_HANDOFF=1) writes the second GEMM's split
+    A operand."""
+    monkeypatch.setenv("RT_FUSE_HANDOFF", "1")
+    prog = Program.load(GOLDEN / "gpt2_b8.json")
+    arr, _ = bind(prog)
+    _, flags = report(prog, arr)
+    gelus = [i for i, nd in enumerate(prog.nodes) if nd.op == OP["GELU"]]
+    for u in gelus:
+        assert flags[u] == 1
+        assert flags[u - 1] == 3 and prog.nodes[u - 1].op == OP["MATMUL_ADD"]
+        assert flags[u + 1] == 4 and prog.nodes[u + 1].op == OP["MATMUL_ADD"]
+
+
+def test_gelu_folds_without_hand_off_by_default(monkeypatch):
+    monkeypatch.delenv("RT_FUSE_HANDOFF", raising=False)
+    prog = Program.load(GOLDEN / "gpt2_b8.json")
+    arr, _ = bind(prog)
+    _, flags = report(prog, arr)
+    for u in [i for i, nd in enumerate(prog.nodes) if nd.op == OP["GELU"]]:
+        assert flags[u - 1:u + 2] == [3, 1, 0]
+
+
+def test_protected_gelu_output_keeps_the_hand_off_out(monkeypatch):
+    """If the GELU's output is a graph output it must be written: the GEMM
+    still applies the GELU but writes the activation, and the next GEMM
+    splits it itself.  (The program is cut after the down-projection so the
+    GELU's buffer is never recycled.)"""
+    import copy
+    monkeypatch.setenv("RT_FUSE_HANDOFF", "1")
+    prog = copy.copy(Program.load(GOLDEN / "gpt2_b8.json"))
+    u = next(i for i, nd in enumerate(prog.nodes) if nd.op == OP["GELU"])
+    prog.nodes = prog.nodes[:u + 2]
+    arr, res = bind(prog)
+    _, flags = report(prog, arr)
+    assert flags[u - 1:u + 2] == [3, 1, 4]
+    nbytes = 4
+    for d in prog.nodes[u].out_shape:
+        nbytes *= d
+    lib = load_library()
+    try:
+        assert lib.rt_protect(res(prog.nodes[u].output), nbytes) == 0
+        flags = (ctypes.c_int * len(prog.nodes))()
+        lib.rt_fusion_report(arr, len(prog.nodes), flags)
+        assert list(flags)[u - 1:u + 2] == [3, 1, 0]
+    finally:
+        lib.rt_unprotect_all()
 
 
 def test_protected_output_blocks_folding():
@@ -80,9 +132,14 @@ def test_protected_output_blocks_folding():
         lib.rt_unprotect_all()
 
 
-@pytest.mark.parametrize("name", ["qwen3_b8", "7b_b8", "toy"])
-def test_no_folding_where_the_chain_does_not_match(name):
+@pytest.mark.parametrize("name,gelus", [("qwen3_b8", 0), ("7b_b8", 1), ("toy", 0)])
+def test_no_layout_folding_where_the_chain_does_not_match(name, gelus):
+    """Qwen3 (RMSNorm/RoPE between the projections and attention) and the
+    custom blocks (bias ADD after the QKV slice) keep their layout copies;
+    only the MLP GELU folds into its GEMM (not in the toy block, whose GEMMs
+    are below the tensor-core threshold)."""
     prog = Program.load(GOLDEN / f"{name}.json")
     arr, _ = bind(prog)
-    n, _ = report(prog, arr)
-    assert n == 0
+    n, flags = report(prog, arr)
+    assert n == gelus
+    assert all(prog.nodes[i].op == OP["GELU"] for i, f in enumerate(flags) if f == 1)

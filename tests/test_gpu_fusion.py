@@ -1,0 +1,87 @@
+"""GEMM epilogue fusion on the GPU: GEMM -> GELU -> GEMM chains (the GELU in
+the first GEMM's epilogue, which hands the second GEMM its split A operand)
+against the oracle, and fusion decisions on real device addresses."""
+
+import ctypes
+
+import numpy as np
+import pytest
+
+import oracle
+from lbr_b200.program import OP, ConstSpec, ProgNode, Program, Ref
+
+pytestmark = pytest.mark.gpu
+
+
+def mlp_program(M, D, F, kind, seed=0):
+    """x[M,D] -> MATMUL_ADD (F) -> [GELU] -> [MATMUL_ADD (D)]; kind = 0, 1, 2 nodes after the first."""
+    rng = np.random.default_rng(seed)
+    stored = {
+        "x": rng.standard_normal((M, D), dtype=np.float32),
+        "w1": (rng.standard_normal((F, D)) * 0.05).astype(np.float32),
+        "b1": rng.standard_normal(F).astype(np.float32) * 0.1,
+        "w2": (rng.standard_normal((D, F)) * 0.05).astype(np.float32),
+        "b2": rng.standard_normal(D).astype(np.float32) * 0.1,
+    }
+    consts = {k: ConstSpec(k, v.shape, "float32", {"kind": "stored"}) for k, v in stored.items()}
+    C = lambda n: Ref("const", n, 0)
+    A = lambda off: Ref("arena", None, off)
+    Y, Z, O = 0, M * F * 4, 2 * M * F * 4
+    nodes = [ProgNode(OP["MATMUL_ADD"], [C("x"), C("w1"), C("b1")], A(Y), [M, F], 4, [D, 1, 1])]
+    out = ("y", [M, F], Y)
+    if kind >= 1:
+        nodes.append(ProgNode(OP["GELU"], [A(Y)], A(Z), [M, F], 4, []))
+        out = ("z", [M, F], Z)
+    if kind >= 2:
+        nodes.append(ProgNode(OP["MATMUL_ADD"], [A(Z), C("w2"), C("b2")], A(O), [M, D], 4, [F, 1, 1]))
+        out = ("o", [M, D], O)
+    outs = {out[0]: {"shape": out[1], "dtype": "float32", "ref": A(out[2])}}
+    return Program(f"mlp{kind}", {}, O + M * D * 4, {}, outs, consts, nodes, stored), out[0]
+
+
+def flags_of(ex, prog):
+    f = (ctypes.c_int * len(prog.nodes))()
+    ex._lib.rt_fusion_report(ex.node_array, len(prog.nodes), f)
+    return list(f)
+
+
+@pytest.mark.parametrize("M,D,F", [(1024, 256, 1024), (300, 192, 520), (640, 128, 1028)])
+@pytest.mark.parametrize("kind,handoff", [(1, "0"), (2, "0"), (2, "1")])
+def test_fused_chain_matches_oracle(M, D, F, kind, handoff, gpu_executor_factory, monkeypatch):
+    monkeypatch.setenv("RT_FUSE_HANDOFF", handoff)
+    prog, name = mlp_program(M, D, F, kind)
+    ex = gpu_executor_factory(prog, dict(prog.stored))
+    got = ex.run({})[name]
+    flags = flags_of(ex, prog)
+    assert flags[:2] == [3, 1]                       # GELU folded into the first GEMM
+    if kind == 2:
+        assert flags[2] == (4 if handoff == "1" else 0)   # A operand handed over: no split pass
+    ref = oracle.run_program("restated", prog, dict(prog.stored), {})[name]
+    np.testing.assert_allclose(got, ref, atol=1e-4, rtol=1e-3)
+
+
+def test_freed_executor_outputs_do_not_block_fusion(gpu_executor_factory):
+    """Graph outputs registered by an executor are dropped when its memory is
+    freed, so a later executor whose buffers land at the same addresses still
+    fuses."""
+    for kind in (0, 1, 2):
+        prog, name = mlp_program(1024, 256, 1024, kind)
+        ex = gpu_executor_factory(prog, dict(prog.stored))
+        ex.run({})
+        if kind:
+            assert flags_of(ex, prog)[:2] == [3, 1]
+        ex.close()
+
+
+@pytest.mark.parametrize("env", [{"RT_GEMM_3XTF32": "1"}, {"RT_GEMM_PAIR": "0"}],
+                         ids=lambda e: ",".join(f"{k}={v}" for k, v in e.items()))
+def test_fused_chain_variants(env):
+    """Chains under the other GEMM variants (3xTF32 planes: hi + fp32 lo; the
+    one-CTA kernel), each in a fresh process."""
+    import os
+    import subprocess
+    import sys
+    r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", "-m", "gpu", "-p", "no:cacheprovider",
+                        __file__, "-k", "test_fused_chain_matches_oracle"],
+                       env=dict(os.environ, **env), capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]

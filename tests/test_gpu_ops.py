@@ -248,3 +248,22 @@ def test_reshape_copy_and_embedding(gpu_executor_factory):
     got, ref = run_both(gpu_executor_factory,
                         single_node_program(OP["EMBEDDING"], [ids, table], [1, 4, 12], [12]))
     np.testing.assert_array_equal(got, table[ids[0]][None])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("env", [
+    {"RT_GEMM_3XTF32": "1"},                       # three tf32 MMAs (hi.hi + hi.lo + lo.hi)
+    {"RT_GEMM_PAIR": "0"},                         # one-CTA kernel everywhere
+    {"RT_GEMM_PAIR": "0", "RT_GEMM_3XTF32": "1"},
+], ids=lambda e: ",".join(f"{k}={v}" for k, v in e.items()))
+def test_matmul_variants(env):
+    """The GEMM variants selected by environment switches (read once per
+    process) pass the same matmul cases, each in a fresh process."""
+    import os
+    import subprocess
+    import sys
+    full = dict(os.environ, **env)
+    r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", "-m", "gpu", "-p", "no:cacheprovider",
+                        __file__, "-k", "test_matmul and not variants"],
+                       env=full, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
