@@ -3,9 +3,12 @@
 // Same function as the reference's flash kernel (csrc/ops/attn.c:121-253):
 // scores = (Q K^T) * 1/sqrtf(D), causal mask as -inf, online softmax with
 // running max starting at -FLT_MAX, O = P V / l, GQA kv head = bh / group.
-// Both products run as 3xTF32 on tcgen05 (hi.hi + hi.lo + lo.hi) so results
-// stay at fp32 level; each P.V tile (128 keys) is accumulated in TMEM and
-// folded into fp32 registers, like the GEMM's K chunks.
+// Both products keep fp32-level accuracy with the GEMM's operand split
+// (x = hi + lo, hi = tf32(x)): hi.hi as a kind::tf32 MMA and the two cross
+// terms as ONE kind::f16 MMA over a doubled K with bf16 operands
+// [hi | lo] x [lo | hi] per 16-wide block (RT_ATTN_3XTF32=1: three tf32 MMAs,
+// hi.hi + hi.lo + lo.hi).  Each P.V tile (128 keys) is accumulated in TMEM
+// and folded into fp32 registers, like the GEMM's K chunks.
 //
 // Tiles are 128 queries x 128 keys, so every score MMA is M=128 x N=128
 // (narrower MMAs are dominated by per-instruction cost on this hardware).
@@ -16,16 +19,20 @@
 //              tile = chunks of 32 or 64 keys x D), each chunk one contiguous
 //              bulk copy of a pre-packed, pre-swizzled image;
 //   warp 1     allocates TMEM and issues the MMAs from one thread:
-//              S = Q_hi.K_hi + Q_hi.K_lo + Q_lo.K_hi (Q from shared memory),
-//              O_tile = P_hi.V_hi + P_hi.V_lo + P_lo.V_hi (P from TMEM);
+//              S = Q.K^T (Q from shared memory), O_tile = P.V (P from TMEM),
+//              each as hi.hi + the cross terms;
 //              S_{j+1} runs while the softmax works on S_j;
 //   warps 2-9  two threads per query row (64 keys and D/2 output columns
 //              each; row maxima / sums exchanged through shared memory behind
 //              bounded mbarrier waits): stage Q hi/lo into shared memory, then
 //              per tile read S from TMEM (freeing it), mask, online softmax in
-//              log2 units, fold the previous O tile into registers, write P
-//              hi/lo to TMEM.
-// TMEM columns: S [0,128) | P_hi [128,256) | P_lo [256,384) | O tile [384, 384+D).
+//              log2 units, fold the previous O tile into registers, write P's
+//              two planes to TMEM.
+// TMEM columns: S [0,128) | P_hi [128,256) | P plane 1 [256,384) | O tile [384, 384+D).
+// Plane 1 of every operand (Q, K, V in shared memory, P in TMEM) is lo as
+// fp32, or for the cross scheme bf16 [hi | lo] (Q, P) / [lo | hi] (K, V) per
+// 16-wide K block -- the same 4 bytes per element, so tiles and offsets are
+// shared by both schemes.
 // K and V are split, V transposed and both packed into per-tile images in the
 // node's workspace by a bandwidth-bound pre-pass (pack_kv_kernel).  All waits
 // are bounded (see sm100_ptx.h).
@@ -97,7 +104,31 @@ struct KvViews {
     int Hkv;                                      // kv heads per batch element
 };
 
-template <int D>
+// bf16 (round to nearest even) of two values, `a` in the low half.
+__device__ __forceinline__ uint32_t bf16x2(float a, float b) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+    return r;
+}
+
+// Plane 1 of four consecutive K elements x (k % 4 == 0, k = position inside a
+// 128-byte row of 32 elements) at row `row` of a swizzled [rows][128 B]
+// block: lo as fp32, or the cross layout (first = hi (A role) / lo (B role)).
+template <bool CROSS, bool A_ROLE>
+__device__ __forceinline__ void put_plane1(uint8_t* blk, int row, int k, float4 h, float4 l) {
+    if (!CROSS) {
+        *reinterpret_cast<float4*>(blk + swz(row, k)) = l;
+        return;
+    }
+    const float4 f = A_ROLE ? h : l, g = A_ROLE ? l : h;
+    const int b = k >> 4, j = k & 15;   // 16-wide block inside the row, position in it
+    // bf16 positions b*32 + j (first) and b*32 + 16 + j (second) = 4-byte slots / 2
+    *reinterpret_cast<uint2*>(blk + swz(row, b * 16 + (j >> 1))) = make_uint2(bf16x2(f.x, f.y), bf16x2(f.z, f.w));
+    *reinterpret_cast<uint2*>(blk + swz(row, b * 16 + 8 + (j >> 1))) =
+        make_uint2(bf16x2(g.x, g.y), bf16x2(g.z, g.w));
+}
+
+template <int D, bool CROSS>
 __global__ void __launch_bounds__(256) pack_kv_kernel(KvViews kv, uint8_t* __restrict__ out, int S, int n_kv) {
     using C = AttnTcCfg<D>;
     __shared__ float sv[32][D + 1];
@@ -113,9 +144,10 @@ __global__ void __launch_bounds__(256) pack_kv_kernel(KvViews kv, uint8_t* __res
         float4 x = k0 + r < S ? *reinterpret_cast<const float4*>(kb + (int64_t)(k0 + r) * kv.k_ss + d)
                               : make_float4(0.f, 0.f, 0.f, 0.f);
         float4 hi = make_float4(tf32_round(x.x), tf32_round(x.y), tf32_round(x.z), tf32_round(x.w));
-        uint8_t* kc = tile + (size_t)(d >> 5) * CHUNK + swz(r, d & 31);
-        *reinterpret_cast<float4*>(kc) = hi;
-        *reinterpret_cast<float4*>(kc + CHUNK / 2) = make_float4(x.x - hi.x, x.y - hi.y, x.z - hi.z, x.w - hi.w);
+        uint8_t* kc = tile + (size_t)(d >> 5) * CHUNK;
+        *reinterpret_cast<float4*>(kc + swz(r, d & 31)) = hi;
+        put_plane1<CROSS, false>(kc + CHUNK / 2, r, d & 31, hi,
+                                 make_float4(x.x - hi.x, x.y - hi.y, x.z - hi.z, x.w - hi.w));
     }
     // V^T: unit = 4 consecutive keys of one feature
     for (int kb32 = 0; kb32 < BKV; kb32 += 32) {
@@ -134,14 +166,14 @@ __global__ void __launch_bounds__(256) pack_kv_kernel(KvViews kv, uint8_t* __res
             const int d = u >> 3, w = (u & 7) * 4;
             float4 x = make_float4(sv[w][d], sv[w + 1][d], sv[w + 2][d], sv[w + 3][d]);
             float4 hi = make_float4(tf32_round(x.x), tf32_round(x.y), tf32_round(x.z), tf32_round(x.w));
-            uint8_t* dst = vcp + swz(d, w);
-            *reinterpret_cast<float4*>(dst) = hi;
-            *reinterpret_cast<float4*>(dst + CHUNK / 2) = make_float4(x.x - hi.x, x.y - hi.y, x.z - hi.z, x.w - hi.w);
+            *reinterpret_cast<float4*>(vcp + swz(d, w)) = hi;
+            put_plane1<CROSS, false>(vcp + CHUNK / 2, d, w, hi,
+                                     make_float4(x.x - hi.x, x.y - hi.y, x.z - hi.z, x.w - hi.w));
         }
     }
 }
 
-template <int D>
+template <int D, bool CROSS>
 __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_constant__ AttnTcParams p) {
     using C = AttnTcCfg<D>;
     constexpr int STAGES = C::STAGES;
@@ -227,6 +259,8 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
         if (lane == 0) {
             constexpr uint32_t idesc_s = ptx::idesc_tf32(BQ, BKV);
             constexpr uint32_t idesc_o = ptx::idesc_tf32(BQ, D);
+            constexpr uint32_t idesc_sx = ptx::idesc_bf16(BQ, BKV);
+            constexpr uint32_t idesc_ox = ptx::idesc_bf16(BQ, D);
             int stage = 0;
             uint32_t ph = 0;
             bool ok = ptx::wait_bounded(q_ready, 0, abort_flag, p.err, ERR_A_MMA, WAIT_NS);
@@ -253,12 +287,17 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
                     const uint64_t al = ptx::smem_desc(ql + c * BQ * 128, 1024, 2);
                     const uint64_t bh0 = ptx::smem_desc(buf, 1024, 2);
                     const uint64_t bl0 = ptx::smem_desc(buf + CHUNK / 2, 1024, 2);
+                    // 32 bytes per K step in both kinds (8 tf32 / 16 bf16)
 #pragma unroll
                     for (int kk = 0; kk < 4; kk++) {
                         const uint64_t off = (uint64_t)((kk * 32) >> 4);
                         ptx::mma_tf32(tmem + COL_S, ah + off, bh0 + off, idesc_s, (c | kk) ? 1u : 0u);
-                        ptx::mma_tf32(tmem + COL_S, ah + off, bl0 + off, idesc_s, 1u);
-                        ptx::mma_tf32(tmem + COL_S, al + off, bh0 + off, idesc_s, 1u);
+                        if (CROSS) {
+                            ptx::mma_bf16(tmem + COL_S, al + off, bl0 + off, idesc_sx, 1u);
+                        } else {
+                            ptx::mma_tf32(tmem + COL_S, ah + off, bl0 + off, idesc_s, 1u);
+                            ptx::mma_tf32(tmem + COL_S, al + off, bh0 + off, idesc_s, 1u);
+                        }
                     }
                     release();
                 }
@@ -275,8 +314,13 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
                         const uint64_t off = (uint64_t)((((kk >> 2) * D * 128) + (kk & 3) * 32) >> 4);
                         const uint32_t kc = c * C::V_KEYS + kk * 8;
                         ptx::mma_tf32_ts(tmem + COL_O, tmem + COL_PH + kc, bh0 + off, idesc_o, (c | kk) ? 1u : 0u);
-                        ptx::mma_tf32_ts(tmem + COL_O, tmem + COL_PH + kc, bl0 + off, idesc_o, 1u);
-                        ptx::mma_tf32_ts(tmem + COL_O, tmem + COL_PL + kc, bh0 + off, idesc_o, 1u);
+                        if (CROSS) {
+                            // doubled K: 8 columns = 16 bf16 of P plane 1 per step, 32 bytes of V plane 1
+                            ptx::mma_bf16_ts(tmem + COL_O, tmem + COL_PL + kc, bl0 + off, idesc_ox, 1u);
+                        } else {
+                            ptx::mma_tf32_ts(tmem + COL_O, tmem + COL_PH + kc, bl0 + off, idesc_o, 1u);
+                            ptx::mma_tf32_ts(tmem + COL_O, tmem + COL_PL + kc, bh0 + off, idesc_o, 1u);
+                        }
                     }
                     release();
                 }
@@ -319,9 +363,9 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
         for (int d = half * DH; d < (half + 1) * DH; d += 4) {
             float4 v = q < p.S ? *reinterpret_cast<const float4*>(qrow + d) : make_float4(0.f, 0.f, 0.f, 0.f);
             float4 h = make_float4(tf32_round(v.x), tf32_round(v.y), tf32_round(v.z), tf32_round(v.w));
-            const uint32_t off = (uint32_t)(d >> 5) * BQ * 128 + swz(row, d & 31);
-            *reinterpret_cast<float4*>(qh + off) = h;
-            *reinterpret_cast<float4*>(ql + off) = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+            const uint32_t blk = (uint32_t)(d >> 5) * BQ * 128;
+            *reinterpret_cast<float4*>(qh + blk + swz(row, d & 31)) = h;
+            put_plane1<CROSS, true>(ql + blk, row, d & 31, h, make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w));
         }
         ptx::fence_proxy_async_smem();
         ptx::mbar_arrive(q_ready);
@@ -396,12 +440,24 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
 #pragma unroll
             for (int c16 = 0; c16 < KH / 16; c16++) {
                 uint32_t ph[16], pl[16];
+                if (CROSS) {   // plane 1: 8 columns of bf16 pairs of hi, then 8 of lo
 #pragma unroll
-                for (int i = 0; i < 16; i++) {
-                    const float pv = sv[c16 * 16 + i];
-                    const float h = tf32_round(pv);
-                    ph[i] = __float_as_uint(h);
-                    pl[i] = __float_as_uint(pv - h);
+                    for (int i = 0; i < 16; i += 2) {
+                        const float a = sv[c16 * 16 + i], b = sv[c16 * 16 + i + 1];
+                        const float ha = tf32_round(a), hb = tf32_round(b);
+                        ph[i] = __float_as_uint(ha);
+                        ph[i + 1] = __float_as_uint(hb);
+                        pl[i / 2] = bf16x2(ha, hb);
+                        pl[8 + i / 2] = bf16x2(a - ha, b - hb);
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 16; i++) {
+                        const float pv = sv[c16 * 16 + i];
+                        const float h = tf32_round(pv);
+                        ph[i] = __float_as_uint(h);
+                        pl[i] = __float_as_uint(pv - h);
+                    }
                 }
                 ptx::tmem_st16(tmem + lane_off + COL_PH + half * KH + c16 * 16, ph);
                 ptx::tmem_st16(tmem + lane_off + COL_PL + half * KH + c16 * 16, pl);
@@ -454,10 +510,22 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
     }
 }
 
+// Cross-term scheme unless RT_ATTN_3XTF32=1.
+bool attn_cross() {
+    static const bool on = [] {
+        const char* e = getenv("RT_ATTN_3XTF32");
+        return !(e && e[0] == '1');
+    }();
+    return on;
+}
+
 template <int D>
 Status launch_tc(const AttnTcParams& prm, int BH, cudaStream_t st) {
     dim3 grid((unsigned)prm.n_qblocks, (unsigned)BH);
-    attn_tc_kernel<D><<<grid, ATHREADS, AttnTcCfg<D>::SMEM, st>>>(prm);
+    if (attn_cross())
+        attn_tc_kernel<D, true><<<grid, ATHREADS, AttnTcCfg<D>::SMEM, st>>>(prm);
+    else
+        attn_tc_kernel<D, false><<<grid, ATHREADS, AttnTcCfg<D>::SMEM, st>>>(prm);
     RT_LAUNCH_CHECK();
     return Status::ok();
 }
@@ -478,10 +546,14 @@ size_t attention_tc_workspace(int64_t BHkv, int64_t S, int D) {
 Status attention_tc_prepare() {
     static bool done = false;
     if (!done) {
-        RT_CUDA_CHECK(cudaFuncSetAttribute(attn_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        RT_CUDA_CHECK(cudaFuncSetAttribute(attn_tc_kernel<64, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            AttnTcCfg<64>::SMEM));
-        RT_CUDA_CHECK(cudaFuncSetAttribute(attn_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           AttnTcCfg<128>::SMEM));
+        RT_CUDA_CHECK(cudaFuncSetAttribute(attn_tc_kernel<128, true>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, AttnTcCfg<128>::SMEM));
+        RT_CUDA_CHECK(cudaFuncSetAttribute(attn_tc_kernel<64, false>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, AttnTcCfg<64>::SMEM));
+        RT_CUDA_CHECK(cudaFuncSetAttribute(attn_tc_kernel<128, false>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, AttnTcCfg<128>::SMEM));
         done = true;
     }
     return Status::ok();
@@ -495,10 +567,12 @@ Status launch_attention_tc(const AttnViews& vw, int64_t BH, int64_t S, int D, in
     const int n_kv = (int)((S + BKV - 1) / BKV);
     dim3 pgrid((unsigned)n_kv, (unsigned)BHkv);
     KvViews kv{vw.k, vw.v, vw.k_sb, vw.k_sh, vw.k_ss, vw.v_sb, vw.v_sh, vw.v_ss, vw.H / group};
-    if (D == 64)
-        pack_kv_kernel<64><<<pgrid, 256, 0, st>>>(kv, reinterpret_cast<uint8_t*>(ws.base), (int)S, n_kv);
-    else
-        pack_kv_kernel<128><<<pgrid, 256, 0, st>>>(kv, reinterpret_cast<uint8_t*>(ws.base), (int)S, n_kv);
+    uint8_t* kvbuf = reinterpret_cast<uint8_t*>(ws.base);
+    const bool cross = attn_cross();
+    if (D == 64 && cross) pack_kv_kernel<64, true><<<pgrid, 256, 0, st>>>(kv, kvbuf, (int)S, n_kv);
+    else if (D == 64) pack_kv_kernel<64, false><<<pgrid, 256, 0, st>>>(kv, kvbuf, (int)S, n_kv);
+    else if (cross) pack_kv_kernel<128, true><<<pgrid, 256, 0, st>>>(kv, kvbuf, (int)S, n_kv);
+    else pack_kv_kernel<128, false><<<pgrid, 256, 0, st>>>(kv, kvbuf, (int)S, n_kv);
     RT_LAUNCH_CHECK();
     *launches += 1;
     AttnTcParams prm;

@@ -267,3 +267,16 @@ def test_matmul_variants(env):
                         __file__, "-k", "test_matmul and not variants"],
                        env=full, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
+
+
+@pytest.mark.gpu
+def test_attention_3xtf32_variant():
+    """The three-tf32-MMA attention (RT_ATTN_3XTF32=1, read once per process)
+    passes the same attention cases, in a fresh process."""
+    import os
+    import subprocess
+    import sys
+    r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", "-m", "gpu", "-p", "no:cacheprovider",
+                        __file__, "-k", "test_attention and not variant"],
+                       env=dict(os.environ, RT_ATTN_3XTF32="1"), capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
