@@ -143,8 +143,11 @@ struct Analysis {
     std::vector<std::vector<Range>> reads;
     std::vector<Range> writes;
 
-    explicit Analysis(const std::vector<OpNode>& ns) : nodes(ns), reads(ns.size()), writes(ns.size()) {
+    // `gone`: nodes already folded away (they neither read nor write)
+    explicit Analysis(const std::vector<OpNode>& ns, const std::vector<bool>* gone = nullptr)
+        : nodes(ns), reads(ns.size()), writes(ns.size()) {
         for (size_t i = 0; i < ns.size(); i++) {
+            if (gone && (*gone)[i]) continue;
             read_ranges(ns[i], reads[i]);
             writes[i] = write_range(ns[i]);
         }
@@ -404,6 +407,85 @@ bool valid(const Analysis& an, const Effective& e, const Proposal& p, const std:
     return true;
 }
 
+// Bias fold: a bias-less GEMM whose output [.., N] is consumed only by
+// last-dim SLICEs, each followed (first reader, nothing in between) by an
+// in-place ADD of a constant bias [len] -- the custom blocks' merged QKV
+// projection.  The GEMM adds one merged bias [N] (the slices' biases at their
+// column ranges, zero elsewhere; built at plan time in a plan-owned buffer)
+// and the ADDs are not launched, which leaves SLICE -> TRANSPOSE chains for
+// the layout fusion.  Returns the folded ADDs in `gone`.
+void plan_bias_folds(const std::vector<OpNode>& nodes, const std::vector<Range>& protect,
+                     std::vector<PlanItem>& items, std::vector<bool>& gone, BiasPlan* bp) {
+    Analysis an(nodes);
+    const int n = (int)nodes.size();
+    for (int g = 0; g < n; g++) {
+        const OpNode& gn = nodes[g];
+        if (gn.op != RT_OP_MATMUL || !gemm_fusable(gn)) continue;
+        GemmProblem gp;
+        if (!decode_gemm(gn, &gp).good() || gp.bias || gp.alpha != 1.0f) continue;
+        const Range W = an.writes[g];
+        const int64_t M = gp.batches * gp.M, N = gp.N;
+        std::vector<int> slices;
+        bool ok = true;
+        for (int j = g + 1; j < n && ok; j++) {
+            bool rd = false;
+            for (const Range& x : an.reads[j]) rd |= overlaps(x, W);
+            if (rd) {
+                const OpNode& sl = nodes[j];
+                if (sl.op == RT_OP_SLICE && sl.inputs[0] == gn.output && sl.elem_size == 4 && sl.extra[0] == M &&
+                    sl.extra[1] == N && sl.extra[4] == 1)
+                    slices.push_back(j);
+                else
+                    ok = false;
+            }
+            if (overlaps(an.writes[j], W)) break;
+        }
+        if (!ok || slices.empty()) continue;
+        bool recycled = false;
+        for (int j = g + 1; j < n; j++) recycled |= overlaps(an.writes[j], W);
+        if (!recycled)
+            for (const Range& pr : protect) ok &= !overlaps(pr, W);
+        std::vector<std::pair<int, int>> adds;          // (ADD node, slice)
+        std::vector<std::pair<int64_t, int64_t>> cols;  // column ranges, for disjointness
+        for (int sidx : slices) {
+            if (!ok) break;
+            const OpNode& sl = nodes[sidx];
+            const Range O = an.writes[sidx];
+            int a = -1;
+            for (int j = sidx + 1; j < n; j++) {
+                bool rd = false;
+                for (const Range& x : an.reads[j]) rd |= overlaps(x, O);
+                if (rd) { a = j; break; }
+                if (overlaps(an.writes[j], O)) break;
+            }
+            if (a < 0) { ok = false; break; }
+            const OpNode& ad = nodes[a];
+            const int64_t len = sl.extra[3];
+            if (ad.op != RT_OP_ADD || ad.extra[0] != 0 || ad.inputs[0] != sl.output || ad.output != sl.output ||
+                ad.elem_size != 4 || last_dim(ad) != len || !is_constant_range(ad.inputs[1], (size_t)len * 4)) {
+                ok = false;
+                break;
+            }
+            for (auto& c : cols)
+                if (sl.extra[2] < c.second && c.first < sl.extra[2] + len) ok = false;
+            cols.push_back({sl.extra[2], sl.extra[2] + len});
+            adds.push_back({a, sidx});
+        }
+        if (!ok) continue;
+        const int64_t off = (int64_t)bp->bytes;
+        bp->bytes += ((size_t)N * 4 + 255) & ~(size_t)255;
+        bp->zero.push_back({off, N * 4});
+        for (auto& ap : adds) {
+            const OpNode& sl = nodes[ap.second];
+            bp->copies.push_back({off + sl.extra[2] * 4, nodes[ap.first].inputs[1], sl.extra[3] * 4});
+            items[ap.first].skip = true;
+            gone[ap.first] = true;
+        }
+        items[g].epi_bias_off = off;
+        if (dbg()) fprintf(stderr, "[fusion] gemm %d: %zu slice biases folded into the epilogue\n", g, adds.size());
+    }
+}
+
 // GEMM epilogue fusion on the schedule left by layout fusion:
 //   GEMM g -> GELU u: g applies the GELU and writes u's output; u is skipped.
 //   ... -> GEMM k reading u's output as its A operand: g writes k's split A
@@ -490,14 +572,17 @@ bool fusion_enabled() {
 
 std::vector<PlanItem> plan_fusions(const std::vector<OpNode>& nodes,
                                    const std::vector<std::pair<uintptr_t, size_t>>& protected_ranges,
-                                   size_t* carry_bytes) {
+                                   size_t* carry_bytes, BiasPlan* bias_plan) {
     std::vector<PlanItem> items(nodes.size());
     if (carry_bytes) *carry_bytes = 0;
-    Analysis an(nodes);
     std::vector<Range> protect;
     for (auto& pr : protected_ranges) protect.push_back(Range{pr.first, pr.first + pr.second});
     // last entry: the final node's output (a graph output unless recycled)
-    protect.push_back(nodes.empty() ? Range{} : an.writes.back());
+    protect.push_back(nodes.empty() ? Range{} : write_range(nodes.back()));
+    std::vector<bool> gone(nodes.size(), false);
+    BiasPlan local_bp;
+    if (fusion_enabled()) plan_bias_folds(nodes, protect, items, gone, bias_plan ? bias_plan : &local_bp);
+    Analysis an(nodes, &gone);
     // candidates per attention node, most ambitious first
     std::vector<std::vector<Proposal>> cands;
     for (size_t a = 0; a < nodes.size(); a++) {

@@ -972,7 +972,7 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
     if (!(s = make_tmap(&prm.tb_hi, b_hi, p.K, p.N, p.batches, b_box, bk)).good()) return s;
     if (!(s = make_tmap(&prm.tb_lo, b_lo, p.K, p.N, p.batches, b_box, bk)).good()) return s;
     prm.c = f && f->out ? f->out : p.c;
-    prm.bias = p.bias;
+    prm.bias = f && f->bias ? f->bias : p.bias;
     prm.alpha = p.alpha;
     prm.act = f ? f->act : 0;
     prm.plane_hi = f ? f->plane_hi : nullptr;

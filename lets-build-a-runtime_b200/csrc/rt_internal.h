@@ -85,6 +85,7 @@ struct GemmFusion {
     void* plane_x = nullptr;
     const float* pre_hi = nullptr;  // this GEMM's A, already split
     const void* pre_x = nullptr;
+    const float* bias = nullptr;    // bias to add (a node without one: a folded bias)
 };
 Status launch_gemm(const OpNode& n, cudaStream_t st, Workspace ws, int* launches,
                    const GemmFusion* f = nullptr);
@@ -125,11 +126,20 @@ struct PlanItem {
     int64_t carry_off = -1;        // producer: write A planes here (byte offset into the carry buffer)
     int64_t presplit_off = -1;     // consumer: A planes are already here; no split pre-pass
     int64_t carry_plane_bytes = 0; // bytes of one plane
+    int64_t epi_bias_off = -1;     // GEMM adds this merged bias (byte offset into the plan's bias buffer)
+};
+// Merged biases of bias folds: a plan-owned device buffer of `bytes`, zeroed
+// in `zero` ranges then filled by device-to-device `copies` (dst offset, src, bytes).
+struct BiasPlan {
+    size_t bytes = 0;
+    std::vector<std::pair<int64_t, int64_t>> zero;
+    struct Copy { int64_t dst; const void* src; int64_t bytes; };
+    std::vector<Copy> copies;
 };
 // `carry_bytes` receives the carry buffer size the items need (0 if none).
 std::vector<PlanItem> plan_fusions(const std::vector<OpNode>& nodes,
                                    const std::vector<std::pair<uintptr_t, size_t>>& protected_ranges,
-                                   size_t* carry_bytes = nullptr);
+                                   size_t* carry_bytes = nullptr, BiasPlan* bias_plan = nullptr);
 size_t attention_workspace_bytes(const OpNode& n);
 Status prepare_attention(const OpNode& n);
 Status launch_elementwise(const OpNode& n, cudaStream_t st, int* launches);

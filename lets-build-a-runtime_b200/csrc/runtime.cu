@@ -46,6 +46,8 @@ struct Plan {
     std::vector<PlanItem> items;   // per node: skipped by layout fusion / strided attention
     char* carry = nullptr;         // split A planes handed from one GEMM's epilogue to the next GEMM
     size_t carry_bytes = 0;
+    char* bias = nullptr;          // merged biases of folded bias ADDs
+    BiasPlan bias_plan;
 };
 
 struct State {
@@ -288,9 +290,10 @@ Status launch_item(Plan& p, size_t i, cudaStream_t st, int* launches) {
         if (p.items[i].skip) return Status::ok();
         if (p.items[i].views) return launch_attention_views(p.nodes[i], p.items[i].attn, st, ws, launches);
         const PlanItem& it = p.items[i];
-        if (it.epi_act || it.epi_out || it.carry_off >= 0 || it.presplit_off >= 0) {
+        if (it.epi_act || it.epi_out || it.carry_off >= 0 || it.presplit_off >= 0 || it.epi_bias_off >= 0) {
             GemmFusion f;
             f.act = it.epi_act;
+            if (it.epi_bias_off >= 0) f.bias = reinterpret_cast<const float*>(p.bias + it.epi_bias_off);
             f.out = static_cast<float*>(it.epi_out);
             if (it.carry_off >= 0) {
                 f.plane_hi = reinterpret_cast<float*>(p.carry + it.carry_off);
@@ -328,9 +331,11 @@ void free_plan(Plan& p) {
     if (p.exec) cudaGraphExecDestroy(p.exec);
     if (p.ws) cudaFree(p.ws);
     if (p.carry) cudaFree(p.carry);
+    if (p.bias) cudaFree(p.bias);
     p.exec = nullptr;
     p.ws = nullptr;
     p.carry = nullptr;
+    p.bias = nullptr;
 }
 
 Status build_plan(const OpNode* nodes, int n, bool capture, Plan** out) {
@@ -340,7 +345,7 @@ Status build_plan(const OpNode* nodes, int n, bool capture, Plan** out) {
         Status s = validate_node(nodes[i], i);
         if (!s.good()) return s;
     }
-    plan->items = plan_fusions(plan->nodes, S().protect, &plan->carry_bytes);
+    plan->items = plan_fusions(plan->nodes, S().protect, &plan->carry_bytes, &plan->bias_plan);
     if (getenv("RT_FUSE_VERBOSE")) {
         int skipped = 0, viewed = 0;
         for (auto& it : plan->items) { skipped += it.skip; viewed += it.views; }
@@ -380,6 +385,21 @@ Status build_plan(const OpNode* nodes, int n, bool capture, Plan** out) {
             cudaGetLastError();
             free_plan(*plan);
             return Status::err(RT_ERR_OOM, "carry buffer allocation failed");
+        }
+    }
+    if (plan->bias_plan.bytes) {   // merged biases: built once, before any capture
+        const BiasPlan& bp = plan->bias_plan;
+        cudaError_t e = cudaMalloc(&plan->bias, bp.bytes);
+        for (auto& z : bp.zero)
+            if (e == cudaSuccess) e = cudaMemsetAsync(plan->bias + z.first, 0, (size_t)z.second, S().stream);
+        for (auto& c : bp.copies)
+            if (e == cudaSuccess)
+                e = cudaMemcpyAsync(plan->bias + c.dst, c.src, (size_t)c.bytes, cudaMemcpyDeviceToDevice, S().stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(S().stream);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            free_plan(*plan);
+            return Status::err(RT_ERR_CUDA, std::string("merged bias: ") + cudaGetErrorString(e));
         }
     }
     cudaStream_t st = S().stream;
@@ -829,7 +849,7 @@ int rt_fusion_report(const OpNode* nodes, int n, int* skipped) {
         int f = it.skip ? 1
                 : it.views ? 2
                 : it.presplit_off >= 0 ? 4
-                : (it.epi_act || it.epi_out || it.carry_off >= 0) ? 3
+                : (it.epi_act || it.epi_out || it.carry_off >= 0 || it.epi_bias_off >= 0) ? 3
                                                                     : 0;
         if (skipped) skipped[i] = f;
         count += items[i].skip;

@@ -134,10 +134,12 @@ def test_protected_output_blocks_folding():
 
 @pytest.mark.parametrize("name,gelus", [("qwen3_b8", 0), ("7b_b8", 1), ("toy", 0)])
 def test_no_layout_folding_where_the_chain_does_not_match(name, gelus):
-    """Qwen3 (RMSNorm/RoPE between the projections and attention) and the
-    custom blocks (bias ADD after the QKV slice) keep their layout copies;
-    only the MLP GELU folds into its GEMM (not in the toy block, whose GEMMs
-    are below the tensor-core threshold)."""
+    """Qwen3 (RMSNorm/RoPE between the projections and attention) keeps its
+    layout copies.  The custom blocks' bias ADD after the QKV slice folds into
+    the merged GEMM only when the bias is a registered constant -- not in this
+    host-only report (tests/test_gpu_fusion.py covers it on the device) -- so
+    here only the MLP GELU folds into its GEMM (not in the toy block, whose
+    GEMMs are below the tensor-core threshold)."""
     prog = Program.load(GOLDEN / f"{name}.json")
     arr, _ = bind(prog)
     n, flags = report(prog, arr)

@@ -85,3 +85,34 @@ def test_fused_chain_variants(env):
                         __file__, "-k", "test_fused_chain_matches_oracle"],
                        env=dict(os.environ, **env), capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
+
+
+@pytest.mark.parametrize("name", ["7b_b1", "block_hd128_s320", "block_mini_causal_s300"])
+def test_custom_block_bias_fold_unlocks_layout_fusion(name, gpu_executor_factory):
+    """Custom blocks: merged QKV MATMUL -> SLICE -> in-place bias ADD ->
+    head-split TRANSPOSE.  The three bias ADDs fold into the GEMM (a merged
+    bias built at plan time), which leaves SLICE -> TRANSPOSE -> ATTENTION
+    chains for the layout fusion.  Outputs are checked against goldens /
+    the reference executor by test_gpu_programs; here, the fusion decision
+    on real device addresses (bias constants registered)."""
+    from conftest import GOLDEN
+    prog = Program.load(GOLDEN / f"{name}.json")
+    ex = gpu_executor_factory(prog, prog.make_constants())
+    flags = flags_of(ex, prog)
+    ops = [nd.op for nd in prog.nodes]
+    mm = ops.index(OP["MATMUL"])
+    if not ex._lib.rt_fusion_report:   # pragma: no cover
+        pytest.skip("no report")
+    tc = flags[mm] == 3
+    folded = [ops[i] for i, f in enumerate(flags) if f == 1]
+    if not tc:   # GEMM below the tensor-core threshold: nothing to fold
+        assert folded.count(OP["ADD"]) == 0
+        return
+    assert folded.count(OP["ADD"]) == 3
+    assert folded.count(OP["SLICE"]) == 3 and folded.count(OP["TRANSPOSE"]) == 4
+    ins = prog.make_inputs(0)
+    got = ex.run(ins)
+    ref = oracle.run_program("restated", prog, prog.make_constants(), ins) if name != "7b_b1" else None
+    if ref is not None:
+        for k in got:
+            np.testing.assert_allclose(got[k], ref[k], atol=1e-4, rtol=1e-3)
