@@ -135,6 +135,11 @@ int rt_kernel_launches(const OpNode* nodes, int n_nodes);
 int rt_profile(const OpNode* nodes, int n_nodes, int reps, float* ms_per_node);
 /* Drop cached plans, graphs and derived constant forms. */
 int rt_reset_plans(void);
+/* Drop the cached plan (captured graph, scratch) of this node array only --
+ * what an executor releases when it is closed while others keep theirs.
+ * rt_plan_count() = plans currently cached (one per distinct node array). */
+int rt_release(const OpNode* nodes, int n_nodes);
+int rt_plan_count(void);
 int rt_synchronize(void);
 /* The library stream (a cudaStream_t), for callers that order work on it. */
 void* rt_stream(void);

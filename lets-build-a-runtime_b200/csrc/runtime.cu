@@ -470,6 +470,52 @@ Status get_plan(const OpNode* nodes, int n, Plan** out) {
     return build_plan(nodes, n, true, out);
 }
 
+// Plans (and for constants, cached splits) that touch [lo, hi): a node
+// writing into it, or any node pointer inside it.
+bool plan_touches(const Plan& p, uintptr_t lo, uintptr_t hi) {
+    for (const OpNode& nd : p.nodes) {
+        const uintptr_t o = reinterpret_cast<uintptr_t>(nd.output);
+        int64_t numel = 1;
+        for (int d = 0; d < nd.n_dims && d < 24; d++) numel *= nd.out_shape[d];
+        const uintptr_t oe = o + (uintptr_t)(numel * (nd.elem_size > 0 ? nd.elem_size : 1));
+        if (o < hi && lo < oe) return true;
+        for (int i = 0; i < nd.n_inputs && i < 12; i++) {
+            const uintptr_t a = reinterpret_cast<uintptr_t>(nd.inputs[i]);
+            if (a >= lo && a < hi) return true;
+        }
+    }
+    return false;
+}
+
+void drop_plans_touching(uintptr_t lo, uintptr_t hi, bool splits_too) {
+    bool synced = false;
+    for (auto it = S().plans.begin(); it != S().plans.end();) {
+        auto& v = it->second;
+        for (size_t k = 0; k < v.size();) {
+            if (plan_touches(*v[k], lo, hi)) {
+                if (!synced) { cudaStreamSynchronize(S().stream); synced = true; }
+                free_plan(*v[k]);
+                v.erase(v.begin() + k);
+            } else {
+                k++;
+            }
+        }
+        it = v.empty() ? S().plans.erase(it) : std::next(it);
+    }
+    if (!splits_too) return;
+    for (auto it = S().splits.begin(); it != S().splits.end();) {
+        const uintptr_t a = reinterpret_cast<uintptr_t>(it->first.src);
+        if (a >= lo && a < hi) {
+            if (!synced) { cudaStreamSynchronize(S().stream); synced = true; }
+            cudaFree(it->second.hi);
+            cudaFree(it->second.lo);
+            it = S().splits.erase(it);
+        } else {
+            ++it;
+        }
+    }
+}
+
 void clear_plans() {
     for (auto& kv : S().plans)
         for (auto& p : kv.second) free_plan(*p);
@@ -612,23 +658,16 @@ int rt_free(void* dev) {
     RT_NEED_INIT;
     auto it = S().allocs.find(reinterpret_cast<uintptr_t>(dev));
     if (it == S().allocs.end() || it->second.host) return fail(RT_ERR_ARGUMENT, "rt_free: unknown pointer");
-    if (it->second.constant) {
-        // derived forms of this constant must go with it
-        cudaStreamSynchronize(S().stream);
-        clear_plans();
-    }
-    // graph outputs registered inside this memory go with it (a later
-    // allocation at the same address belongs to another graph)
+    // Plans that use this memory, and derived forms (splits) of a constant,
+    // go with it; other graphs keep their captured plans.  Graph outputs
+    // registered inside it go too (a later allocation at the same address
+    // belongs to another graph).
     const uintptr_t lo = it->first, hi = lo + it->second.bytes;
+    drop_plans_touching(lo, hi, it->second.constant);
     auto& pr = S().protect;
-    const size_t before = pr.size();
     for (size_t k = 0; k < pr.size();)
         if (pr[k].first >= lo && pr[k].first < hi) pr.erase(pr.begin() + k);
         else k++;
-    if (pr.size() != before) {
-        cudaStreamSynchronize(S().stream);
-        clear_plans();   // plans were made with the old protections
-    }
     cudaFree(dev);
     S().allocs.erase(it);
     return RT_OK;
@@ -798,6 +837,32 @@ int rt_profile(const OpNode* nodes, int n, int reps, float* ms_per_node) {
     return RT_OK;
 }
 
+int rt_release(const OpNode* nodes, int n) {
+    RT_GUARD;
+    if (!S().initialized || n < 0 || (n > 0 && !nodes)) return RT_OK;
+    uint64_t h = fnv1a(nodes, sizeof(OpNode) * (size_t)n, (uint64_t)n);
+    auto it = S().plans.find(h);
+    if (it == S().plans.end()) return RT_OK;
+    cudaStreamSynchronize(S().stream);
+    auto& v = it->second;
+    for (size_t k = 0; k < v.size();) {
+        if ((int)v[k]->nodes.size() == n && memcmp(v[k]->nodes.data(), nodes, sizeof(OpNode) * n) == 0) {
+            free_plan(*v[k]);
+            v.erase(v.begin() + k);
+        } else {
+            k++;
+        }
+    }
+    if (v.empty()) S().plans.erase(it);
+    return RT_OK;
+}
+
+int rt_plan_count(void) {
+    int c = 0;
+    for (auto& kv : S().plans) c += (int)kv.second.size();
+    return c;
+}
+
 int rt_reset_plans(void) {
     RT_GUARD;
     RT_NEED_INIT;
@@ -822,10 +887,9 @@ int rt_protect(const void* ptr, size_t bytes) {
     RT_GUARD;
     if (!ptr) return fail(RT_ERR_NULL_POINTER, "rt_protect: NULL");
     S().protect.push_back({reinterpret_cast<uintptr_t>(ptr), bytes});
-    if (S().initialized) {   // plans built without this range may have folded it away
-        cudaStreamSynchronize(S().stream);
-        clear_plans();
-    }
+    // plans built without this range may have folded a writer of it away
+    const uintptr_t lo = reinterpret_cast<uintptr_t>(ptr);
+    if (S().initialized) drop_plans_touching(lo, lo + bytes, false);
     return RT_OK;
 }
 

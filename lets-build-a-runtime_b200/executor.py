@@ -70,6 +70,7 @@ def load_library(path: str | Path | None = None) -> ctypes.CDLL:
         "rt_reset_plans": ([], i), "rt_synchronize": ([], i), "rt_stream": ([], vp),
         "rt_fusion_report": ([ctypes.POINTER(COpNode), i, ctypes.POINTER(ctypes.c_int)], i),
         "rt_protect": ([vp, sz], i), "rt_unprotect_all": ([], i),
+        "rt_release": ([ctypes.POINTER(COpNode), i], i), "rt_plan_count": ([], i),
         "rt_last_error": ([], i), "rt_last_error_message": ([], ctypes.c_char_p),
         "rt_clear_error": ([], None),
     }
@@ -120,12 +121,64 @@ class RunProfile:
         return "\n".join(lines)
 
 
-class CudaCompiledExecutor:
-    """Compiled executor whose one C-ABI call runs the graph on a B200."""
+class ConstantPool:
+    """Device-resident constants shared by several executors.
 
-    def __init__(self, profile: bool = False, device: int = 0, lib_path=None) -> None:
+    The reference re-plans and re-compiles for every new dynamic-shape binding
+    (``Session.rebind``, runtime/session.py:187-207) while the weight buffers
+    stay the same numpy arrays (``resolve_graph`` shares them,
+    runtime/ops.py:589-613).  Executors compiled against one pool upload each
+    such array once: entries are keyed by the host array (data address, size,
+    dtype) and hold a reference to it, so the address cannot be reused while
+    the entry lives.  Like ``rt_mark_constant``, it assumes constants are not
+    modified in place afterwards; ``clear()`` drops every entry.
+    """
+
+    def __init__(self, device: int = 0, lib_path=None) -> None:
         self._lib = load_library(lib_path)
         check(self._lib, self._lib.rt_init(device), "rt_init")
+        self._entries: dict[tuple, tuple[int, np.ndarray]] = {}
+        self.uploads = 0
+
+    def get(self, arr: np.ndarray) -> int:
+        arr = np.ascontiguousarray(arr)
+        key = (arr.__array_interface__["data"][0], arr.nbytes, arr.dtype.str)
+        hit = self._entries.get(key)
+        if hit is not None:
+            return hit[0]
+        lib = self._lib
+        ptr = lib.rt_alloc(max(arr.nbytes, 1))
+        if not ptr:
+            check(lib, lib.rt_last_error() or 9, f"rt_alloc({arr.nbytes})")
+        check(lib, lib.rt_upload(ptr, arr.ctypes.data, arr.nbytes), "upload constant")
+        check(lib, lib.rt_mark_constant(ptr, arr.nbytes), "mark constant")
+        self._entries[key] = (ptr, arr)
+        self.uploads += 1
+        return ptr
+
+    def __len__(self) -> int:
+        return len(self._entries)
+
+    def clear(self) -> None:
+        if self._entries:
+            self._lib.rt_synchronize()
+        for ptr, _ in self._entries.values():
+            self._lib.rt_free(ptr)
+        self._entries.clear()
+
+
+class CudaCompiledExecutor:
+    """Compiled executor whose one C-ABI call runs the graph on a B200.
+
+    ``constants``: an optional :class:`ConstantPool` shared with other
+    executors (dynamic-shape bindings of one model); without one, the
+    executor owns its constants."""
+
+    def __init__(self, profile: bool = False, device: int = 0, lib_path=None,
+                 constants: ConstantPool | None = None) -> None:
+        self._lib = load_library(lib_path)
+        check(self._lib, self._lib.rt_init(device), "rt_init")
+        self._pool = constants
         self._profile = profile
         self._last_profile: RunProfile | None = None
         self._device_allocs: list[int] = []
@@ -153,6 +206,9 @@ class CudaCompiledExecutor:
             arr = np.ascontiguousarray(constants[name], dtype=spec.dtype)
             if arr.nbytes != spec.nbytes:
                 raise ValueError(f"constant {name}: {arr.nbytes} bytes, plan expects {spec.nbytes}")
+            if self._pool is not None:
+                self._const_ptr[name] = self._pool.get(arr)
+                continue
             ptr = self._alloc(arr.nbytes)
             check(lib, lib.rt_upload(ptr, arr.ctypes.data, arr.nbytes), f"upload {name}")
             check(lib, lib.rt_mark_constant(ptr, arr.nbytes), f"mark {name}")
@@ -287,7 +343,8 @@ class CudaCompiledExecutor:
         lib = self._lib
         if self._device_allocs or self._host_allocs:
             lib.rt_synchronize()
-            lib.rt_reset_plans()
+            if self._nodes is not None:   # this graph's plan only; other executors keep theirs
+                lib.rt_release(self._nodes, self._n_nodes)
         for p in self._device_allocs:
             lib.rt_free(p)
         for p in self._host_allocs:

@@ -56,6 +56,7 @@ import runtime.executor.compiled as ref_compiled            # noqa: E402
 from runtime.exporter import export_model                   # noqa: E402
 from runtime.passes import run_pipeline                     # noqa: E402
 from runtime.planner import plan as ref_plan                # noqa: E402
+from runtime.ops import resolve_graph                       # noqa: E402
 
 REF_LIB = ctypes.CDLL(str(REPO / "oracle" / "_ref" / "libexecutor.so"))
 REF_LIB.execute.argtypes = [ctypes.POINTER(ref_common.COpNode), ctypes.c_int]
@@ -231,6 +232,38 @@ def build(name, spec):
     del ex, graph, model
 
 
+DYN_SEQ = (64, 128, 200, 384)
+
+
+def build_dynamic():
+    """One causal block exported ONCE with a symbolic sequence length S
+    (the reference's dynamic-shape path, tests/test_dynamic_shapes.py), then
+    ``resolve_graph`` + ``plan`` per binding: dyn_s<S>.json share constant
+    names and shapes, as the reference's rebind shares weight arrays."""
+    torch.manual_seed(0)
+    model = CustomBlock(256, 4, 1024, True).eval()
+    x = torch.randn(1, 32, 256)
+    graph = export_model(model, (x,), dynamic_dims={"S": [("x", 1)]})
+    run_pipeline(graph)
+    shapes = None
+    for S in DYN_SEQ:
+        t0 = time.time()
+        resolved = resolve_graph(graph, {"S": S})
+        ep = ref_plan(resolved)
+        name = f"dyn_s{S}"
+        meta = {"config": name, "batch": 1, "seq_len": S, "d_model": 256, "bindings": {"S": S},
+                "generator": "tests/golden/make_programs.py"}
+        prog = program_from_plan(ep, name, meta)
+        ex = _check_against_reference_compile(prog, ep, resolved)
+        cs = {n: (c.shape, c.dtype) for n, c in prog.constants.items()}
+        assert shapes is None or cs == shapes, "constants differ between bindings"
+        shapes = cs
+        prog.save(HERE / f"{name}.json")
+        print(f"{name}: {len(prog.nodes)} nodes, arena {prog.arena_size/2**20:.1f} MiB, "
+              f"{time.time()-t0:.1f}s", flush=True)
+        del ex
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", nargs="*")
@@ -239,6 +272,8 @@ def main():
         if args.only and not any(name.startswith(o) for o in args.only):
             continue
         build(name, spec)
+    if not args.only or any(o.startswith("dyn") for o in args.only):
+        build_dynamic()
 
 
 if __name__ == "__main__":
