@@ -30,9 +30,12 @@
 // The tensor core's fp32 accumulation does not round like IEEE adds, and its
 // error grows with the number of MMAs summed into one accumulator (measured
 // on B200: 1.5e-3 max abs at K=16384 with one accumulator per tile).  So each
-// tile's K is accumulated in TMEM in chunks (128 by default) and the chunk
-// sums are added in fp32 registers on the CUDA cores: error stays at the
-// level of OpenBLAS sgemm (1.6e-5 at K=16384) at no measurable cost.
+// tile's K is accumulated in TMEM in chunks (256 by default) and the chunk
+// sums are added in fp32 registers on the CUDA cores.  Measured max error
+// against fp64, per sqrt(K), unit-variance operands, K = 768..16384: 4.8e-6
+// (chunk 128), 7.2e-6 (256), 1.1e-5 (384), 1.9e-5 (768) -- numpy's fp32
+// sgemm: 2.2e-6; a longer chunk means fewer accumulator hand-offs to the
+// epilogue (GPT-2 body: 1.50 ms at 128, 1.45 ms at 256).
 //
 // Kernel: persistent, one CTA per SM, 320 threads in three roles:
 //   warp 0     TMA producer: per K-block, four tile loads (A plane 0/1,
@@ -769,13 +772,17 @@ Status make_tmap(CUtensorMap* m, const float* base, int64_t K, int64_t rows, int
     return Status::ok();
 }
 
-// K accumulated per TMEM chunk (see the file comment).  RT_GEMM_KCHUNK (a
-// multiple of 32) overrides the default of 128.
+// K accumulated per TMEM chunk (see the file comment): 256 for the cross-
+// term scheme, 128 for 3xTF32 (three accumulating MMAs per K step instead of
+// two: its error at 256 exceeds the cross scheme's at 256).  RT_GEMM_KCHUNK
+// (a multiple of 32) overrides both.
+bool cross_scheme();
 int k_chunk() {
     static int v = [] {
+        const int dflt = cross_scheme() ? 256 : 128;
         const char* e = getenv("RT_GEMM_KCHUNK");
-        int k = e ? atoi(e) : 128;
-        if (k < 32 || k % 32) k = 128;
+        int k = e ? atoi(e) : dflt;
+        if (k < 32 || k % 32) k = dflt;
         return k;
     }();
     return v;
@@ -1002,7 +1009,8 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
         prm.splits = 2;
         RT_CUDA_CHECK(cudaMemsetAsync(prm.c, 0, (size_t)p.batches * p.M * p.N * 4, st));
     }
-    prm.kb_split = ((prm.n_chunks + prm.splits - 1) / prm.splits) * prm.kb_per_chunk;
+    // equal halves of the K blocks (each split accumulates its own TMEM chunks)
+    prm.kb_split = (prm.k_blocks + prm.splits - 1) / prm.splits;
     prm.total_items = prm.total_tiles * prm.splits;
     prm.err = kernel_error_flag();
     const int grid = prm.total_items < workers ? prm.total_items : workers;
