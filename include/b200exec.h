@@ -158,7 +158,8 @@ int rt_unprotect_all(void);
  * attention node launched with strided operands, 3 for a GEMM that applies a
  * folded activation and/or writes the split A operand of a later GEMM in its
  * epilogue, 4 for a GEMM whose A operand arrives that way (no split pass),
- * 0 otherwise.  Returns the number of folded nodes.  Host only: needs no
+ * 5 for the last node of a folded RMSNorm + rotary-embedding chain (it runs
+ * the fused kernel), 0 otherwise.  Returns the number of folded nodes.  Host only: needs no
  * device and no rt_init.  RT_FUSE=0 turns all fusion off. */
 int rt_fusion_report(const OpNode* nodes, int n_nodes, int* flags);
 

@@ -143,14 +143,18 @@ struct Analysis {
     std::vector<std::vector<Range>> reads;
     std::vector<Range> writes;
 
-    // `gone`: nodes already folded away (they neither read nor write)
-    explicit Analysis(const std::vector<OpNode>& ns, const std::vector<bool>* gone = nullptr)
+    // `gone`: nodes already folded away (they neither read nor write);
+    // `reads_of`: nodes that now run a fused kernel reading other ranges
+    explicit Analysis(const std::vector<OpNode>& ns, const std::vector<bool>* gone = nullptr,
+                      const std::vector<std::pair<int, std::vector<Range>>>* reads_of = nullptr)
         : nodes(ns), reads(ns.size()), writes(ns.size()) {
         for (size_t i = 0; i < ns.size(); i++) {
             if (gone && (*gone)[i]) continue;
             read_ranges(ns[i], reads[i]);
             writes[i] = write_range(ns[i]);
         }
+        if (reads_of)
+            for (auto& ro : *reads_of) reads[ro.first] = ro.second;
     }
     int last_writer(Range r, int before) const {
         for (int j = before - 1; j >= 0; j--)
@@ -486,6 +490,183 @@ void plan_bias_folds(const std::vector<OpNode>& nodes, const std::vector<Range>&
     }
 }
 
+
+// Rotary fold: the exporter's per-head RMSNorm + rotary embedding (Qwen3),
+//   Y -(SLICE)-> [B,S,H*D] -> RMSNORM(w, rows of D) -> TRANSPOSE -> X [B,H,S,D]
+//   m1 = MUL(X, cos[1,1,S,D]);  x1 = SLICE(X, 0, D/2);  x2 = SLICE(X, D/2, D/2)
+//   n2 = NEG(x2);  c = CAT(n2, x1);  m2 = MUL(c, sin);  out = ADD(m1, m2)
+// runs as one kernel at the ADD (norm_rope_kernel).  Conditions: the chain
+// is exactly this; every intermediate output is read by chain members only
+// (and is not a graph output); Y, w, cos and sin are not written between the
+// chain's first node and the ADD; the ADD's output does not overlap them.
+struct RopeMatch {
+    int add = -1;
+    std::vector<int> chain;        // every node of the chain but the ADD
+    RopeFold rp{};
+    std::vector<Range> reads;      // what the fused kernel reads
+    int first = -1;
+};
+
+int writer_of(const Analysis& an, const void* p, size_t bytes, int before) {
+    return an.last_writer(rng(p, bytes), before);
+}
+
+bool rope_chain(const Analysis& an, int a, RopeMatch& m) {
+    const std::vector<OpNode>& N = an.nodes;
+    const OpNode& ad = N[a];
+    if (ad.op != RT_OP_ADD || ad.extra[0] != 1 || ad.n_dims != 4 || ad.elem_size != 4) return false;
+    const int64_t B = ad.out_shape[0], H = ad.out_shape[1], S = ad.out_shape[2], D = ad.out_shape[3];
+    if (D != 64 && D != 128) return false;
+    const size_t bytes = (size_t)(B * H * S * D) * 4, half = bytes / 2;
+    // the two MULs, in either input order
+    int w0 = writer_of(an, ad.inputs[0], bytes, a), w1 = writer_of(an, ad.inputs[1], bytes, a);
+    if (w0 < 0 || w1 < 0) return false;
+    auto is_bmul = [&](int k) {
+        const OpNode& x = N[k];
+        return x.op == RT_OP_MUL && x.extra[0] == 2 && x.extra[1] == 4 && x.n_dims == 4 &&
+               x.out_shape[0] == B && x.out_shape[1] == H && x.out_shape[2] == S && x.out_shape[3] == D &&
+               x.extra[2] == H * S * D && x.extra[3] == S * D && x.extra[4] == D && x.extra[5] == 1 &&
+               x.extra[6] == 0 && x.extra[7] == 0 && x.extra[9] == 1 && x.extra[8] > 0;
+    };
+    if (!is_bmul(w0) || !is_bmul(w1)) return false;
+    // m2 is the MUL whose first input comes from the CAT
+    int m1 = w0, m2 = w1;
+    int cat = writer_of(an, N[m2].inputs[0], bytes, m2);
+    if (cat < 0 || N[cat].op != RT_OP_CAT) {
+        std::swap(m1, m2);
+        cat = writer_of(an, N[m2].inputs[0], bytes, m2);
+        if (cat < 0 || N[cat].op != RT_OP_CAT) return false;
+    }
+    if (N[m1].output != ad.inputs[0] && N[m1].output != ad.inputs[1]) return false;
+    const OpNode& ct = N[cat];
+    if (ct.n_inputs != 2 || ct.extra[0] != 3 || ct.extra[1] != D / 2 || ct.extra[2] != D / 2 || ct.n_dims != 4 ||
+        ct.output != N[m2].inputs[0])
+        return false;
+    const int neg = writer_of(an, ct.inputs[0], half, cat);
+    if (neg < 0 || N[neg].op != RT_OP_NEG || N[neg].output != ct.inputs[0]) return false;
+    const int x2 = writer_of(an, N[neg].inputs[0], half, neg);
+    const int x1 = writer_of(an, ct.inputs[1], half, cat);
+    auto is_half_slice = [&](int k, int start, const void* out) {
+        if (k < 0) return false;
+        const OpNode& x = N[k];
+        return x.op == RT_OP_SLICE && x.elem_size == 4 && x.output == out && x.extra[0] == B * H * S &&
+               x.extra[1] == D && x.extra[2] == start && x.extra[3] == D / 2 && x.extra[4] == 1;
+    };
+    if (!is_half_slice(x2, (int)(D / 2), N[neg].inputs[0]) || !is_half_slice(x1, 0, ct.inputs[1])) return false;
+    const void* X = N[m1].inputs[0];
+    if (N[x1].inputs[0] != X || N[x2].inputs[0] != X) return false;
+    const int tr = writer_of(an, X, bytes, std::min(m1, std::min(x1, x2)));
+    if (tr < 0) return false;
+    const OpNode& t = N[tr];
+    if (t.op != RT_OP_TRANSPOSE || t.output != X || t.n_dims != 4 || t.extra[0] != B || t.extra[1] != S ||
+        t.extra[2] != 1 || t.extra[3] != H || t.extra[4] != D)
+        return false;
+    const int rn = writer_of(an, t.inputs[0], bytes, tr);
+    if (rn < 0) return false;
+    const OpNode& r = N[rn];
+    if (r.op != RT_OP_RMSNORM || r.output != t.inputs[0] || last_dim(r) != D || r.elem_size != 4) return false;
+    // Y: the RMSNORM input, or the projection a last-dim SLICE took it from
+    const float* y = static_cast<const float*>(r.inputs[0]);
+    int64_t y_ss = H * D, y_sb = S * H * D;
+    Range ysrc = rng(r.inputs[0], bytes);
+    int first = rn;
+    std::vector<int> chain = {rn, tr, m1, x1, x2, neg, cat, m2};
+    const int sl = writer_of(an, r.inputs[0], bytes, rn);
+    if (sl >= 0 && N[sl].op == RT_OP_SLICE && N[sl].output == r.inputs[0] && N[sl].elem_size == 4 &&
+        N[sl].extra[0] == B * S && N[sl].extra[3] == H * D && N[sl].extra[4] == 1) {
+        const int64_t W = N[sl].extra[1];
+        y = static_cast<const float*>(N[sl].inputs[0]) + N[sl].extra[2];
+        y_ss = W;
+        y_sb = S * W;
+        ysrc = rng(N[sl].inputs[0], (size_t)(B * S * W) * 4);
+        first = sl;
+        chain.push_back(sl);
+    }
+    if (!aligned_view(y, y_sb, y_ss, D)) return false;
+    const int64_t cs_ss = N[m1].extra[8];
+    if (N[m2].extra[8] != cs_ss) return false;
+    m.add = a;
+    m.chain = chain;
+    m.first = first;
+    m.rp = RopeFold{y, y_sb, y_ss, static_cast<const float*>(r.inputs[1]), extra_float(r, 0),
+                    static_cast<const float*>(N[m1].inputs[1]), static_cast<const float*>(N[m2].inputs[1]), cs_ss,
+                    static_cast<float*>(ad.output), (int)B, (int)H, (int)S, (int)D};
+    const size_t cs_bytes = (size_t)((S - 1) * cs_ss + D) * 4;
+    m.reads = {ysrc, rng(r.inputs[1], (size_t)D * 4), rng(N[m1].inputs[1], cs_bytes), rng(N[m2].inputs[1], cs_bytes)};
+    return true;
+}
+
+bool rope_valid(const Analysis& an, const RopeMatch& m, const std::vector<Range>& protect) {
+    std::vector<bool> in_chain(an.nodes.size(), false);
+    for (int k : m.chain) in_chain[k] = true;
+    in_chain[m.add] = true;
+    // No reader outside the chain, and no graph output, may see a value a
+    // folded chain node would have written: walking back from each such read
+    // over earlier writers of the range, a folded node must not come before
+    // a kept writer that covers the range.
+    auto covers = [](Range w, Range x) { return w.lo <= x.lo && x.hi <= w.hi; };
+    auto sees_folded = [&](Range x, int before) {
+        for (int i = before - 1; i >= m.first; i--) {
+            if (!overlaps(an.writes[i], x)) continue;
+            if (in_chain[i] && i != m.add) return true;
+            if (covers(an.writes[i], x)) return false;
+        }
+        return false;
+    };
+    for (int j = m.first + 1; j < (int)an.nodes.size(); j++) {
+        if (in_chain[j]) continue;
+        for (const Range& x : an.reads[j])
+            if (sees_folded(x, j)) {
+                if (dbg()) fprintf(stderr, "[fusion]   rotary: node %d reads a folded value\n", j);
+                return false;
+            }
+    }
+    for (const Range& pr : protect)
+        if (sees_folded(pr, (int)an.nodes.size())) {
+            if (dbg()) fprintf(stderr, "[fusion]   rotary: a graph output holds a folded value\n");
+            return false;
+        }
+    // sources intact from the chain's start to the ADD; output clear of them
+    for (int j = m.first + 1; j < m.add; j++)
+        if (!in_chain[j])
+            for (const Range& src : m.reads)
+                if (overlaps(an.writes[j], src)) {
+                    if (dbg()) fprintf(stderr, "[fusion]   rotary: source written by node %d\n", j);
+                    return false;
+                }
+    for (const Range& src : m.reads)
+        if (overlaps(an.writes[m.add], src)) {
+            if (dbg()) fprintf(stderr, "[fusion]   rotary: output overlaps a source\n");
+            return false;
+        }
+    return true;
+}
+
+void plan_rope_folds(const std::vector<OpNode>& nodes, const std::vector<Range>& protect,
+                     std::vector<PlanItem>& items, std::vector<bool>& gone,
+                     std::vector<std::pair<int, std::vector<Range>>>& reads_of) {
+    Analysis an(nodes, &gone);
+    for (int a = 0; a < (int)nodes.size(); a++) {
+        if (gone[a]) continue;
+        RopeMatch m;
+        if (!rope_chain(an, a, m)) continue;
+        bool clash = false;
+        for (int k : m.chain) clash |= gone[k];
+        if (clash || !rope_valid(an, m, protect)) {
+            if (dbg()) fprintf(stderr, "[fusion] rotary chain ending at %d: not folded\n", a);
+            continue;
+        }
+        for (int k : m.chain) {
+            items[k].skip = true;
+            gone[k] = true;
+        }
+        items[a].rope = true;
+        items[a].rp = m.rp;
+        reads_of.push_back({a, m.reads});
+        if (dbg()) fprintf(stderr, "[fusion] rotary chain of %zu nodes folded into node %d\n", m.chain.size() + 1, a);
+    }
+}
+
 // GEMM epilogue fusion on the schedule left by layout fusion:
 //   GEMM g -> GELU u: g applies the GELU and writes u's output; u is skipped.
 //   ... -> GEMM k reading u's output as its A operand: g writes k's split A
@@ -581,8 +762,12 @@ std::vector<PlanItem> plan_fusions(const std::vector<OpNode>& nodes,
     protect.push_back(nodes.empty() ? Range{} : write_range(nodes.back()));
     std::vector<bool> gone(nodes.size(), false);
     BiasPlan local_bp;
-    if (fusion_enabled()) plan_bias_folds(nodes, protect, items, gone, bias_plan ? bias_plan : &local_bp);
-    Analysis an(nodes, &gone);
+    std::vector<std::pair<int, std::vector<Range>>> reads_of;
+    if (fusion_enabled()) {
+        plan_bias_folds(nodes, protect, items, gone, bias_plan ? bias_plan : &local_bp);
+        plan_rope_folds(nodes, protect, items, gone, reads_of);
+    }
+    Analysis an(nodes, &gone, &reads_of);
     // candidates per attention node, most ambitious first
     std::vector<std::vector<Proposal>> cands;
     for (size_t a = 0; a < nodes.size(); a++) {

@@ -284,4 +284,70 @@ Status launch_reduce(const OpNode& nd, cudaStream_t st, int* launches) {
     return Status::ok();
 }
 
+namespace {
+
+// One warp per (b, s, h) row of D = 32 * VPT elements (warps in (b, s, h)
+// order: consecutive warps read consecutive heads of one position).  The
+// RMSNorm arithmetic is the warp-per-row path of row_kernel (same lane
+// mapping, same sum order); the rotation pairs element d with d +- D/2,
+// which lives VPT*16 elements = 16 lanes away.  Products and the sum are
+// rounded as the separate MUL / NEG / CAT / ADD nodes would round them.
+template <int VPT>
+__global__ void __launch_bounds__(256) norm_rope_kernel(RopeFold r) {
+    constexpr int D = 32 * VPT;
+    const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int64_t rows = (int64_t)r.B * r.S * r.H;
+    if (row >= rows) return;
+    const int lane = threadIdx.x & 31;
+    const int h = (int)(row % r.H);
+    const int64_t bs = row / r.H;
+    const int s = (int)(bs % r.S), b = (int)(bs / r.S);
+    const float* yr = r.y + b * r.y_sb + (int64_t)s * r.y_ss + (int64_t)h * D + lane * VPT;
+    float v[VPT];
+    if (VPT == 4) {
+        const float4 t = *reinterpret_cast<const float4*>(yr);
+        v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+    } else {
+#pragma unroll
+        for (int i = 0; i < VPT; i++) v[i] = yr[i];
+    }
+    float q = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VPT; i++) q += v[i] * v[i];
+    const float ss = warp_sum(q);
+    const float scale = 1.0f / sqrtf(ss / D + r.eps);
+    const float* cr = r.cos + (int64_t)s * r.cs_ss + lane * VPT;
+    const float* sr = r.sin + (int64_t)s * r.cs_ss + lane * VPT;
+    const bool first_half = lane < 16;
+    float o[VPT];
+#pragma unroll
+    for (int i = 0; i < VPT; i++) {
+        const float n = v[i] * scale * r.w[lane * VPT + i];
+        const float partner = __shfl_xor_sync(0xffffffffu, n, 16);
+        const float rot = first_half ? -partner : partner;
+        o[i] = __fadd_rn(__fmul_rn(n, cr[i]), __fmul_rn(rot, sr[i]));
+    }
+    float* orow = r.out + (((int64_t)b * r.H + h) * r.S + s) * D + lane * VPT;
+    if (VPT == 4) {
+        *reinterpret_cast<float4*>(orow) = make_float4(o[0], o[1], o[2], o[3]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < VPT; i++) orow[i] = o[i];
+    }
+}
+
+}  // namespace
+
+Status launch_norm_rope(const RopeFold& r, cudaStream_t st, int* launches) {
+    const int64_t rows = (int64_t)r.B * r.S * r.H;
+    if (rows == 0) return Status::ok();
+    const unsigned grid = (unsigned)((rows + 7) / 8);
+    if (r.D == 128) norm_rope_kernel<4><<<grid, 256, 0, st>>>(r);
+    else if (r.D == 64) norm_rope_kernel<2><<<grid, 256, 0, st>>>(r);
+    else return Status::err(RT_ERR_UNSUPPORTED, "norm_rope: head_dim must be 64 or 128");
+    RT_LAUNCH_CHECK();
+    *launches += 1;
+    return Status::ok();
+}
+
 }  // namespace rt

@@ -110,6 +110,24 @@ bool attention_default_views(const OpNode& n, AttnViews* v);
 bool attention_takes_views(const OpNode& n);
 Status launch_attention_views(const OpNode& n, const AttnViews& v, cudaStream_t st, Workspace ws, int* launches);
 
+// Fused per-head RMSNorm + rotary embedding + head split (fusion.cu folds the
+// exporter's SLICE -> RMSNORM -> TRANSPOSE -> MUL(cos) / SLICE,SLICE,NEG,CAT,
+// MUL(sin) -> ADD chain into the final ADD):
+//   out[b,h,s,:] = rope(rmsnorm(y[b,s,h,:]) * w), rope(x) = x*cos[s] + rot(x)*sin[s],
+//   rot(x)[d] = d < D/2 ? -x[d+D/2] : x[d-D/2].
+struct RopeFold {
+    const float* y;              // element (b, s, h, d) at y + b*y_sb + s*y_ss + h*D + d
+    int64_t y_sb, y_ss;
+    const float* w;              // RMSNorm weight [D]
+    float eps;
+    const float* cos;            // row s at cos + s*cs_ss (likewise sin)
+    const float* sin;
+    int64_t cs_ss;
+    float* out;                  // [B, H, S, D] contiguous
+    int B, H, S, D;
+};
+Status launch_norm_rope(const RopeFold& r, cudaStream_t st, int* launches);
+
 // Per-node outcome of the plan-time layout fusion (fusion.cu).
 struct PlanItem {
     bool skip = false;    // producer folded into its consumer: not launched
@@ -127,6 +145,8 @@ struct PlanItem {
     int64_t presplit_off = -1;     // consumer: A planes are already here; no split pre-pass
     int64_t carry_plane_bytes = 0; // bytes of one plane
     int64_t epi_bias_off = -1;     // GEMM adds this merged bias (byte offset into the plan's bias buffer)
+    bool rope = false;             // this (ADD) node launches the fused norm + rotary kernel instead
+    RopeFold rp{};
 };
 // Merged biases of bias folds: a plan-owned device buffer of `bytes`, zeroed
 // in `zero` ranges then filled by device-to-device `copies` (dst offset, src, bytes).

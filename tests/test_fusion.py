@@ -132,10 +132,22 @@ def test_protected_output_blocks_folding():
         lib.rt_unprotect_all()
 
 
-@pytest.mark.parametrize("name,gelus", [("qwen3_b8", 0), ("7b_b8", 1), ("toy", 0)])
+def test_qwen3_rotary_chains_fold():
+    """Qwen3 q/k paths: SLICE -> RMSNORM -> TRANSPOSE -> rotary (MUL, SLICE, SLICE,
+    NEG, CAT, MUL, ADD) run as one fused kernel at the ADD: 9 of 10 nodes per
+    chain skipped, 2 chains per layer."""
+    prog = Program.load(GOLDEN / "qwen3_b8.json")
+    arr, _ = bind(prog)
+    n, flags = report(prog, arr)
+    assert n == 36
+    assert [prog.nodes[i].op for i, f in enumerate(flags) if f == 5] == [OP["ADD"]] * 4
+    folded = sorted({prog.nodes[i].op for i, f in enumerate(flags) if f == 1})
+    assert folded == sorted({OP[k] for k in ("SLICE", "RMSNORM", "TRANSPOSE", "MUL", "NEG", "CAT")})
+
+
+@pytest.mark.parametrize("name,gelus", [("7b_b8", 1), ("toy", 0)])
 def test_no_layout_folding_where_the_chain_does_not_match(name, gelus):
-    """Qwen3 (RMSNorm/RoPE between the projections and attention) keeps its
-    layout copies.  The custom blocks' bias ADD after the QKV slice folds into
+    """The custom blocks' bias ADD after the QKV slice folds into
     the merged GEMM only when the bias is a registered constant -- not in this
     host-only report (tests/test_gpu_fusion.py covers it on the device) -- so
     here only the MLP GELU folds into its GEMM (not in the toy block, whose
