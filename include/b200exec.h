@@ -124,6 +124,21 @@ int rt_execute(const OpNode* nodes, int n_nodes, int flags);
  * device->host copies, all on the library stream, then one synchronise. */
 int rt_execute_io(const OpNode* nodes, int n_nodes,
                   const RtCopy* h2d, int n_in, const RtCopy* d2h, int n_out);
+/* One batch as independent chunks (no counterpart in the reference): chunk c
+ * runs its own node array -- the graph planned for that chunk's rows, with
+ * its own arena -- between its host-to-device and device-to-host copies, on
+ * its own stream, so one chunk's copies overlap another chunk's kernels.
+ * Only valid when the chunks share no intermediate memory and the model
+ * treats batch rows independently.  Synchronous, like rt_execute_io. */
+typedef struct RtChunk {
+    const OpNode* nodes;
+    int n_nodes;
+    const RtCopy* h2d;
+    int n_in;
+    const RtCopy* d2h;
+    int n_out;
+} RtChunk;
+int rt_execute_chunks(const RtChunk* chunks, int n_chunks);
 /* Validate and prepare (capture) without running. */
 int rt_prepare(const OpNode* nodes, int n_nodes);
 /* Kernel launches one execute of this node array issues (after prepare). */

@@ -62,6 +62,7 @@ struct State {
     std::vector<std::pair<uintptr_t, size_t>> protect;   // graph outputs (rt_protect)
     volatile int* kerr_host = nullptr;   // host-mapped error word written by kernels
     int* kerr_dev = nullptr;
+    std::vector<cudaStream_t> chunk_streams;   // rt_execute_chunks, created on first use
 };
 
 State& S() {
@@ -615,6 +616,11 @@ int rt_destroy(void) {
     RT_GUARD;
     if (!S().initialized) return RT_OK;
     cudaStreamSynchronize(S().stream);
+    for (cudaStream_t st : S().chunk_streams) {
+        cudaStreamSynchronize(st);
+        cudaStreamDestroy(st);
+    }
+    S().chunk_streams.clear();
     clear_plans();
     for (auto& kv : S().allocs) {
         if (kv.second.host) cudaFreeHost(reinterpret_cast<void*>(kv.first));
@@ -794,6 +800,53 @@ int rt_execute_io(const OpNode* nodes, int n, const RtCopy* h2d, int n_in, const
     }
     cudaError_t e = cudaStreamSynchronize(st);
     if (e != cudaSuccess) return fail(RT_ERR_CUDA, std::string("execute_io: ") + cudaGetErrorString(e));
+    if (int k = take_kernel_error())
+        return fail(RT_ERR_KERNEL_TIMEOUT, "a kernel abandoned a bounded wait, code " + std::to_string(k));
+    return RT_OK;
+}
+
+int rt_execute_chunks(const RtChunk* chunks, int n_chunks) {
+    RT_GUARD;
+    RT_NEED_INIT;
+    if (n_chunks < 0 || (n_chunks > 0 && !chunks)) return fail(RT_ERR_ARGUMENT, "rt_execute_chunks: bad chunk array");
+    std::vector<Plan*> plans((size_t)n_chunks);
+    for (int c = 0; c < n_chunks; c++) {   // plan (and capture) before anything is enqueued
+        Status s = get_plan(chunks[c].nodes, chunks[c].n_nodes, &plans[c]);
+        if (!s.good()) {
+            s.msg = "chunk " + std::to_string(c) + ": " + s.msg;
+            return fail(s);
+        }
+    }
+    auto& ss = S().chunk_streams;
+    while ((int)ss.size() < n_chunks) {
+        cudaStream_t st = nullptr;
+        if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess)
+            return fail(RT_ERR_CUDA, "rt_execute_chunks: stream creation failed");
+        ss.push_back(st);
+    }
+    // work already queued on the library stream comes first
+    cudaEvent_t ready = nullptr;
+    if (cudaEventCreateWithFlags(&ready, cudaEventDisableTiming) != cudaSuccess)
+        return fail(RT_ERR_CUDA, "rt_execute_chunks: event creation failed");
+    cudaEventRecord(ready, S().stream);
+    cudaError_t e = cudaSuccess;
+    for (int c = 0; c < n_chunks && e == cudaSuccess; c++) {
+        cudaStream_t st = ss[c];
+        e = cudaStreamWaitEvent(st, ready, 0);
+        for (int i = 0; i < chunks[c].n_in && e == cudaSuccess; i++)
+            e = cudaMemcpyAsync(chunks[c].h2d[i].dst, chunks[c].h2d[i].src, chunks[c].h2d[i].bytes,
+                                cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess && plans[c]->exec) e = cudaGraphLaunch(plans[c]->exec, st);
+        for (int i = 0; i < chunks[c].n_out && e == cudaSuccess; i++)
+            e = cudaMemcpyAsync(chunks[c].d2h[i].dst, chunks[c].d2h[i].src, chunks[c].d2h[i].bytes,
+                                cudaMemcpyDeviceToHost, st);
+    }
+    for (int c = 0; c < n_chunks; c++) {
+        cudaError_t e2 = cudaStreamSynchronize(ss[c]);
+        if (e == cudaSuccess) e = e2;
+    }
+    cudaEventDestroy(ready);
+    if (e != cudaSuccess) return fail(RT_ERR_CUDA, std::string("execute_chunks: ") + cudaGetErrorString(e));
     if (int k = take_kernel_error())
         return fail(RT_ERR_KERNEL_TIMEOUT, "a kernel abandoned a bounded wait, code " + std::to_string(k));
     return RT_OK;
