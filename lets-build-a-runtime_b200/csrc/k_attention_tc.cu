@@ -76,6 +76,7 @@ struct AttnTcParams {
     int64_t o_sb, o_sh, o_ss;   // same for O
     int H;                      // query heads per batch element
     int S, group, causal, n_qblocks;
+    int heads_fast;             // grid (BH, q blocks) instead of (q blocks, BH)
     float scale;
     int* err;
 };
@@ -204,8 +205,13 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
     }
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int bh = blockIdx.y;
-    const int qb = p.causal ? p.n_qblocks - 1 - (int)blockIdx.x : (int)blockIdx.x;   // long rows first
+    // Launch order.  Heads fastest: under a causal mask every head's longest
+    // query blocks start before any shorter one (longest first), which evens
+    // out the last wave -- when all heads' packed K/V stays in L2.  Otherwise
+    // query blocks fastest, so the CTAs in flight share few heads' K/V.
+    const int bh = p.heads_fast ? (int)blockIdx.x : (int)blockIdx.y;
+    const int qi = p.heads_fast ? (int)blockIdx.y : (int)blockIdx.x;
+    const int qb = p.causal ? p.n_qblocks - 1 - qi : qi;
     const int q0 = qb * BQ;
     const int bhkv = bh / p.group;
     const int kv_len = p.causal ? min(p.S, q0 + BQ) : p.S;
@@ -521,7 +527,8 @@ bool attn_cross() {
 
 template <int D>
 Status launch_tc(const AttnTcParams& prm, int BH, cudaStream_t st) {
-    dim3 grid((unsigned)prm.n_qblocks, (unsigned)BH);
+    dim3 grid = prm.heads_fast ? dim3((unsigned)BH, (unsigned)prm.n_qblocks)
+                               : dim3((unsigned)prm.n_qblocks, (unsigned)BH);
     if (attn_cross())
         attn_tc_kernel<D, true><<<grid, ATHREADS, AttnTcCfg<D>::SMEM, st>>>(prm);
     else
@@ -535,7 +542,7 @@ Status launch_tc(const AttnTcParams& prm, int BH, cudaStream_t st) {
 // Shapes this kernel takes: no custom mask, head_dim 64 or 128, at least one
 // full 128-query block.
 bool attention_tc_applicable(int64_t S, int D, bool has_mask, int64_t BH) {
-    return !has_mask && (D == 64 || D == 128) && S >= 128 && BH <= 65535 && S < (1 << 30);
+    return !has_mask && (D == 64 || D == 128) && S >= 128 && BH <= 65535 && (S + BQ - 1) / BQ <= 65535;
 }
 
 size_t attention_tc_workspace(int64_t BHkv, int64_t S, int D) {
@@ -588,6 +595,7 @@ Status launch_attention_tc(const AttnViews& vw, int64_t BH, int64_t S, int D, in
     prm.group = group;
     prm.causal = causal;
     prm.n_qblocks = (int)((S + BQ - 1) / BQ);
+    prm.heads_fast = attention_tc_workspace(BHkv, S, D) <= ((size_t)512 << 20) ? 1 : 0;
     prm.scale = 1.0f / sqrtf((float)D);
     prm.err = kernel_error_flag();
     *launches += 1;
