@@ -174,7 +174,8 @@ int rt_unprotect_all(void);
  * folded activation and/or writes the split A operand of a later GEMM in its
  * epilogue, 4 for a GEMM whose A operand arrives that way (no split pass),
  * 5 for the last node of a folded RMSNorm + rotary-embedding chain (it runs
- * the fused kernel), 0 otherwise.  Returns the number of folded nodes.  Host only: needs no
+ * the fused kernel), 6 for a gated activation reading its inputs through
+ * strided views of the tensor its folded SLICEs took them from, 0 otherwise.  Returns the number of folded nodes.  Host only: needs no
  * device and no rt_init.  RT_FUSE=0 turns all fusion off. */
 int rt_fusion_report(const OpNode* nodes, int n_nodes, int* flags);
 

@@ -667,6 +667,74 @@ void plan_rope_folds(const std::vector<OpNode>& nodes, const std::vector<Range>&
     }
 }
 
+
+// Gated-MLP fold: GATED_ACT whose x and/or up input is a last-dim SLICE of a
+// wider tensor (Qwen3: the merged gate/up projection) reads that tensor through
+// a row-strided view; the SLICE is not launched.  Conditions as for the
+// rotary fold: nobody outside (slice -> GATED_ACT) sees the slice's output, and
+// the sliced tensor is not written before the GATED_ACT, whose output does not
+// overlap it.
+void plan_gated_folds(const std::vector<OpNode>& nodes, const std::vector<Range>& protect,
+                      std::vector<PlanItem>& items, std::vector<bool>& gone,
+                      std::vector<std::pair<int, std::vector<Range>>>& reads_of) {
+    Analysis an(nodes, &gone);
+    const int n = (int)nodes.size();
+    for (int g = 0; g < n; g++) {
+        const OpNode& ga = nodes[g];
+        if (gone[g] || ga.op != RT_OP_GATED_ACT || ga.elem_size != 4) continue;
+        const int64_t N = last_dim(ga), rows = N ? total_elements(ga) / N : 0;
+        const int slot_x = 0, slot_up = ga.extra[0] ? 2 : 1;
+        GatedViews v{static_cast<const float*>(ga.inputs[slot_x]), static_cast<const float*>(ga.inputs[slot_up]), N, N};
+        std::vector<int> folded;
+        std::vector<Range> reads = an.reads[g];
+        for (int slot : {slot_x, slot_up}) {
+            const size_t bytes = (size_t)(rows * N) * 4;
+            const int sl = an.last_writer(rng(ga.inputs[slot], bytes), g);
+            if (sl < 0 || gone[sl]) continue;
+            const OpNode& s = nodes[sl];
+            if (s.op != RT_OP_SLICE || s.output != ga.inputs[slot] || s.elem_size != 4 || s.extra[0] != rows ||
+                s.extra[3] != N || s.extra[4] != 1)
+                continue;
+            const int64_t W = s.extra[1];
+            const float* base = static_cast<const float*>(s.inputs[0]) + s.extra[2];
+            const Range src = rng(s.inputs[0], (size_t)(rows * W) * 4);
+            // the slice's output: read by this GATED_ACT only (walking back from every other reader)
+            bool ok = true;
+            const Range out = an.writes[sl];
+            auto covers = [](Range w, Range x) { return w.lo <= x.lo && x.hi <= w.hi; };
+            auto sees_slice = [&](Range x, int before) {
+                for (int i = before - 1; i >= sl; i--) {
+                    if (!overlaps(an.writes[i], x)) continue;
+                    if (i == sl) return true;
+                    if (covers(an.writes[i], x)) return false;
+                }
+                return false;
+            };
+            for (int j = sl + 1; j < n && ok; j++) {
+                if (j == g) continue;
+                for (const Range& x : an.reads[j]) ok &= !(overlaps(x, out) && sees_slice(x, j));
+            }
+            for (const Range& pr : protect) ok &= !(overlaps(pr, out) && sees_slice(pr, n));
+            for (int j = sl + 1; j < g && ok; j++) ok &= !overlaps(an.writes[j], src);
+            ok &= !overlaps(an.writes[g], src);
+            if (!ok) continue;
+            (slot == slot_x ? v.x : v.up) = base;
+            (slot == slot_x ? v.x_ld : v.up_ld) = W;
+            folded.push_back(sl);
+            reads.push_back(src);
+        }
+        if (folded.empty()) continue;
+        for (int sl : folded) {
+            items[sl].skip = true;
+            gone[sl] = true;
+        }
+        items[g].gated = true;
+        items[g].gv = v;
+        reads_of.push_back({g, reads});
+        if (dbg()) fprintf(stderr, "[fusion] gated activation %d reads %zu slice(s) through views\n", g, folded.size());
+    }
+}
+
 // GEMM epilogue fusion on the schedule left by layout fusion:
 //   GEMM g -> GELU u: g applies the GELU and writes u's output; u is skipped.
 //   ... -> GEMM k reading u's output as its A operand: g writes k's split A
@@ -766,6 +834,7 @@ std::vector<PlanItem> plan_fusions(const std::vector<OpNode>& nodes,
     if (fusion_enabled()) {
         plan_bias_folds(nodes, protect, items, gone, bias_plan ? bias_plan : &local_bp);
         plan_rope_folds(nodes, protect, items, gone, reads_of);
+        plan_gated_folds(nodes, protect, items, gone, reads_of);
     }
     Analysis an(nodes, &gone, &reads_of);
     // candidates per attention node, most ambitious first

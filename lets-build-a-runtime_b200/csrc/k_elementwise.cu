@@ -309,4 +309,56 @@ Status launch_elementwise(const OpNode& nd, cudaStream_t st, int* launches) {
     }
 }
 
+namespace {
+
+// gated activation with row-strided inputs (see GatedViews); 4 columns per
+// thread when every row start is 16-byte aligned.
+template <int ACT>
+__global__ void gated_views_kernel(GatedViews v, const float* __restrict__ bias, float* __restrict__ y,
+                                   int64_t rows, int64_t N, bool vec) {
+    const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    if (vec) {
+        const int64_t per_row = N >> 2, total = rows * per_row;
+        for (int64_t i = tid; i < total; i += stride) {
+            const int64_t r = i / per_row, c = (i - r * per_row) << 2;
+            float4 a = *reinterpret_cast<const float4*>(v.x + r * v.x_ld + c);
+            const float4 u = *reinterpret_cast<const float4*>(v.up + r * v.up_ld + c);
+            if (bias) {
+                const float4 bb = *reinterpret_cast<const float4*>(bias + c);
+                a.x += bb.x; a.y += bb.y; a.z += bb.z; a.w += bb.w;
+            }
+            float4 o;
+            o.x = (ACT == 0 ? silu(a.x) : gelu_tanh(a.x)) * u.x;
+            o.y = (ACT == 0 ? silu(a.y) : gelu_tanh(a.y)) * u.y;
+            o.z = (ACT == 0 ? silu(a.z) : gelu_tanh(a.z)) * u.z;
+            o.w = (ACT == 0 ? silu(a.w) : gelu_tanh(a.w)) * u.w;
+            *reinterpret_cast<float4*>(y + r * N + c) = o;
+        }
+    } else {
+        for (int64_t i = tid; i < rows * N; i += stride) {
+            const int64_t r = i / N, c = i - r * N;
+            const float a = v.x[r * v.x_ld + c] + (bias ? bias[c] : 0.0f);
+            y[i] = (ACT == 0 ? silu(a) : gelu_tanh(a)) * v.up[r * v.up_ld + c];
+        }
+    }
+}
+
+}  // namespace
+
+Status launch_gated_views(const OpNode& nd, const GatedViews& v, cudaStream_t st, int* launches) {
+    const int has_bias = nd.extra[0], act = nd.extra[1];
+    const float* bias = has_bias ? (const float*)nd.inputs[1] : nullptr;
+    float* y = (float*)nd.output;
+    const int64_t N = last_dim(nd), rows = N ? total_elements(nd) / N : 0;
+    const bool vec = N % 4 == 0 && v.x_ld % 4 == 0 && v.up_ld % 4 == 0 && aligned16(v.x) && aligned16(v.up) &&
+                     aligned16(y) && (!bias || aligned16(bias));
+    const int grid = grid_for(vec ? rows * N / 4 : rows * N, kThreads);
+    if (act == 0) gated_views_kernel<0><<<grid, kThreads, 0, st>>>(v, bias, y, rows, N, vec);
+    else gated_views_kernel<1><<<grid, kThreads, 0, st>>>(v, bias, y, rows, N, vec);
+    RT_LAUNCH_CHECK();
+    *launches += 1;
+    return Status::ok();
+}
+
 }  // namespace rt

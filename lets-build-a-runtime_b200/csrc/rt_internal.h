@@ -128,6 +128,15 @@ struct RopeFold {
 };
 Status launch_norm_rope(const RopeFold& r, cudaStream_t st, int* launches);
 
+// GATED_ACT reading x / up through row-strided views (a folded last-dim SLICE
+// each): element (r, c) of x at x + r*x_ld + c; the output stays contiguous.
+struct GatedViews {
+    const float* x;
+    const float* up;
+    int64_t x_ld, up_ld;
+};
+Status launch_gated_views(const OpNode& n, const GatedViews& v, cudaStream_t st, int* launches);
+
 // Per-node outcome of the plan-time layout fusion (fusion.cu).
 struct PlanItem {
     bool skip = false;    // producer folded into its consumer: not launched
@@ -147,6 +156,8 @@ struct PlanItem {
     int64_t epi_bias_off = -1;     // GEMM adds this merged bias (byte offset into the plan's bias buffer)
     bool rope = false;             // this (ADD) node launches the fused norm + rotary kernel instead
     RopeFold rp{};
+    bool gated = false;            // this GATED_ACT reads its inputs through `gv`
+    GatedViews gv{};
 };
 // Merged biases of bias folds: a plan-owned device buffer of `bytes`, zeroed
 // in `zero` ranges then filled by device-to-device `copies` (dst offset, src, bytes).

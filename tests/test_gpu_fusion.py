@@ -116,3 +116,27 @@ def test_custom_block_bias_fold_unlocks_layout_fusion(name, gpu_executor_factory
     if ref is not None:
         for k in got:
             np.testing.assert_allclose(got[k], ref[k], atol=1e-4, rtol=1e-3)
+
+
+@pytest.mark.parametrize("act,bias", [(0, False), (1, True)])
+def test_gated_activation_reads_slices_through_views(act, bias, gpu_executor_factory):
+    """SLICE(M, 0, F), SLICE(M, F, F) -> GATED_ACT: the slices fold into row-strided
+    views of M (flag 6 on the GATED_ACT, 1 on both slices); result vs the oracle."""
+    R, F = 300, 520
+    rng = np.random.default_rng(11)
+    stored = {"m": rng.standard_normal((R, 2 * F), dtype=np.float32),
+              "b": rng.standard_normal(F).astype(np.float32)}
+    consts = {k: ConstSpec(k, v.shape, "float32", {"kind": "stored"}) for k, v in stored.items()}
+    A = lambda off: Ref("arena", None, off)
+    sz = R * F * 4
+    nodes = [ProgNode(OP["SLICE"], [Ref("const", "m", 0)], A(0), [R, F], 4, [R, 2 * F, 0, F, 1]),
+             ProgNode(OP["SLICE"], [Ref("const", "m", 0)], A(sz), [R, F], 4, [R, 2 * F, F, F, 1])]
+    ins = [A(0), Ref("const", "b", 0), A(sz)] if bias else [A(0), A(sz)]
+    nodes.append(ProgNode(OP["GATED_ACT"], ins, A(2 * sz), [R, F], 4, [int(bias), act]))
+    prog = Program("gated", {}, 3 * sz, {}, {"y": {"shape": [R, F], "dtype": "float32", "ref": A(2 * sz)}},
+                   consts, nodes, stored)
+    ex = gpu_executor_factory(prog, dict(stored))
+    assert flags_of(ex, prog) == [1, 1, 6]
+    got = ex.run({})["y"]
+    ref = oracle.run_program("restated", prog, dict(stored), {})["y"]
+    np.testing.assert_allclose(got, ref, rtol=2e-6, atol=2e-6)
