@@ -172,10 +172,13 @@ int rt_unprotect_all(void);
  * SLICE / TRANSPOSE around attention, a GELU after a GEMM), 2 for an
  * attention node launched with strided operands, 3 for a GEMM that applies a
  * folded activation and/or writes the split A operand of a later GEMM in its
- * epilogue, 4 for a GEMM whose A operand arrives that way (no split pass),
+ * epilogue (its A may arrive split as well), 4 for a GEMM whose only fusion is
+ * that its A operand arrives split (no split pass),
  * 5 for the last node of a folded RMSNorm + rotary-embedding chain (it runs
  * the fused kernel), 6 for a gated activation reading its inputs through
- * strided views of the tensor its folded SLICEs took them from, 0 otherwise.  Returns the number of folded nodes.  Host only: needs no
+ * strided views of the tensor its folded SLICEs took them from, 8 for a
+ * LAYERNORM / RMSNORM writing the split A operand of the GEMM reading it
+ * (that GEMM: 4), 0 otherwise.  Returns the number of folded nodes.  Host only: needs no
  * device and no rt_init.  RT_FUSE=0 turns all fusion off. */
 int rt_fusion_report(const OpNode* nodes, int n_nodes, int* flags);
 

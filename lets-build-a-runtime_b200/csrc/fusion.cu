@@ -17,7 +17,8 @@
 // Every node's read and write extents are computed from its op, shape and
 // extras; a node whose read extent is not known blocks any fusion across it.
 // RT_FUSE=0 disables the pass (RT_FUSE_GEMM=0 only the GEMM epilogue chains;
-// RT_FUSE_HANDOFF=1 turns on the split-operand hand-off between GEMMs).
+// RT_FUSE_HANDOFF=1 turns on the split-operand hand-off between GEMMs;
+// RT_FUSE_NORM_SPLIT=0 turns off the norm -> GEMM split-operand hand-off).
 #include <stdio.h>
 #include <stdlib.h>
 
@@ -735,6 +736,25 @@ void plan_gated_folds(const std::vector<OpNode>& nodes, const std::vector<Range>
     }
 }
 
+// Regions of the plan's carry buffer (split operands handed from a producer
+// to the GEMM that reads them): a region is reused once the span of the
+// hand-off that last used it (producer .. consumer node) is over.
+struct CarryAlloc {
+    struct Region { int64_t off, size; int busy_until; };
+    std::vector<Region> regions;
+    int64_t total = 0;
+    int64_t take(int start, int end, int64_t size) {
+        for (Region& r : regions)
+            if (r.busy_until < start && r.size >= size) {
+                r.busy_until = end;
+                return r.off;
+            }
+        regions.push_back({total, size, end});
+        total += size;
+        return regions.back().off;
+    }
+};
+
 // GEMM epilogue fusion on the schedule left by layout fusion:
 //   GEMM g -> GELU u: g applies the GELU and writes u's output; u is skipped.
 //   ... -> GEMM k reading u's output as its A operand: g writes k's split A
@@ -747,7 +767,7 @@ void plan_gated_folds(const std::vector<OpNode>& nodes, const std::vector<Range>
 // hand-off, u's output is read by k alone, through A only.  Chains share one
 // carry buffer, so their [g, k] spans must not overlap.
 void plan_gemm_chains(const Analysis& an, const Effective& e, std::vector<PlanItem>& items,
-                      const std::vector<Range>& protect, size_t* carry_bytes) {
+                      const std::vector<Range>& protect, CarryAlloc& carry_alloc) {
     const int n = (int)an.nodes.size();
     auto is_gemm = [](const OpNode& x) { return x.op == RT_OP_MATMUL || x.op == RT_OP_MATMUL_ADD; };
     auto next_reader = [&](int from, Range r) {
@@ -758,8 +778,6 @@ void plan_gemm_chains(const Analysis& an, const Effective& e, std::vector<PlanIt
         }
         return -1;
     };
-    size_t carry = 0;
-    int carry_busy_until = -1;
     for (int g = 0; g < n; g++) {
         const OpNode& gn = an.nodes[g];
         if (e.skipped[g] || items[g].views || !is_gemm(gn) || !gemm_fusable(gn)) continue;
@@ -786,7 +804,7 @@ void plan_gemm_chains(const Analysis& an, const Effective& e, std::vector<PlanIt
         const char* hv = getenv("RT_FUSE_HANDOFF");   // read per plan
         if (!(hv && hv[0] == '1')) continue;
         const int k = next_reader(u, U);
-        if (k < 0 || g <= carry_busy_until) continue;
+        if (k < 0) continue;
         const OpNode& kn = an.nodes[k];
         if (!is_gemm(kn) || kn.inputs[0] != un.output || items[k].redirect_slot >= 0 || !gemm_fusable(kn)) continue;
         GemmProblem gp, kp;
@@ -798,15 +816,56 @@ void plan_gemm_chains(const Analysis& an, const Effective& e, std::vector<PlanIt
         for (size_t i = 1; i < e.reads[k].size(); i++) only_a &= !overlaps(e.reads[k][i], U);
         if (!only_a || !dead_output(an, u, k, protect)) continue;
         const int64_t plane = (int64_t)(((U.hi - U.lo) + 255) & ~(uintptr_t)255);
-        items[g].carry_off = 0;
+        const int64_t off = carry_alloc.take(g, k, 2 * plane);
+        items[g].carry_off = off;
         items[g].carry_plane_bytes = plane;
-        items[k].presplit_off = 0;
+        items[k].presplit_off = off;
         items[k].carry_plane_bytes = plane;
-        if ((size_t)(2 * plane) > carry) carry = (size_t)(2 * plane);
-        carry_busy_until = k;
         if (dbg()) fprintf(stderr, "[fusion] gemm %d: writes the split A operand of gemm %d\n", g, k);
     }
-    if (carry_bytes) *carry_bytes = carry;
+}
+
+// Norm -> GEMM hand-off: a LAYERNORM / RMSNORM whose output is read only as
+// the A operand of the next GEMM writes that GEMM's split planes (the same
+// bits its split pass would produce) into the carry buffer, and the GEMM
+// skips its split pass: 8 bytes written per element instead of 4, and the
+// pass's 12 bytes and a launch saved.
+void plan_norm_handoffs(const Analysis& an, const Effective& e, std::vector<PlanItem>& items,
+                        const std::vector<Range>& protect, CarryAlloc& carry_alloc) {
+    const int n = (int)an.nodes.size();
+    for (int m = 0; m < n; m++) {
+        const OpNode& nm = an.nodes[m];
+        PlanItem& it = items[m];
+        if (e.skipped[m] || it.skip || it.rope || it.gated || it.redirect_slot >= 0 || !norm_planes_supported(nm))
+            continue;
+        const Range L = an.writes[m];
+        int k = -1;
+        for (int j = m + 1; j < n; j++) {
+            if (e.skipped[j] || items[j].skip) continue;
+            if (eff_reads(e, j, L)) { k = j; break; }
+            if (overlaps(e.writes[j], L)) break;
+        }
+        if (k < 0) continue;
+        const OpNode& kn = an.nodes[k];
+        PlanItem& ki = items[k];
+        if ((kn.op != RT_OP_MATMUL && kn.op != RT_OP_MATMUL_ADD) || kn.inputs[0] != nm.output ||
+            ki.presplit_off >= 0 || ki.redirect_slot >= 0 || !gemm_fusable(kn))
+            continue;
+        GemmProblem kp;
+        if (!decode_gemm(kn, &kp).good() || (uintptr_t)(kp.batches * kp.M * kp.K * 4) != L.hi - L.lo ||
+            kp.K != last_dim(nm))
+            continue;
+        bool only_a = true;
+        for (size_t i = 1; i < e.reads[k].size(); i++) only_a &= !overlaps(e.reads[k][i], L);
+        if (!only_a || !dead_output(an, m, k, protect)) continue;
+        const int64_t plane = (int64_t)(((L.hi - L.lo) + 255) & ~(uintptr_t)255);
+        const int64_t off = carry_alloc.take(m, k, 2 * plane);
+        it.norm_planes_off = off;
+        it.carry_plane_bytes = plane;
+        ki.presplit_off = off;
+        ki.carry_plane_bytes = plane;
+        if (dbg()) fprintf(stderr, "[fusion] norm %d: writes the split A operand of gemm %d\n", m, k);
+    }
 }
 
 bool fusion_enabled() {
@@ -894,7 +953,14 @@ std::vector<PlanItem> plan_fusions(const std::vector<OpNode>& nodes,
                 const char* v = getenv("RT_FUSE_GEMM");
                 return !(v && v[0] == '0');
             }();
-            if (fusion_enabled() && gemm_chains) plan_gemm_chains(an, e, items, protect, carry_bytes);
+            CarryAlloc carry_alloc;
+            if (fusion_enabled() && gemm_chains) plan_gemm_chains(an, e, items, protect, carry_alloc);
+            static const bool norm_handoff = [] {
+                const char* v = getenv("RT_FUSE_NORM_SPLIT");
+                return !(v && v[0] == '0');
+            }();
+            if (fusion_enabled() && norm_handoff) plan_norm_handoffs(an, e, items, protect, carry_alloc);
+            if (carry_bytes) *carry_bytes = (size_t)carry_alloc.total;
             break;
         }
         pick[owner[bad]]++;

@@ -891,6 +891,8 @@ size_t round256(size_t b) { return (b + 255) & ~(size_t)255; }
 
 }  // namespace
 
+bool gemm_cross_scheme() { return cross_scheme(); }
+
 bool tc_gemm_applicable(const GemmProblem& p) {
     if (p.K % 4 != 0) return false;                                  // TMA row stride: 16-byte multiple
     if ((double)p.M * p.N * p.K < 8.0 * 1024 * 1024) return false;   // tiny: the CUDA-core GEMM wins

@@ -13,6 +13,7 @@
 // the row fits 32 lanes x VPT floats, one 256-thread CTA per row up to 4096
 // floats, and a three-pass loop beyond that.  Reductions are warp shuffles
 // (+ shared memory across warps); everything accumulates in fp32.
+#include "dev_math.h"
 #include "rt_internal.h"
 
 namespace rt {
@@ -47,12 +48,15 @@ __device__ __forceinline__ float block_reduce(float v, float* sh) {
 // One row per group of THREADS threads (a warp or the whole CTA); each
 // thread holds VPT floats of the row: elements (v*THREADS + t)*4 .. +3 when
 // VEC (C % 4 == 0, aligned), else elements v*THREADS + t.
-template <int KIND, int THREADS, int VPT, bool VEC>
+// PLANES: the row is a GEMM's A operand; write its split planes (hi to y,
+// plane 1 to `x1`, mode `cross`) instead of the fp32 row.
+template <int KIND, int THREADS, int VPT, bool VEC, bool PLANES = false>
 __global__ void __launch_bounds__(256) row_kernel(const float* __restrict__ x,
                                                   const float* __restrict__ g,
                                                   const float* __restrict__ b,
                                                   float* __restrict__ y, int64_t rows, int C,
-                                                  float eps) {
+                                                  float eps, uint16_t* __restrict__ x1 = nullptr,
+                                                  bool cross = true) {
     __shared__ float sh[32];
     constexpr int GROUPS = 256 / THREADS;  // rows handled by one CTA at a time
     int group = threadIdx.x / THREADS;
@@ -132,7 +136,8 @@ __global__ void __launch_bounds__(256) row_kernel(const float* __restrict__ x,
                         else val = val / scale;
                         op[k] = val + shift;
                     }
-                    *reinterpret_cast<float4*>(yr + c) = o;
+                    if (PLANES) store_split4(yr, x1 + row * C * 2, c, C, o, cross);
+                    else *reinterpret_cast<float4*>(yr + c) = o;
                 }
             }
         } else {
@@ -188,14 +193,25 @@ __global__ void __launch_bounds__(256) row_loop_kernel(const float* __restrict__
     }
 }
 
-template <int KIND, int THREADS, int VPT, bool VEC>
+template <int KIND, int THREADS, int VPT, bool VEC, bool PLANES = false>
 void launch_rows(const float* x, const float* g, const float* b, float* y, int64_t rows, int C,
-                 float eps, cudaStream_t st) {
+                 float eps, cudaStream_t st, uint16_t* x1 = nullptr, bool cross = true) {
     constexpr int GROUPS = 256 / THREADS;
     int64_t blocks = (rows + GROUPS - 1) / GROUPS;
     int64_t cap = (int64_t)g_num_sms * (THREADS == 32 ? 8 : 4) * 4;
     int grid = (int)(blocks < cap ? blocks : cap);
-    row_kernel<KIND, THREADS, VPT, VEC><<<grid, 256, 0, st>>>(x, g, b, y, rows, C, eps);
+    row_kernel<KIND, THREADS, VPT, VEC, PLANES><<<grid, 256, 0, st>>>(x, g, b, y, rows, C, eps, x1, cross);
+}
+
+template <int KIND>
+void run_rows_planes(const float* x, const float* g, const float* b, float* hi, uint16_t* x1, int64_t rows,
+                     int C, float eps, bool cross, cudaStream_t st) {
+    if (C <= 128) launch_rows<KIND, 32, 4, true, true>(x, g, b, hi, rows, C, eps, st, x1, cross);
+    else if (C <= 256) launch_rows<KIND, 32, 8, true, true>(x, g, b, hi, rows, C, eps, st, x1, cross);
+    else if (C <= 512) launch_rows<KIND, 32, 16, true, true>(x, g, b, hi, rows, C, eps, st, x1, cross);
+    else if (C <= 1024) launch_rows<KIND, 32, 32, true, true>(x, g, b, hi, rows, C, eps, st, x1, cross);
+    else if (C <= 2048) launch_rows<KIND, 256, 8, true, true>(x, g, b, hi, rows, C, eps, st, x1, cross);
+    else launch_rows<KIND, 256, 16, true, true>(x, g, b, hi, rows, C, eps, st, x1, cross);
 }
 
 template <int KIND>
@@ -345,6 +361,31 @@ Status launch_norm_rope(const RopeFold& r, cudaStream_t st, int* launches) {
     if (r.D == 128) norm_rope_kernel<4><<<grid, 256, 0, st>>>(r);
     else if (r.D == 64) norm_rope_kernel<2><<<grid, 256, 0, st>>>(r);
     else return Status::err(RT_ERR_UNSUPPORTED, "norm_rope: head_dim must be 64 or 128");
+    RT_LAUNCH_CHECK();
+    *launches += 1;
+    return Status::ok();
+}
+
+// LAYERNORM / RMSNORM whose output only feeds a GEMM's A operand: the rows
+// go out as that GEMM's split planes (see row_kernel PLANES).
+bool norm_planes_supported(const OpNode& n) {
+    const int C = last_dim(n);
+    return (n.op == RT_OP_LAYERNORM || n.op == RT_OP_RMSNORM) && n.elem_size == 4 && C > 0 && C <= 4096 &&
+           C % 4 == 0 && aligned16(n.inputs[0]);
+}
+
+Status launch_norm_planes(const OpNode& nd, float* hi, void* x1, bool cross, cudaStream_t st, int* launches) {
+    const int C = last_dim(nd);
+    const int64_t rows = total_elements(nd) / C;
+    if (rows == 0) return Status::ok();
+    const float* x = (const float*)nd.inputs[0];
+    const float eps = extra_float(nd, 0);
+    uint16_t* xp = static_cast<uint16_t*>(x1);
+    if (nd.op == RT_OP_LAYERNORM)
+        run_rows_planes<N_LAYER>(x, (const float*)nd.inputs[1], (const float*)nd.inputs[2], hi, xp, rows, C, eps,
+                                 cross, st);
+    else
+        run_rows_planes<N_RMS>(x, (const float*)nd.inputs[1], nullptr, hi, xp, rows, C, eps, cross, st);
     RT_LAUNCH_CHECK();
     *launches += 1;
     return Status::ok();

@@ -91,6 +91,9 @@ Status launch_gemm(const OpNode& n, cudaStream_t st, Workspace ws, int* launches
                    const GemmFusion* f = nullptr);
 // Whether a GEMM node can take a GemmFusion (tensor-core path).
 bool gemm_fusable(const OpNode& n);
+bool gemm_cross_scheme();   // plane 1 of split operands: cross (true) or lo (false)
+bool norm_planes_supported(const OpNode& n);
+Status launch_norm_planes(const OpNode& n, float* hi, void* x1, bool cross, cudaStream_t st, int* launches);
 Status prepare_gemm(const OpNode& n, cudaStream_t st);   // constant splits, before capture
 
 Status launch_attention(const OpNode& n, cudaStream_t st, Workspace ws, int* launches);
@@ -153,6 +156,7 @@ struct PlanItem {
     int64_t carry_off = -1;        // producer: write A planes here (byte offset into the carry buffer)
     int64_t presplit_off = -1;     // consumer: A planes are already here; no split pre-pass
     int64_t carry_plane_bytes = 0; // bytes of one plane
+    int64_t norm_planes_off = -1;  // LAYERNORM / RMSNORM: write the consumer GEMM's split A planes here
     int64_t epi_bias_off = -1;     // GEMM adds this merged bias (byte offset into the plan's bias buffer)
     bool rope = false;             // this (ADD) node launches the fused norm + rotary kernel instead
     RopeFold rp{};

@@ -291,6 +291,11 @@ Status launch_item(Plan& p, size_t i, cudaStream_t st, int* launches) {
         if (p.items[i].skip) return Status::ok();
         if (p.items[i].rope) return launch_norm_rope(p.items[i].rp, st, launches);
         if (p.items[i].gated) return launch_gated_views(p.nodes[i], p.items[i].gv, st, launches);
+        if (p.items[i].norm_planes_off >= 0) {
+            char* base = p.carry + p.items[i].norm_planes_off;
+            return launch_norm_planes(p.nodes[i], reinterpret_cast<float*>(base), base + p.items[i].carry_plane_bytes,
+                                      gemm_cross_scheme(), st, launches);
+        }
         if (p.items[i].views) return launch_attention_views(p.nodes[i], p.items[i].attn, st, ws, launches);
         const PlanItem& it = p.items[i];
         if (it.epi_act || it.epi_out || it.carry_off >= 0 || it.presplit_off >= 0 || it.epi_bias_off >= 0) {
@@ -969,9 +974,10 @@ int rt_fusion_report(const OpNode* nodes, int n, int* skipped) {
                 : it.views ? 2
                 : it.rope ? 5
                 : it.gated ? 6
-                : it.presplit_off >= 0 ? 4
+                : it.norm_planes_off >= 0 ? 8
                 : (it.epi_act || it.epi_out || it.carry_off >= 0 || it.epi_bias_off >= 0) ? 3
-                                                                    : 0;
+                : it.presplit_off >= 0 ? 4
+                                        : 0;
         if (skipped) skipped[i] = f;
         count += items[i].skip;
     }

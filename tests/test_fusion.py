@@ -157,3 +157,18 @@ def test_no_layout_folding_where_the_chain_does_not_match(name, gelus):
     n, flags = report(prog, arr)
     assert n == gelus
     assert all(prog.nodes[i].op == OP["GELU"] for i, f in enumerate(flags) if f == 1)
+
+
+@pytest.mark.parametrize("name,pairs", [("gpt2_b8", 4), ("7b_b8", 2), ("qwen3_b8", 4)])
+def test_norms_write_the_split_operand_of_their_gemm(name, pairs):
+    """A LAYERNORM / RMSNORM read only as the next GEMM's A operand writes that
+    GEMM's split planes (flag 8); the GEMM skips its split pass (flag 4)."""
+    prog = Program.load(GOLDEN / f"{name}.json")
+    arr, _ = bind(prog)
+    _, flags = report(prog, arr)
+    producers = [i for i, f in enumerate(flags) if f == 8]
+    assert len(producers) == pairs
+    assert all(prog.nodes[i].op in (OP["LAYERNORM"], OP["RMSNORM"]) for i in producers)
+    # the consumer: 4, or 3 when it also folds an activation into its epilogue
+    assert all(flags[i + 1] in (3, 4) and prog.nodes[i + 1].op in (OP["MATMUL"], OP["MATMUL_ADD"])
+               for i in producers)
