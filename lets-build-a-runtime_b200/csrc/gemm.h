@@ -37,4 +37,8 @@ Status split_operand(const float* x, float* hi, float* lo, int64_t batches, int6
 // fp32 3-D tensor map {d0 (contiguous), d1, d2}, box {box0, box1, 1}, swizzle 0/64/128 bytes.
 Status encode_tmap_f32_3d(CUtensorMap* m, const float* base, int64_t d0, int64_t d1, int64_t d2, int box0,
                           int box1, int swizzle_bytes);
+// fp32 tensor map of any rank (<= 5) with explicit byte strides of dims 1..rank-1
+// (multiples of 16; dim 0 contiguous); out-of-range elements read as zero.
+Status encode_tmap_f32(CUtensorMap* m, const float* base, int rank, const int64_t* dims,
+                       const int64_t* byte_strides, const int* box, int swizzle_bytes);
 }  // namespace rt

@@ -12,22 +12,28 @@
 //
 // Tiles are 128 queries x 128 keys, so every score MMA is M=128 x N=128
 // (narrower MMAs are dominated by per-instruction cost on this hardware).
-// One CTA = 128 queries of one (batch, head); 320 threads:
-//   warp 0     producer: streams 32 KiB chunks through a shared-memory ring in
-//              exactly the order the MMAs consume them -- K_0, K_1, V_0, K_2,
-//              V_1, ... (K tile = D/32 chunks of 32 features x 128 keys, V^T
-//              tile = chunks of 32 or 64 keys x D), each chunk one contiguous
-//              bulk copy of a pre-packed, pre-swizzled image;
+// Work item = 128 queries of one (batch, head); the grid is persistent (one
+// CTA per SM looping over items) so that one item's prologue (Q load, first
+// scores) and epilogue (last P.V, O store) overlap its neighbours'.  384
+// threads:
+//   warp 0     producer: per item, the raw Q rows (one bulk copy per row, once
+//              the previous item's score MMAs are done with the Q space), then
+//              32 KiB chunks through a shared-memory ring in exactly the order
+//              the MMAs consume them -- K_0, K_1, V_0, K_2, V_1, ... (K tile =
+//              D/32 chunks of 32 features x 128 keys, V^T tile = chunks of 32
+//              or 64 keys x D), each chunk one contiguous bulk copy of a
+//              pre-packed, pre-swizzled image;
 //   warp 1     allocates TMEM and issues the MMAs from one thread:
 //              S = Q.K^T (Q from shared memory), O_tile = P.V (P from TMEM),
 //              each as hi.hi + the cross terms;
 //              S_{j+1} runs while the softmax works on S_j;
-//   warps 2-9  two threads per query row (64 keys and D/2 output columns
+//   warps 4-11 two threads per query row (64 keys and D/2 output columns
 //              each; row maxima / sums exchanged through shared memory behind
-//              bounded mbarrier waits): stage Q hi/lo into shared memory, then
-//              per tile read S from TMEM (freeing it), mask, online softmax in
-//              log2 units, fold the previous O tile into registers, write P's
-//              two planes to TMEM.
+//              bounded mbarrier waits): split the raw Q rows into the hi /
+//              plane-1 layouts, then per tile read S from TMEM (freeing it),
+//              mask, online softmax in log2 units, fold the previous O tile
+//              into registers, write P's two planes to TMEM; after an item's
+//              last tile, stage the next item's Q before the final O fold.
 // TMEM columns: S [0,128) | P_hi [128,256) | P plane 1 [256,384) | O tile [384, 384+D).
 // Plane 1 of every operand (Q, K, V in shared memory, P in TMEM) is lo as
 // fp32, or for the cross scheme bf16 [hi | lo] (Q, P) / [lo | hi] (K, V) per
@@ -47,7 +53,13 @@ int* kernel_error_flag();
 
 namespace {
 
-constexpr int BQ = 128, BKV = 128, SOFT_WARPS = 8, ATHREADS = 64 + 32 * SOFT_WARPS;
+// Warpgroup 0: producer (warp 0), MMA issuer (warp 1), two idle warps;
+// warpgroups 1-2: the softmax.  Launched at 168 registers a thread (384 x 168
+// fit the SM's 64 Ki), then rebalanced: warpgroup 0 down to REG_CTRL, the
+// softmax up to REG_SOFT (128 x 120 + 256 x 192 = 384 x 168).
+constexpr int BQ = 128, BKV = 128, SOFT_WARPS = 8, ATHREADS = 128 + 32 * SOFT_WARPS;
+constexpr int REG_CTRL = 120, REG_SOFT = 192;
+static_assert(128 * REG_CTRL + 32 * SOFT_WARPS * REG_SOFT <= ATHREADS * 168, "register split");
 constexpr int CHUNK = 32 * 1024;                      // ring stage / packed chunk
 constexpr uint64_t WAIT_NS = 2000000000ull;
 constexpr int ERR_A_PROD = 0x201, ERR_A_MMA = 0x202, ERR_A_SOFT = 0x203, ERR_A_DRAIN = 0x204;
@@ -61,13 +73,16 @@ struct AttnTcCfg {
     static constexpr int V_CHUNKS = BKV / V_KEYS;
     static constexpr int TILE_BYTES = (K_CHUNKS + V_CHUNKS) * CHUNK;
     static constexpr int STAGES = D == 128 ? 3 : 5;
-    static constexpr int BODY = 2 * Q_BYTES + STAGES * CHUNK + 256 /*barriers*/ + 4 * BQ * 4 /*row exchange*/;
-    static constexpr int SMEM = BODY + 768;   // + alignment slack; 232448 B, the per-CTA maximum
-    static_assert(SMEM <= 232448, "shared memory budget");
+    static constexpr int BAR_BYTES = 384;                       // mbarriers, TMEM slot, flags, item ring
+    static constexpr int BODY = 2 * Q_BYTES + STAGES * CHUNK + BAR_BYTES + 4 * BQ * 4 /*row exchange*/;
+    static constexpr int SMEM = 232448;                         // the per-CTA maximum; BODY + alignment slack
+    static_assert(BODY + 512 <= SMEM, "shared memory budget");
     static_assert(COL_O + D <= 512, "TMEM budget");
 };
 
 struct AttnTcParams {
+    CUtensorMap tq;      // Q as {32-feature blocks: D, rows, heads, batch} (middle two in stride order)
+    int q_rows_dim;      // which tensor-map dim (1 or 2) runs over rows; the other over heads
     const uint8_t* kv;   // packed tiles [BHkv][n_kv][K chunks | V chunks]
     int n_kv;            // key tiles per head
     const float* q;
@@ -76,7 +91,9 @@ struct AttnTcParams {
     int64_t o_sb, o_sh, o_ss;   // same for O
     int H;                      // query heads per batch element
     int S, group, causal, n_qblocks;
-    int heads_fast;             // grid (BH, q blocks) instead of (q blocks, BH)
+    int BH, n_items;            // (batch, head) pairs; work items = BH x query blocks
+    int heads_fast;             // item order: heads fastest instead of query blocks fastest
+    int* counter;               // next item to take (zeroed by the pack kernel before each launch)
     float scale;
     int* err;
 };
@@ -112,6 +129,28 @@ __device__ __forceinline__ uint32_t bf16x2(float a, float b) {
     return r;
 }
 
+// Softmax-side conversions on the integer / FMA pipes.  The conversion
+// instructions (cvt to tf32 or bf16x2) issue on the same narrow pipe as ex2,
+// and with one exponential per score that pipe bounded the softmax.
+// tf32 (nearest, ties away) of a finite x by integer rounding of its magnitude
+// bits: the same value cvt.rna.tf32.f32 gives.
+__device__ __forceinline__ float tf32_rna_int(float x) {
+    return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
+}
+// bf16 by truncation (upper halves) of two values, `a` in the low half.  Used
+// for P's plane 1 only: the cross terms carry a relative weight of 2^-11, so
+// truncation's 2^-8 (against 2^-9 for nearest) moves a product by ~2^-19.
+__device__ __forceinline__ uint32_t bf16x2_trunc(float a, float b) {
+    return __byte_perm(__float_as_uint(a), __float_as_uint(b), 0x7632);
+}
+// 2^x with the hardware approximation (flushes results below 2^-126 to 0;
+// 2^-inf = 0, which the causal mask relies on).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // Plane 1 of four consecutive K elements x (k % 4 == 0, k = position inside a
 // 128-byte row of 32 elements) at row `row` of a swizzled [rows][128 B]
 // block: lo as fp32, or the cross layout (first = hi (A role) / lo (B role)).
@@ -130,48 +169,70 @@ __device__ __forceinline__ void put_plane1(uint8_t* blk, int row, int k, float4 
 }
 
 template <int D, bool CROSS>
-__global__ void __launch_bounds__(256) pack_kv_kernel(KvViews kv, uint8_t* __restrict__ out, int S, int n_kv) {
+__global__ void __launch_bounds__(256) pack_kv_kernel(KvViews kv, uint8_t* __restrict__ out, int S, int n_kv,
+                                                      int* counter) {
     using C = AttnTcCfg<D>;
+    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *counter = 0;   // the attention kernel's item counter
+    constexpr int PER = 32 * D / 4 / 256;   // 4-element units per thread, of K and of V
     __shared__ float sv[32][D + 1];
-    const int j = blockIdx.x, h = blockIdx.y;
-    const int k0 = j * BKV;
+    // one block = 32 keys (sub-block `sub` of key tile j): all global loads first
+    const int j = blockIdx.x >> 2, sub = blockIdx.x & 3, h = blockIdx.y;
+    const int k0 = j * BKV + sub * 32;
     uint8_t* tile = out + ((size_t)h * n_kv + j) * C::TILE_BYTES;
     const int bb = h / kv.Hkv, hh = h % kv.Hkv;
     const float* kb = kv.k + bb * kv.k_sb + hh * kv.k_sh;
     const float* vb = kv.v + bb * kv.v_sb + hh * kv.v_sh;
+    float4 xk[PER], xv[PER];
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+        const int u = threadIdx.x + i * 256, r = u / (D / 4), d = (u % (D / 4)) * 4;
+        const bool in = k0 + r < S;
+        xk[i] = in ? *reinterpret_cast<const float4*>(kb + (int64_t)(k0 + r) * kv.k_ss + d) : make_float4(0.f, 0.f, 0.f, 0.f);
+        xv[i] = in ? *reinterpret_cast<const float4*>(vb + (int64_t)(k0 + r) * kv.v_ss + d) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     // K: unit = 4 consecutive features of one key
-    for (int u = threadIdx.x; u < BKV * D / 4; u += blockDim.x) {
-        const int r = u / (D / 4), d = (u % (D / 4)) * 4;
-        float4 x = k0 + r < S ? *reinterpret_cast<const float4*>(kb + (int64_t)(k0 + r) * kv.k_ss + d)
-                              : make_float4(0.f, 0.f, 0.f, 0.f);
-        float4 hi = make_float4(tf32_round(x.x), tf32_round(x.y), tf32_round(x.z), tf32_round(x.w));
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+        const int u = threadIdx.x + i * 256, r = u / (D / 4), d = (u % (D / 4)) * 4;
+        sv[r][d] = xv[i].x; sv[r][d + 1] = xv[i].y; sv[r][d + 2] = xv[i].z; sv[r][d + 3] = xv[i].w;
+        const float4 x = xk[i];
+        const float4 hi = make_float4(tf32_round(x.x), tf32_round(x.y), tf32_round(x.z), tf32_round(x.w));
         uint8_t* kc = tile + (size_t)(d >> 5) * CHUNK;
-        *reinterpret_cast<float4*>(kc + swz(r, d & 31)) = hi;
-        put_plane1<CROSS, false>(kc + CHUNK / 2, r, d & 31, hi,
+        *reinterpret_cast<float4*>(kc + swz(sub * 32 + r, d & 31)) = hi;
+        put_plane1<CROSS, false>(kc + CHUNK / 2, sub * 32 + r, d & 31, hi,
                                  make_float4(x.x - hi.x, x.y - hi.y, x.z - hi.z, x.w - hi.w));
     }
+    __syncthreads();
     // V^T: unit = 4 consecutive keys of one feature
-    for (int kb32 = 0; kb32 < BKV; kb32 += 32) {
-        __syncthreads();
-        for (int u = threadIdx.x; u < 32 * D / 4; u += blockDim.x) {
-            const int r = u / (D / 4), d = (u % (D / 4)) * 4;
-            const int key = k0 + kb32 + r;
-            float4 x = key < S ? *reinterpret_cast<const float4*>(vb + (int64_t)key * kv.v_ss + d)
-                               : make_float4(0.f, 0.f, 0.f, 0.f);
-            sv[r][d] = x.x; sv[r][d + 1] = x.y; sv[r][d + 2] = x.z; sv[r][d + 3] = x.w;
-        }
-        __syncthreads();
-        const int vc = kb32 / C::V_KEYS, sub = (kb32 % C::V_KEYS) >> 5;
-        uint8_t* vcp = tile + (size_t)(C::K_CHUNKS + vc) * CHUNK + (size_t)sub * D * 128;
-        for (int u = threadIdx.x; u < D * 8; u += blockDim.x) {
-            const int d = u >> 3, w = (u & 7) * 4;
-            float4 x = make_float4(sv[w][d], sv[w + 1][d], sv[w + 2][d], sv[w + 3][d]);
-            float4 hi = make_float4(tf32_round(x.x), tf32_round(x.y), tf32_round(x.z), tf32_round(x.w));
-            *reinterpret_cast<float4*>(vcp + swz(d, w)) = hi;
-            put_plane1<CROSS, false>(vcp + CHUNK / 2, d, w, hi,
-                                     make_float4(x.x - hi.x, x.y - hi.y, x.z - hi.z, x.w - hi.w));
-        }
+    const int vc = (sub * 32) / C::V_KEYS, vsub = ((sub * 32) % C::V_KEYS) >> 5;
+    uint8_t* vcp = tile + (size_t)(C::K_CHUNKS + vc) * CHUNK + (size_t)vsub * D * 128;
+    for (int u = threadIdx.x; u < D * 8; u += blockDim.x) {
+        const int d = u >> 3, w = (u & 7) * 4;
+        const float4 x = make_float4(sv[w][d], sv[w + 1][d], sv[w + 2][d], sv[w + 3][d]);
+        const float4 hi = make_float4(tf32_round(x.x), tf32_round(x.y), tf32_round(x.z), tf32_round(x.w));
+        *reinterpret_cast<float4*>(vcp + swz(d, w)) = hi;
+        put_plane1<CROSS, false>(vcp + CHUNK / 2, d, w, hi,
+                                 make_float4(x.x - hi.x, x.y - hi.y, x.z - hi.z, x.w - hi.w));
     }
+}
+
+// One work item = 128 queries of one (batch, head).  The grid is persistent
+// (one CTA per SM); each CTA's producer takes the next item from a global
+// counter, so items run in their list order across the GPU as on a plain
+// grid -- longest causal blocks first, and the items in flight share few
+// heads' K/V in L2 -- with no per-CTA start-up per item.
+struct AttnItem {
+    int bh, q0, n_tiles;
+};
+
+__device__ __forceinline__ void attn_decode(const AttnTcParams& p, int L, AttnItem& it) {
+    const int bh = p.heads_fast ? L % p.BH : L / p.n_qblocks;
+    const int qi = p.heads_fast ? L / p.BH : L % p.n_qblocks;
+    const int qb = p.causal ? p.n_qblocks - 1 - qi : qi;
+    it.bh = bh;
+    it.q0 = qb * BQ;
+    const int kv_len = p.causal ? min(p.S, it.q0 + BQ) : p.S;
+    it.n_tiles = (kv_len + BKV - 1) / BKV;
 }
 
 template <int D, bool CROSS>
@@ -191,40 +252,34 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
     uint64_t* s_free = s_full + 1;
     uint64_t* p_full = s_full + 2;
     uint64_t* pv_full = s_full + 3;
-    uint64_t* q_ready = s_full + 4;
+    uint64_t* q_ready = s_full + 4;               // Q planes written (per item)
     uint64_t* drain = s_full + 5;
-    uint64_t* pair_bar = s_full + 6;              // [4 quarters][3]
-    constexpr int NBAR = 2 * STAGES + 6 + 12;
+    uint64_t* q_full = s_full + 6;                // raw Q block landed (per item)
+    uint64_t* q_free = s_full + 7;                // the item's score MMAs done: Q space reusable
+    uint64_t* pair_bar = s_full + 8;              // [4 quarters][3]
+    uint64_t* item_full = pair_bar + 12;          // [4] item ring slot written (producer -> the other roles)
+    constexpr int NBAR = 2 * STAGES + 8 + 12 + 4;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NBAR);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    int* issued = const_cast<int*>(abort_flag) + 1;    // [STAGES] phase of the last load, -1 none
-    float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);   // [2][2][128]
+    int* issued = const_cast<int*>(abort_flag) + 1;    // [STAGES + 1] phase of the last load (ring, Q), -1 none
+    volatile int* items = issued + STAGES + 1;         // [4] item ring: item r in slot r % 4, -1 = no more
+    static_assert(NBAR * 8 + 8 + 4 * (STAGES + 1) + 16 <= C::BAR_BYTES, "barrier area");
+    float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + C::BAR_BYTES);   // [2][2][128]
     if ((smem - smem_raw) + C::BODY > C::SMEM) {   // dynamic shared memory less aligned than assumed
         if (threadIdx.x == 0 && p.err) atomicCAS(p.err, 0, 0x205);
         return;
     }
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // Launch order.  Heads fastest: under a causal mask every head's longest
-    // query blocks start before any shorter one (longest first), which evens
-    // out the last wave -- when all heads' packed K/V stays in L2.  Otherwise
-    // query blocks fastest, so the CTAs in flight share few heads' K/V.
-    const int bh = p.heads_fast ? (int)blockIdx.x : (int)blockIdx.y;
-    const int qi = p.heads_fast ? (int)blockIdx.y : (int)blockIdx.x;
-    const int qb = p.causal ? p.n_qblocks - 1 - qi : qi;
-    const int q0 = qb * BQ;
-    const int bhkv = bh / p.group;
-    const int kv_len = p.causal ? min(p.S, q0 + BQ) : p.S;
-    const int n_tiles = (kv_len + BKV - 1) / BKV;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < NBAR; i++) {
             uint32_t cnt = 1;
             if (&bars[i] == s_free || &bars[i] == p_full || &bars[i] == q_ready) cnt = 32 * SOFT_WARPS;
-            if (&bars[i] >= pair_bar) cnt = 64;
+            if (&bars[i] >= pair_bar && &bars[i] < item_full) cnt = 64;
             ptx::mbar_init(&bars[i], cnt);
         }
-        for (int s = 0; s < STAGES; s++) issued[s] = -1;
+        for (int s = 0; s <= STAGES; s++) issued[s] = -1;
         *abort_flag = 0;
         ptx::fence_mbar_init();
     }
@@ -233,9 +288,23 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
     __syncthreads();
     ptx::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-
+    // Item r for the MMA / softmax roles: 1 = got it, 0 = no more items, -1 = wait abandoned.
+    // Slot r % 4 is rewritten for item r + 4 only after every role has moved past item r + 2.
+    auto take = [&](int r, AttnItem& it, int code) -> int {
+        if (!ptx::wait_bounded(&item_full[r & 3], (r >> 2) & 1, abort_flag, p.err, code, WAIT_NS)) return -1;
+        const int L = items[r & 3];
+        if (L < 0) return 0;
+        attn_decode(p, L, it);
+        return 1;
+    };
+    if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REG_CTRL));
     if (warp == 0) {
         // ---------------------------------------------------- producer
+        // Per item: the raw Q block (D/32 tensor-map loads of 128 rows x 32
+        // features, 128-byte swizzled into the hi plane's place, rows past S
+        // zero-filled; once the previous item's score MMAs are done with the
+        // Q planes), then the K/V chunks.
         if (lane == 0) {
             int stage = 0;
             uint32_t ph = 0;
@@ -252,12 +321,29 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
                     ph ^= 1;
                 }
             };
-            auto tile = [&](int j) { return p.kv + ((size_t)bhkv * p.n_kv + j) * C::TILE_BYTES; };
-            for (int c = 0; c < C::K_CHUNKS; c++) push(tile(0) + c * CHUNK);
-            for (int j = 0; j < n_tiles && ok; j++) {
-                if (j + 1 < n_tiles)
-                    for (int c = 0; c < C::K_CHUNKS; c++) push(tile(j + 1) + c * CHUNK);
-                for (int c = 0; c < C::V_CHUNKS; c++) push(tile(j) + (C::K_CHUNKS + c) * CHUNK);
+            AttnItem it;
+            for (int r = 0; ok; r++) {
+                const int L = atomicAdd(p.counter, 1);
+                items[r & 3] = L < p.n_items ? L : -1;
+                ptx::mbar_arrive(&item_full[r & 3]);
+                if (L >= p.n_items) break;
+                attn_decode(p, L, it);
+                if (r > 0 && !(ok = ptx::wait_bounded(q_free, (r - 1) & 1, abort_flag, p.err, ERR_A_PROD, WAIT_NS)))
+                    break;
+                const int h = it.bh % p.H, b = it.bh / p.H;
+                const int c1 = p.q_rows_dim == 1 ? it.q0 : h, c2 = p.q_rows_dim == 1 ? h : it.q0;
+                ptx::mbar_expect_tx(q_full, (uint32_t)C::Q_BYTES);
+                issued[STAGES] = r & 1;
+                for (int blk = 0; blk < D / 32; blk++)
+                    ptx::tma_load_4d(qh + blk * BQ * 128, &p.tq, q_full, blk * 32, c1, c2, b);
+                const uint8_t* kv = p.kv + (size_t)(it.bh / p.group) * p.n_kv * C::TILE_BYTES;
+                for (int c = 0; c < C::K_CHUNKS; c++) push(kv + c * CHUNK);
+                for (int j = 0; j < it.n_tiles && ok; j++) {
+                    if (j + 1 < it.n_tiles)
+                        for (int c = 0; c < C::K_CHUNKS; c++) push(kv + (size_t)(j + 1) * C::TILE_BYTES + c * CHUNK);
+                    for (int c = 0; c < C::V_CHUNKS; c++)
+                        push(kv + (size_t)j * C::TILE_BYTES + (C::K_CHUNKS + c) * CHUNK);
+                }
             }
         }
     } else if (warp == 1) {
@@ -269,8 +355,7 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
             constexpr uint32_t idesc_ox = ptx::idesc_bf16(BQ, D);
             int stage = 0;
             uint32_t ph = 0;
-            bool ok = ptx::wait_bounded(q_ready, 0, abort_flag, p.err, ERR_A_MMA, WAIT_NS);
-            ptx::tc_fence_after();
+            bool ok = true;
             auto pop = [&]() -> uint8_t* {
                 if (!ok) return nullptr;
                 if (!(ok = ptx::wait_bounded(&full[stage], ph, abort_flag, p.err, ERR_A_MMA, WAIT_NS)))
@@ -332,167 +417,219 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
                 }
                 if (ok) ptx::mma_commit(pv_full);
             };
-            if (ok && n_tiles > 0) issue_s();
-            for (int j = 0; j < n_tiles && ok; j++) {
-                if (j + 1 < n_tiles) {   // S_{j+1} once the softmax has read S_j out of TMEM
-                    if (!(ok = ptx::wait_bounded(s_free, j & 1, abort_flag, p.err, ERR_A_MMA, WAIT_NS))) break;
-                    ptx::tc_fence_after();
-                    issue_s();
+            // T counts tiles over all items: the per-tile barriers flip once per tile.
+            int T = 0;
+            AttnItem it;
+            for (int r = 0; ok; r++) {
+                const int got = take(r, it, ERR_A_MMA);
+                if (got <= 0) {
+                    ok = got == 0;
+                    break;
                 }
-                if (!ok) break;
-                if (!(ok = ptx::wait_bounded(p_full, j & 1, abort_flag, p.err, ERR_A_MMA, WAIT_NS))) break;
+                if (!(ok = ptx::wait_bounded(q_ready, r & 1, abort_flag, p.err, ERR_A_MMA, WAIT_NS))) break;
+                // S of the previous item's last tile read out of TMEM
+                if (T > 0 && !(ok = ptx::wait_bounded(s_free, (T - 1) & 1, abort_flag, p.err, ERR_A_MMA, WAIT_NS)))
+                    break;
                 ptx::tc_fence_after();
-                issue_pv();
+                issue_s();
+                if (ok && it.n_tiles == 1) ptx::mma_commit(q_free);
+                for (int j = 0; j < it.n_tiles && ok; j++, T++) {
+                    if (j + 1 < it.n_tiles) {   // S_{j+1} once the softmax has read S_j out of TMEM
+                        if (!(ok = ptx::wait_bounded(s_free, T & 1, abort_flag, p.err, ERR_A_MMA, WAIT_NS))) break;
+                        ptx::tc_fence_after();
+                        issue_s();
+                        if (ok && j + 2 == it.n_tiles) ptx::mma_commit(q_free);
+                    }
+                    if (!ok) break;
+                    if (!(ok = ptx::wait_bounded(p_full, T & 1, abort_flag, p.err, ERR_A_MMA, WAIT_NS))) break;
+                    ptx::tc_fence_after();
+                    issue_pv();
+                }
             }
             ptx::mma_commit(drain);
             volatile int no_abort = 0;
             ptx::wait_bounded(drain, 0, &no_abort, p.err, ERR_A_DRAIN, WAIT_NS);
         }
         __syncwarp();
+    }
     } else {
-        // ---------------------------------------------------- softmax rows (warps 2..9)
-        const int quarter = warp & 3;
-        const int half = (warp - 2) >> 2;
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REG_SOFT));
+        // ---------------------------------------------------- softmax rows (warps 4..11)
+        const int quarter = warp & 3;   // TMEM lanes 32*quarter.. are this warp's rows
+        const int half = (warp - 4) >> 2;
         const int row = quarter * 32 + lane;
-        const int q = q0 + row;
         const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
         constexpr int DH = D / 2, KH = BKV / 2;   // per-thread output columns / score columns
-        const float* qrow = p.q + (bh / p.H) * p.q_sb + (bh % p.H) * p.q_sh + (int64_t)(q < p.S ? q : 0) * p.q_ss;
         const float sl2 = p.scale * 1.4426950408889634f;   // scores in log2 units: exp(x) = 2^(x log2 e)
         auto pair_sync = [&](int which, uint32_t parity) -> bool {
             uint64_t* b = &pair_bar[quarter * 3 + which];
             ptx::mbar_arrive(b);
             return ptx::wait_bounded(b, parity, abort_flag, p.err, ERR_A_SOFT, WAIT_NS);
         };
-        // stage this thread's half of the Q row: hi and lo, 128-byte swizzled
+        // This thread's half of its Q row: the raw values sit where their hi
+        // parts go (the load used the planes' swizzle), so each thread splits
+        // its own elements in place and writes plane 1 beside them.
+        auto stage_q = [&](int r) -> bool {
+            if (!ptx::wait_bounded(q_full, r & 1, abort_flag, p.err, ERR_A_SOFT, WAIT_NS)) return false;
 #pragma unroll 4
-        for (int d = half * DH; d < (half + 1) * DH; d += 4) {
-            float4 v = q < p.S ? *reinterpret_cast<const float4*>(qrow + d) : make_float4(0.f, 0.f, 0.f, 0.f);
-            float4 h = make_float4(tf32_round(v.x), tf32_round(v.y), tf32_round(v.z), tf32_round(v.w));
-            const uint32_t blk = (uint32_t)(d >> 5) * BQ * 128;
-            *reinterpret_cast<float4*>(qh + blk + swz(row, d & 31)) = h;
-            put_plane1<CROSS, true>(ql + blk, row, d & 31, h, make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w));
-        }
-        ptx::fence_proxy_async_smem();
-        ptx::mbar_arrive(q_ready);
+            for (int i = 0; i < DH; i += 4) {
+                const int d = half * DH + i;
+                const uint32_t at = (uint32_t)(d >> 5) * BQ * 128 + swz(row, d & 31);
+                const float4 v = *reinterpret_cast<const float4*>(qh + at);
+                const float4 h = make_float4(tf32_round(v.x), tf32_round(v.y), tf32_round(v.z), tf32_round(v.w));
+                *reinterpret_cast<float4*>(qh + at) = h;
+                put_plane1<CROSS, true>(ql + (uint32_t)(d >> 5) * BQ * 128, row, d & 31, h,
+                                        make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w));
+            }
+            ptx::fence_proxy_async_smem();
+            ptx::mbar_arrive(q_ready);
+            return true;
+        };
 
-        float m = -FLT_MAX, l = 0.0f;   // m in log2 units; -FLT_MAX as the reference's initial max
-        float o[DH];
-#pragma unroll
-        for (int i = 0; i < DH; i++) o[i] = 0.0f;
         bool ok = true;
-        for (int j = 0; j < n_tiles; j++) {
-            if (!(ok = ptx::wait_bounded(s_full, j & 1, abort_flag, p.err, ERR_A_SOFT, WAIT_NS))) break;
-            ptx::tc_fence_after();
-            float sv[KH];
-            {
-                uint32_t r[KH];
-#pragma unroll
-                for (int c16 = 0; c16 < KH / 16; c16++)
-                    ptx::tmem_ld16(tmem + lane_off + COL_S + half * KH + c16 * 16,
-                                   *reinterpret_cast<uint32_t(*)[16]>(&r[c16 * 16]));
-                ptx::tmem_ld_wait();
-#pragma unroll
-                for (int i = 0; i < KH; i++) sv[i] = __uint_as_float(r[i]) * sl2;
+        int T = 0;
+        AttnItem it;
+        int got = take(0, it, ERR_A_SOFT);
+        if (got < 0) ok = false;
+        if (got > 0) ok = stage_q(0);
+        for (int r = 0; ok; r++) {
+            if ((got = take(r, it, ERR_A_SOFT)) <= 0) {
+                ok = got == 0;
+                break;
             }
-            ptx::tc_fence_before();
-            ptx::mbar_arrive(s_free);   // S may be overwritten by the next tile's MMAs
-            const int k0 = j * BKV + half * KH;
-            const bool full = k0 + KH <= p.S && (!p.causal || k0 + KH - 1 <= q);
-            float mt = -INFINITY;
-            if (full) {
+            const int q = it.q0 + row;
+            float m = -FLT_MAX, l = 0.0f;   // m in log2 units; -FLT_MAX as the reference's initial max
+            float o[DH];
 #pragma unroll
-                for (int i = 0; i < KH; i++) mt = fmaxf(mt, sv[i]);
-            } else {
-#pragma unroll
-                for (int i = 0; i < KH; i++) {
-                    const int kj = k0 + i;
-                    if (kj >= p.S || (p.causal && kj > q)) sv[i] = -INFINITY;
-                    mt = fmaxf(mt, sv[i]);
-                }
-            }
-            red[((j & 1) * 2 + half) * BQ + row] = mt;
-            if (!(ok = pair_sync(j & 1, (j >> 1) & 1))) break;
-            mt = fmaxf(mt, red[((j & 1) * 2 + (half ^ 1)) * BQ + row]);
-            const float m_new = mt > m ? mt : m;
-            float lt = 0.0f;
-#pragma unroll
-            for (int i = 0; i < KH; i++) {
-                sv[i] = exp2f(sv[i] - m_new);   // masked: 2^-inf = 0
-                lt += sv[i];
-            }
-            if (j > 0) {   // O tile j-1 (relative to the old max): fold, freeing the tile and P
-                if (!(ok = ptx::wait_bounded(pv_full, (j - 1) & 1, abort_flag, p.err, ERR_A_SOFT, WAIT_NS))) break;
+            for (int i = 0; i < DH; i++) o[i] = 0.0f;
+            for (int j = 0; j < it.n_tiles; j++, T++) {
+                if (!(ok = ptx::wait_bounded(s_full, T & 1, abort_flag, p.err, ERR_A_SOFT, WAIT_NS))) break;
                 ptx::tc_fence_after();
+                float sv[KH];
+                {
+                    uint32_t rr[KH];
 #pragma unroll
-                for (int g = 0; g < DH / 32; g++) {   // 32 columns per batch keeps registers in bounds
-                    uint32_t r[32];
-                    ptx::tmem_ld16(tmem + lane_off + COL_O + half * DH + g * 32, *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
-                    ptx::tmem_ld16(tmem + lane_off + COL_O + half * DH + g * 32 + 16,
-                                   *reinterpret_cast<uint32_t(*)[16]>(&r[16]));
+                    for (int c16 = 0; c16 < KH / 16; c16++)
+                        ptx::tmem_ld16(tmem + lane_off + COL_S + half * KH + c16 * 16,
+                                       *reinterpret_cast<uint32_t(*)[16]>(&rr[c16 * 16]));
                     ptx::tmem_ld_wait();
 #pragma unroll
-                    for (int i = 0; i < 32; i++) o[g * 32 + i] += __uint_as_float(r[i]);
+                    for (int i = 0; i < KH; i++) sv[i] = __uint_as_float(rr[i]) * sl2;
                 }
-            }
-            if (m_new > m) {   // running max grew: rescale (corr would be 1 otherwise)
-                const float corr = exp2f(m - m_new);
-                l *= corr;
+                ptx::tc_fence_before();
+                ptx::mbar_arrive(s_free);   // S may be overwritten by the next tile's MMAs
+                const int k0 = j * BKV + half * KH;
+                const bool full_tile = k0 + KH <= p.S && (!p.causal || k0 + KH - 1 <= q);
+                float mt = -INFINITY;
+                if (full_tile) {
 #pragma unroll
-                for (int i = 0; i < DH; i++) o[i] *= corr;
-                m = m_new;
-            }
-            l += lt;
-#pragma unroll
-            for (int c16 = 0; c16 < KH / 16; c16++) {
-                uint32_t ph[16], pl[16];
-                if (CROSS) {   // plane 1: 8 columns of bf16 pairs of hi, then 8 of lo
-#pragma unroll
-                    for (int i = 0; i < 16; i += 2) {
-                        const float a = sv[c16 * 16 + i], b = sv[c16 * 16 + i + 1];
-                        const float ha = tf32_round(a), hb = tf32_round(b);
-                        ph[i] = __float_as_uint(ha);
-                        ph[i + 1] = __float_as_uint(hb);
-                        pl[i / 2] = bf16x2(ha, hb);
-                        pl[8 + i / 2] = bf16x2(a - ha, b - hb);
-                    }
+                    for (int i = 0; i < KH; i++) mt = fmaxf(mt, sv[i]);
                 } else {
 #pragma unroll
-                    for (int i = 0; i < 16; i++) {
-                        const float pv = sv[c16 * 16 + i];
-                        const float h = tf32_round(pv);
-                        ph[i] = __float_as_uint(h);
-                        pl[i] = __float_as_uint(pv - h);
+                    for (int i = 0; i < KH; i++) {
+                        const int kj = k0 + i;
+                        if (kj >= p.S || (p.causal && kj > q)) sv[i] = -INFINITY;
+                        mt = fmaxf(mt, sv[i]);
                     }
                 }
-                ptx::tmem_st16(tmem + lane_off + COL_PH + half * KH + c16 * 16, ph);
-                ptx::tmem_st16(tmem + lane_off + COL_PL + half * KH + c16 * 16, pl);
-            }
-            ptx::tmem_st_wait();
-            ptx::tc_fence_before();
-            ptx::mbar_arrive(p_full);
-        }
-        if (ok && n_tiles > 0 &&
-            ptx::wait_bounded(pv_full, (n_tiles - 1) & 1, abort_flag, p.err, ERR_A_SOFT, WAIT_NS)) {
-            ptx::tc_fence_after();
-            {
-                uint32_t r[DH];
+                red[((T & 1) * 2 + half) * BQ + row] = mt;
+                if (!(ok = pair_sync(T & 1, (T >> 1) & 1))) break;
+                mt = fmaxf(mt, red[((T & 1) * 2 + (half ^ 1)) * BQ + row]);
+                const float m_new = mt > m ? mt : m;
+                float lt = 0.0f;
 #pragma unroll
-                for (int c16 = 0; c16 < DH / 16; c16++)
-                    ptx::tmem_ld16(tmem + lane_off + COL_O + half * DH + c16 * 16,
-                                   *reinterpret_cast<uint32_t(*)[16]>(&r[c16 * 16]));
+                for (int i = 0; i < KH; i++) {
+                    sv[i] = ex2_approx(sv[i] - m_new);   // masked: 2^-inf = 0
+                    lt += sv[i];
+                }
+                if (j > 0) {   // O tile j-1 (relative to the old max): fold, freeing the tile and P
+                    if (!(ok = ptx::wait_bounded(pv_full, (T - 1) & 1, abort_flag, p.err, ERR_A_SOFT, WAIT_NS)))
+                        break;
+                    ptx::tc_fence_after();
+#pragma unroll
+                    for (int g = 0; g < DH / 32; g++) {   // 32 columns per batch keeps registers in bounds
+                        uint32_t rr[32];
+                        ptx::tmem_ld16(tmem + lane_off + COL_O + half * DH + g * 32,
+                                       *reinterpret_cast<uint32_t(*)[16]>(&rr[0]));
+                        ptx::tmem_ld16(tmem + lane_off + COL_O + half * DH + g * 32 + 16,
+                                       *reinterpret_cast<uint32_t(*)[16]>(&rr[16]));
+                        ptx::tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 32; i++) o[g * 32 + i] += __uint_as_float(rr[i]);
+                    }
+                }
+                if (m_new > m) {   // running max grew: rescale (corr would be 1 otherwise)
+                    const float corr = ex2_approx(m - m_new);
+                    l *= corr;
+#pragma unroll
+                    for (int i = 0; i < DH; i++) o[i] *= corr;
+                    m = m_new;
+                }
+                l += lt;
+#pragma unroll
+                for (int c16 = 0; c16 < KH / 16; c16++) {
+                    uint32_t ph[16], pl[16];
+                    if (CROSS) {   // plane 1: 8 columns of bf16 pairs of hi, then 8 of lo
+#pragma unroll
+                        for (int i = 0; i < 16; i += 2) {
+                            const float a = sv[c16 * 16 + i], b = sv[c16 * 16 + i + 1];
+                            const float ha = tf32_rna_int(a), hb = tf32_rna_int(b);
+                            ph[i] = __float_as_uint(ha);
+                            ph[i + 1] = __float_as_uint(hb);
+                            pl[i / 2] = bf16x2_trunc(ha, hb);
+                            pl[8 + i / 2] = bf16x2_trunc(a - ha, b - hb);
+                        }
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 16; i++) {
+                            const float pv = sv[c16 * 16 + i];
+                            const float h = tf32_rna_int(pv);
+                            ph[i] = __float_as_uint(h);
+                            pl[i] = __float_as_uint(pv - h);
+                        }
+                    }
+                    ptx::tmem_st16(tmem + lane_off + COL_PH + half * KH + c16 * 16, ph);
+                    ptx::tmem_st16(tmem + lane_off + COL_PL + half * KH + c16 * 16, pl);
+                }
+                ptx::tmem_st_wait();
+                ptx::tc_fence_before();
+                ptx::mbar_arrive(p_full);
+            }
+            if (!ok) break;
+            // Row sum over both halves.  The exchange slot of parity T & 1 was
+            // last read for tile T - 2; the next item's first tile reuses it only
+            // after every softmax thread has arrived on q_ready in stage_q below.
+            red[((T & 1) * 2 + half) * BQ + row] = l;
+            const bool paired = pair_sync(2, r & 1);
+            l += red[((T & 1) * 2 + (half ^ 1)) * BQ + row];
+            if (!paired) {
+                ok = false;
+                break;
+            }
+            // The next item's Q while this item's last P.V runs.
+            AttnItem nx;
+            if ((got = take(r + 1, nx, ERR_A_SOFT)) < 0) {
+                ok = false;
+                break;
+            }
+            if (got > 0 && !(ok = stage_q(r + 1))) break;
+            if (!(ok = ptx::wait_bounded(pv_full, (T - 1) & 1, abort_flag, p.err, ERR_A_SOFT, WAIT_NS))) break;
+            ptx::tc_fence_after();
+#pragma unroll
+            for (int g = 0; g < DH / 32; g++) {
+                uint32_t rr[32];
+                ptx::tmem_ld16(tmem + lane_off + COL_O + half * DH + g * 32, *reinterpret_cast<uint32_t(*)[16]>(&rr[0]));
+                ptx::tmem_ld16(tmem + lane_off + COL_O + half * DH + g * 32 + 16,
+                               *reinterpret_cast<uint32_t(*)[16]>(&rr[16]));
                 ptx::tmem_ld_wait();
 #pragma unroll
-                for (int i = 0; i < DH; i++) o[i] += __uint_as_float(r[i]);
+                for (int i = 0; i < 32; i++) o[g * 32 + i] += __uint_as_float(rr[i]);
             }
-            // the exchange buffer of parity n_tiles&1 was last read for tile n_tiles-2
-            const int fb = n_tiles & 1;
-            red[(fb * 2 + half) * BQ + row] = l;
-            const bool paired = pair_sync(2, 0);
-            l += red[(fb * 2 + (half ^ 1)) * BQ + row];
-            if (paired && q < p.S) {
+            ptx::tc_fence_before();
+            if (q < p.S) {
                 const float inv = 1.0f / l;
-                float* orow = p.o + (bh / p.H) * p.o_sb + (bh % p.H) * p.o_sh + (int64_t)q * p.o_ss + half * DH;
+                float* orow = p.o + (int64_t)(it.bh / p.H) * p.o_sb + (int64_t)(it.bh % p.H) * p.o_sh +
+                              (int64_t)q * p.o_ss + half * DH;
 #pragma unroll
                 for (int i = 0; i < DH; i += 4)
                     *reinterpret_cast<float4*>(orow + i) =
@@ -508,6 +645,8 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
         for (int s = 0; s < STAGES; s++)
             if (issued[s] >= 0)
                 ptx::wait_bounded(&full[s], (uint32_t)issued[s], &no_abort, nullptr, 0, 100000000ull);
+        if (issued[STAGES] >= 0)
+            ptx::wait_bounded(q_full, (uint32_t)issued[STAGES], &no_abort, nullptr, 0, 100000000ull);
     }
     __syncthreads();
     if (warp == 1) {
@@ -527,8 +666,8 @@ bool attn_cross() {
 
 template <int D>
 Status launch_tc(const AttnTcParams& prm, int BH, cudaStream_t st) {
-    dim3 grid = prm.heads_fast ? dim3((unsigned)BH, (unsigned)prm.n_qblocks)
-                               : dim3((unsigned)prm.n_qblocks, (unsigned)BH);
+    (void)BH;
+    const dim3 grid((unsigned)min(prm.n_items, g_num_sms));   // persistent: one CTA per SM
     if (attn_cross())
         attn_tc_kernel<D, true><<<grid, ATHREADS, AttnTcCfg<D>::SMEM, st>>>(prm);
     else
@@ -542,12 +681,12 @@ Status launch_tc(const AttnTcParams& prm, int BH, cudaStream_t st) {
 // Shapes this kernel takes: no custom mask, head_dim 64 or 128, at least one
 // full 128-query block.
 bool attention_tc_applicable(int64_t S, int D, bool has_mask, int64_t BH) {
-    return !has_mask && (D == 64 || D == 128) && S >= 128 && BH <= 65535 && (S + BQ - 1) / BQ <= 65535;
+    return !has_mask && (D == 64 || D == 128) && S >= 128 && BH * ((S + BQ - 1) / BQ) <= INT32_MAX;
 }
 
 size_t attention_tc_workspace(int64_t BHkv, int64_t S, int D) {
     const size_t tile = D == 128 ? AttnTcCfg<128>::TILE_BYTES : AttnTcCfg<64>::TILE_BYTES;
-    return (size_t)BHkv * ((S + BKV - 1) / BKV) * tile;
+    return (size_t)BHkv * ((S + BKV - 1) / BKV) * tile + 256;   // + the item counter
 }
 
 Status attention_tc_prepare() {
@@ -572,14 +711,15 @@ Status launch_attention_tc(const AttnViews& vw, int64_t BH, int64_t S, int D, in
     if (ws.bytes < attention_tc_workspace(BHkv, S, D))
         return Status::err(RT_ERR_ARGUMENT, "attention: workspace too small");
     const int n_kv = (int)((S + BKV - 1) / BKV);
-    dim3 pgrid((unsigned)n_kv, (unsigned)BHkv);
+    dim3 pgrid((unsigned)(n_kv * 4), (unsigned)BHkv);
     KvViews kv{vw.k, vw.v, vw.k_sb, vw.k_sh, vw.k_ss, vw.v_sb, vw.v_sh, vw.v_ss, vw.H / group};
     uint8_t* kvbuf = reinterpret_cast<uint8_t*>(ws.base);
+    int* counter = reinterpret_cast<int*>(kvbuf + attention_tc_workspace(BHkv, S, D) - 256);
     const bool cross = attn_cross();
-    if (D == 64 && cross) pack_kv_kernel<64, true><<<pgrid, 256, 0, st>>>(kv, kvbuf, (int)S, n_kv);
-    else if (D == 64) pack_kv_kernel<64, false><<<pgrid, 256, 0, st>>>(kv, kvbuf, (int)S, n_kv);
-    else if (cross) pack_kv_kernel<128, true><<<pgrid, 256, 0, st>>>(kv, kvbuf, (int)S, n_kv);
-    else pack_kv_kernel<128, false><<<pgrid, 256, 0, st>>>(kv, kvbuf, (int)S, n_kv);
+    if (D == 64 && cross) pack_kv_kernel<64, true><<<pgrid, 256, 0, st>>>(kv, kvbuf, (int)S, n_kv, counter);
+    else if (D == 64) pack_kv_kernel<64, false><<<pgrid, 256, 0, st>>>(kv, kvbuf, (int)S, n_kv, counter);
+    else if (cross) pack_kv_kernel<128, true><<<pgrid, 256, 0, st>>>(kv, kvbuf, (int)S, n_kv, counter);
+    else pack_kv_kernel<128, false><<<pgrid, 256, 0, st>>>(kv, kvbuf, (int)S, n_kv, counter);
     RT_LAUNCH_CHECK();
     *launches += 1;
     AttnTcParams prm;
@@ -595,8 +735,22 @@ Status launch_attention_tc(const AttnViews& vw, int64_t BH, int64_t S, int D, in
     prm.group = group;
     prm.causal = causal;
     prm.n_qblocks = (int)((S + BQ - 1) / BQ);
+    prm.BH = (int)BH;
+    prm.n_items = (int)(BH * prm.n_qblocks);
+    prm.counter = counter;
     prm.heads_fast = attention_tc_workspace(BHkv, S, D) <= ((size_t)512 << 20) ? 1 : 0;
     prm.scale = 1.0f / sqrtf((float)D);
+    {   // Q tensor map: rows and heads ordered by stride (the driver wants them increasing)
+        const bool rows_first = vw.q_ss <= vw.q_sh;
+        const int64_t B = BH / vw.H;
+        const int64_t dims[4] = {D, rows_first ? S : vw.H, rows_first ? vw.H : S, B};
+        const int64_t strides[3] = {4 * (rows_first ? vw.q_ss : vw.q_sh), 4 * (rows_first ? vw.q_sh : vw.q_ss),
+                                    4 * vw.q_sb};
+        const int box[4] = {32, rows_first ? BQ : 1, rows_first ? 1 : BQ, 1};
+        Status s = encode_tmap_f32(&prm.tq, vw.q, 4, dims, strides, box, 128);
+        if (!s.good()) return s;
+        prm.q_rows_dim = rows_first ? 1 : 2;
+    }
     prm.err = kernel_error_flag();
     *launches += 1;
     return D == 64 ? launch_tc<64>(prm, (int)BH, st) : launch_tc<128>(prm, (int)BH, st);

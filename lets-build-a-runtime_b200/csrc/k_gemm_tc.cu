@@ -1166,6 +1166,30 @@ Status split_operand(const float* x, float* hi, float* lo, int64_t batches, int6
     return run_split(x, hi, lo, batches, rows, K, transpose, 0, st);
 }
 
+Status encode_tmap_f32(CUtensorMap* m, const float* base, int rank, const int64_t* dims,
+                       const int64_t* byte_strides, const int* box, int swizzle_bytes) {
+    auto fn = encode_fn();
+    if (!fn) return Status::err(RT_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    if (rank < 1 || rank > 5) return Status::err(RT_ERR_ARGUMENT, "tensor map rank");
+    cuuint64_t d[5], st[4];
+    cuuint32_t bx[5], estr[5];
+    for (int i = 0; i < rank; i++) {
+        d[i] = (cuuint64_t)dims[i];
+        bx[i] = (cuuint32_t)box[i];
+        estr[i] = 1;
+        if (i > 0) st[i - 1] = (cuuint64_t)byte_strides[i - 1];
+    }
+    CUtensorMapSwizzle sw = swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                            : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                  : CU_TENSOR_MAP_SWIZZLE_NONE;
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank, const_cast<float*>(base), d, st, bx, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return Status::err(RT_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+    return Status::ok();
+}
+
 Status encode_tmap_f32_3d(CUtensorMap* m, const float* base, int64_t d0, int64_t d1, int64_t d2, int box0,
                           int box1, int swizzle_bytes) {
     auto fn = encode_fn();
