@@ -44,6 +44,8 @@
 // are bounded (see sm100_ptx.h).
 #include <float.h>
 
+#include <algorithm>
+
 #include "gemm.h"
 #include "sm100_ptx.h"
 
@@ -92,7 +94,7 @@ struct AttnTcParams {
     int H;                      // query heads per batch element
     int S, group, causal, n_qblocks;
     int BH, n_items;            // (batch, head) pairs; work items = BH x query blocks
-    int heads_fast;             // item order: heads fastest instead of query blocks fastest
+    int head_group;             // item order: groups of this many (batch, head) pairs, heads fastest inside
     int* counter;               // next item to take (zeroed by the pack kernel before each launch)
     float scale;
     int* err;
@@ -220,14 +222,21 @@ __global__ void __launch_bounds__(256) pack_kv_kernel(KvViews kv, uint8_t* __res
 // (one CTA per SM); each CTA's producer takes the next item from a global
 // counter, so items run in their list order across the GPU as on a plain
 // grid -- longest causal blocks first, and the items in flight share few
-// heads' K/V in L2 -- with no per-CTA start-up per item.
+// heads' K/V in L2 -- with no per-CTA start-up per item.  Item order: heads
+// in groups whose packed K/V totals ~48 MB (RT_ATTN_GROUP_MB overrides),
+// inside a group all heads' longest query block first, then the next
+// longest; measured against all heads at once (GPT-2: 100 MB of K/V in
+// flight) and 16 MB groups, 48 MB was fastest on every config here.
 struct AttnItem {
     int bh, q0, n_tiles;
 };
 
 __device__ __forceinline__ void attn_decode(const AttnTcParams& p, int L, AttnItem& it) {
-    const int bh = p.heads_fast ? L % p.BH : L / p.n_qblocks;
-    const int qi = p.heads_fast ? L / p.BH : L % p.n_qblocks;
+    const int per = p.head_group * p.n_qblocks;   // items per head group
+    const int g = L / per, r = L - g * per;
+    const int gh = min(p.head_group, p.BH - g * p.head_group);
+    const int bh = g * p.head_group + r % gh;
+    const int qi = r / gh;
     const int qb = p.causal ? p.n_qblocks - 1 - qi : qi;
     it.bh = bh;
     it.q0 = qb * BQ;
@@ -738,7 +747,12 @@ Status launch_attention_tc(const AttnViews& vw, int64_t BH, int64_t S, int D, in
     prm.BH = (int)BH;
     prm.n_items = (int)(BH * prm.n_qblocks);
     prm.counter = counter;
-    prm.heads_fast = attention_tc_workspace(BHkv, S, D) <= ((size_t)512 << 20) ? 1 : 0;
+    {   // heads of one group together hold at most ~budget bytes of packed K/V
+        size_t budget = (size_t)48 << 20;
+        if (const char* e = getenv("RT_ATTN_GROUP_MB")) budget = (size_t)atoll(e) << 20;
+        const size_t per_head = (size_t)n_kv * (D == 128 ? AttnTcCfg<128>::TILE_BYTES : AttnTcCfg<64>::TILE_BYTES) / group;
+        prm.head_group = (int)std::max<int64_t>(1, std::min<int64_t>(BH, (int64_t)(budget / per_head)));
+    }
     prm.scale = 1.0f / sqrtf((float)D);
     {   // Q tensor map: rows and heads ordered by stride (the driver wants them increasing)
         const bool rows_first = vw.q_ss <= vw.q_sh;
