@@ -868,6 +868,84 @@ void plan_norm_handoffs(const Analysis& an, const Effective& e, std::vector<Plan
     }
 }
 
+// Attention -> GEMM split hand-off: an attention writing the merged
+// [B, S, H*D] layout whose output is read only by the next GEMM, as its A
+// operand, writes that GEMM's split A planes (carry buffer) from its O store;
+// the GEMM skips its split pass.  Conditions as for the norm hand-off, on the
+// schedule left by the layout folds (the output is the fused attention's).
+// Opt-in (RT_FUSE_ATTN_SPLIT=1): on GPT-2 the plane stores cost the attention
+// (+14 us per forward) about what the projection GEMMs save (-22 us), so the
+// forward time does not move.
+void plan_attn_handoffs(const Analysis& an, const Effective& e, std::vector<PlanItem>& items,
+                        const std::vector<Range>& protect, CarryAlloc& carry_alloc) {
+    const int n = (int)an.nodes.size();
+    for (int a = 0; a < n; a++) {
+        PlanItem& it = items[a];
+        if (!it.views || e.skipped[a] || it.skip || an.nodes[a].n_dims != 4) continue;
+        const AttnViews& v = it.attn;
+        const OpNode& na = an.nodes[a];
+        const int64_t B = na.out_shape[0], H = na.out_shape[1], S = na.out_shape[2], D = na.out_shape[3];
+        const Range L = e.writes[a];
+        if (L.hi - L.lo != (uintptr_t)(B * H * S * D * 4) || reinterpret_cast<uintptr_t>(v.o) != L.lo ||
+            v.o_sh != D || v.o_ss != H * D || v.o_sb != S * H * D || (H * D) % 16 != 0) {
+            if (dbg()) fprintf(stderr, "[fusion] attention %d: output not merged [rows][H*D] (%zu bytes, o %p lo %p, strides %lld %lld %lld)\n", a,
+                               (size_t)(L.hi - L.lo), (void*)v.o, (void*)L.lo, (long long)v.o_sb, (long long)v.o_sh, (long long)v.o_ss);
+            continue;
+        }
+        int k = -1;
+        for (int j = a + 1; j < n; j++) {
+            if (e.skipped[j] || items[j].skip) continue;
+            if (eff_reads(e, j, L)) { k = j; break; }
+            if (overlaps(e.writes[j], L)) break;
+        }
+        if (k < 0) continue;
+        const OpNode& kn = an.nodes[k];
+        PlanItem& ki = items[k];
+        if (dbg()) fprintf(stderr, "[fusion] attention %d: first reader %d (op %d)\n", a, k, kn.op);
+        if (kn.op != RT_OP_MATMUL && kn.op != RT_OP_MATMUL_ADD) continue;
+        const void* a_ptr = ki.redirect_slot == 0 ? ki.redirect_ptr : kn.inputs[0];
+        if (reinterpret_cast<uintptr_t>(a_ptr) != L.lo || ki.presplit_off >= 0 || !gemm_fusable(kn)) {
+            if (dbg()) fprintf(stderr, "[fusion]   A %p L %p presplit %lld fusable %d\n", a_ptr, (void*)L.lo,
+                               (long long)ki.presplit_off, (int)gemm_fusable(kn));
+            continue;
+        }
+        GemmProblem kp;
+        if (!decode_gemm(kn, &kp).good() || (uintptr_t)(kp.batches * kp.M * kp.K * 4) != L.hi - L.lo ||
+            kp.K != H * D) {
+            if (dbg()) fprintf(stderr, "[fusion]   gemm shape does not match\n");
+            continue;
+        }
+        bool only_a = true;
+        for (size_t i = 1; i < e.reads[k].size(); i++) only_a &= !overlaps(e.reads[k][i], L);
+        if (!only_a) {
+            if (dbg()) fprintf(stderr, "[fusion]   read through B / bias too\n");
+            continue;
+        }
+        // dead after k: no other reader before the memory is rewritten, not a graph output
+        bool dead = true, rewritten = false;
+        for (int j = a + 1; j < n && dead && !rewritten; j++) {
+            if (j != k && eff_reads(e, j, L)) {
+                dead = false;
+                if (dbg()) fprintf(stderr, "[fusion]   read by %d\n", j);
+            }
+            if (j >= k && overlaps(e.writes[j], L)) rewritten = true;   // k may write its output over L
+        }
+        if (!rewritten)
+            for (const Range& pr : protect) dead &= !overlaps(pr, L);
+        if (!dead) {
+            if (dbg()) fprintf(stderr, "[fusion]   output read again or a graph output\n");
+            continue;
+        }
+        const int64_t plane = (int64_t)(((L.hi - L.lo) + 255) & ~(uintptr_t)255);
+        const int64_t off = carry_alloc.take(a, k, 2 * plane);
+        it.attn_planes_off = off;
+        it.carry_plane_bytes = plane;
+        ki.presplit_off = off;
+        ki.carry_plane_bytes = plane;
+        if (dbg()) fprintf(stderr, "[fusion] attention %d: writes the split A operand of gemm %d\n", a, k);
+    }
+}
+
 bool fusion_enabled() {
     static const bool on = [] {
         const char* e = getenv("RT_FUSE");
@@ -960,6 +1038,9 @@ std::vector<PlanItem> plan_fusions(const std::vector<OpNode>& nodes,
                 return !(v && v[0] == '0');
             }();
             if (fusion_enabled() && norm_handoff) plan_norm_handoffs(an, e, items, protect, carry_alloc);
+            const char* av = getenv("RT_FUSE_ATTN_SPLIT");   // read per plan; opt-in (see plan_attn_handoffs)
+            const bool attn_handoff = av && av[0] == '1';
+            if (fusion_enabled() && attn_handoff) plan_attn_handoffs(an, e, items, protect, carry_alloc);
             if (carry_bytes) *carry_bytes = (size_t)carry_alloc.total;
             break;
         }

@@ -96,6 +96,8 @@ struct AttnTcParams {
     int BH, n_items;            // (batch, head) pairs; work items = BH x query blocks
     int head_group;             // item order: groups of this many (batch, head) pairs, heads fastest inside
     int* counter;               // next item to take (zeroed by the pack kernel before each launch)
+    uint8_t* ox;                // non-null: O written as a GEMM's split A planes (hi at o, plane 1 here)
+    int ox_cross;
     float scale;
     int* err;
 };
@@ -144,6 +146,12 @@ __device__ __forceinline__ float tf32_rna_int(float x) {
 // truncation's 2^-8 (against 2^-9 for nearest) moves a product by ~2^-19.
 __device__ __forceinline__ uint32_t bf16x2_trunc(float a, float b) {
     return __byte_perm(__float_as_uint(a), __float_as_uint(b), 0x7632);
+}
+// bf16 (nearest, ties to even) of two finite values by integer rounding,
+// `a` in the low half: the same bits as cvt.rn.bf16x2.f32.
+__device__ __forceinline__ uint32_t bf16x2_rn_int(float a, float b) {
+    const uint32_t ua = __float_as_uint(a), ub = __float_as_uint(b);
+    return ((ua + 0x7FFFu + ((ua >> 16) & 1u)) >> 16) | ((ub + 0x7FFFu + ((ub >> 16) & 1u)) & 0xFFFF0000u);
 }
 // 2^x with the hardware approximation (flushes results below 2^-126 to 0;
 // 2^-inf = 0, which the causal mask relies on).
@@ -637,12 +645,46 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
             ptx::tc_fence_before();
             if (q < p.S) {
                 const float inv = 1.0f / l;
-                float* orow = p.o + (int64_t)(it.bh / p.H) * p.o_sb + (int64_t)(it.bh % p.H) * p.o_sh +
-                              (int64_t)q * p.o_ss + half * DH;
+                const int64_t e0 = (int64_t)(it.bh / p.H) * p.o_sb + (int64_t)(it.bh % p.H) * p.o_sh +
+                                   (int64_t)q * p.o_ss + half * DH;
+                float* orow = p.o + e0;
+                if (!p.ox) {
 #pragma unroll
-                for (int i = 0; i < DH; i += 4)
-                    *reinterpret_cast<float4*>(orow + i) =
-                        make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+                    for (int i = 0; i < DH; i += 4)
+                        *reinterpret_cast<float4*>(orow + i) =
+                            make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+                } else {
+                    // split planes of the next GEMM's A operand: hi here, plane 1 at the
+                    // same element offsets; e0 starts a 16-wide K block (D/2 is a multiple of 16)
+#pragma unroll
+                    for (int i = 0; i < DH; i += 16) {
+                        uint32_t hb[8], lb[8];
+#pragma unroll
+                        for (int t = 0; t < 16; t += 4) {
+                            const float4 v = make_float4(o[i + t] * inv, o[i + t + 1] * inv, o[i + t + 2] * inv,
+                                                         o[i + t + 3] * inv);
+                            const float4 h = make_float4(tf32_rna_int(v.x), tf32_rna_int(v.y), tf32_rna_int(v.z),
+                                                         tf32_rna_int(v.w));
+                            const float4 lo = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+                            *reinterpret_cast<float4*>(orow + i + t) = h;
+                            if (p.ox_cross) {
+                                hb[t / 2] = bf16x2_rn_int(h.x, h.y);
+                                hb[t / 2 + 1] = bf16x2_rn_int(h.z, h.w);
+                                lb[t / 2] = bf16x2_rn_int(lo.x, lo.y);
+                                lb[t / 2 + 1] = bf16x2_rn_int(lo.z, lo.w);
+                            } else {
+                                *reinterpret_cast<float4*>(p.ox + (e0 + i + t) * 4) = lo;
+                            }
+                        }
+                        if (p.ox_cross) {
+                            uint4* blk = reinterpret_cast<uint4*>(p.ox + (e0 + i) * 4);   // 64 bytes: hi | lo
+                            blk[0] = make_uint4(hb[0], hb[1], hb[2], hb[3]);
+                            blk[1] = make_uint4(hb[4], hb[5], hb[6], hb[7]);
+                            blk[2] = make_uint4(lb[0], lb[1], lb[2], lb[3]);
+                            blk[3] = make_uint4(lb[4], lb[5], lb[6], lb[7]);
+                        }
+                    }
+                }
             }
         }
     }
@@ -747,6 +789,8 @@ Status launch_attention_tc(const AttnViews& vw, int64_t BH, int64_t S, int D, in
     prm.BH = (int)BH;
     prm.n_items = (int)(BH * prm.n_qblocks);
     prm.counter = counter;
+    prm.ox = vw.ox;
+    prm.ox_cross = vw.ox_cross;
     {   // heads of one group together hold at most ~budget bytes of packed K/V
         size_t budget = (size_t)48 << 20;
         if (const char* e = getenv("RT_ATTN_GROUP_MB")) budget = (size_t)atoll(e) << 20;

@@ -106,6 +106,11 @@ struct AttnViews {
     float* o;
     int64_t q_sb, q_sh, q_ss, k_sb, k_sh, k_ss, v_sb, v_sh, v_ss, o_sb, o_sh, o_ss;
     int H;   // query heads per batch element
+    // Non-null: O is the A operand of a following GEMM, written as its split
+    // planes -- hi at `o` (same view), plane 1 here at the same element
+    // offsets x 4 bytes (O contiguous [rows][K], K % 16 == 0).
+    uint8_t* ox = nullptr;
+    int ox_cross = 1;   // plane 1 layout: 1 cross (bf16 [hi | lo] per 16 block), 0 lo (fp32)
 };
 // Contiguous [B, H, S, D] views of an ATTENTION node's operands (4-D nodes only).
 bool attention_default_views(const OpNode& n, AttnViews* v);
@@ -157,6 +162,7 @@ struct PlanItem {
     int64_t presplit_off = -1;     // consumer: A planes are already here; no split pre-pass
     int64_t carry_plane_bytes = 0; // bytes of one plane
     int64_t norm_planes_off = -1;  // LAYERNORM / RMSNORM: write the consumer GEMM's split A planes here
+    int64_t attn_planes_off = -1;  // ATTENTION (merged-layout views): the same, from its O store
     int64_t epi_bias_off = -1;     // GEMM adds this merged bias (byte offset into the plan's bias buffer)
     bool rope = false;             // this (ADD) node launches the fused norm + rotary kernel instead
     RopeFold rp{};

@@ -296,7 +296,16 @@ Status launch_item(Plan& p, size_t i, cudaStream_t st, int* launches) {
             return launch_norm_planes(p.nodes[i], reinterpret_cast<float*>(base), base + p.items[i].carry_plane_bytes,
                                       gemm_cross_scheme(), st, launches);
         }
-        if (p.items[i].views) return launch_attention_views(p.nodes[i], p.items[i].attn, st, ws, launches);
+        if (p.items[i].views) {
+            AttnViews v = p.items[i].attn;
+            if (p.items[i].attn_planes_off >= 0) {
+                char* base = p.carry + p.items[i].attn_planes_off;
+                v.o = reinterpret_cast<float*>(base);
+                v.ox = reinterpret_cast<uint8_t*>(base + p.items[i].carry_plane_bytes);
+                v.ox_cross = gemm_cross_scheme() ? 1 : 0;
+            }
+            return launch_attention_views(p.nodes[i], v, st, ws, launches);
+        }
         const PlanItem& it = p.items[i];
         if (it.epi_act || it.epi_out || it.carry_off >= 0 || it.presplit_off >= 0 || it.epi_bias_off >= 0) {
             GemmFusion f;

@@ -172,3 +172,20 @@ def test_norms_write_the_split_operand_of_their_gemm(name, pairs):
     # the consumer: 4, or 3 when it also folds an activation into its epilogue
     assert all(flags[i + 1] in (3, 4) and prog.nodes[i + 1].op in (OP["MATMUL"], OP["MATMUL_ADD"])
                for i in producers)
+
+
+def test_attention_writes_the_projection_split_operand(monkeypatch):
+    """GPT-2: each attention (its head merge folded, writing [B, S, H*D]) is
+    read only by the output projection's A operand; with RT_FUSE_ATTN_SPLIT=1
+    it writes that GEMM's split planes and the GEMM skips its split pass (the
+    default keeps the split pass)."""
+    prog = Program.load(GOLDEN / "gpt2_b8.json")
+    arr, _ = bind(prog)
+    ops = [nd.op for nd in prog.nodes]
+    proj = [i for i, op in enumerate(ops) if op == OP["MATMUL_ADD"] and OP["ATTENTION"] in ops[max(0, i - 3):i]]
+    assert len(proj) == 2
+    _, flags = report(prog, arr)
+    assert [flags[i] for i in proj] == [0, 0]
+    monkeypatch.setenv("RT_FUSE_ATTN_SPLIT", "1")
+    _, flags = report(prog, arr)
+    assert [flags[i] for i in proj] == [4, 4]

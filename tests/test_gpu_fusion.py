@@ -140,3 +140,34 @@ def test_gated_activation_reads_slices_through_views(act, bias, gpu_executor_fac
     got = ex.run({})["y"]
     ref = oracle.run_program("restated", prog, dict(stored), {})["y"]
     np.testing.assert_allclose(got, ref, rtol=2e-6, atol=2e-6)
+
+
+@pytest.mark.parametrize("attn_split", ["1", "0"])
+def test_attention_split_hand_off_matches_golden(attn_split, gpu_executor_factory, monkeypatch):
+    """GPT-2 mini body at S = 300 (a partial last query block): the attention
+    writes the projection GEMM's split A planes (RT_FUSE_ATTN_SPLIT=1) or its
+    plain output (0, the default) and the result matches the
+    reference executor's golden output."""
+    from conftest import load_golden
+    from test_gpu_programs import assert_parity
+    monkeypatch.setenv("RT_FUSE_ATTN_SPLIT", attn_split)
+    prog, ins, outs = load_golden("gpt2_mini_s300")
+    ex = gpu_executor_factory(prog, prog.make_constants())
+    got = ex.run(ins)
+    for k, ref in outs.items():
+        assert_parity(got[k], ref, f"gpt2_mini_s300:{k}")
+    flags = flags_of(ex, prog)
+    ops = [nd.op for nd in prog.nodes]
+    proj = [i for i, op in enumerate(ops) if op == OP["MATMUL_ADD"] and OP["ATTENTION"] in ops[max(0, i - 3):i]]
+    assert proj and all(flags[i] == (4 if attn_split == "1" else 0) for i in proj)
+
+
+def test_attention_split_hand_off_3xtf32():
+    """The same hand-off with the 3xTF32 plane layout (hi + fp32 lo), in a fresh process."""
+    import os
+    import subprocess
+    import sys
+    r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", "-m", "gpu", "-p", "no:cacheprovider",
+                        __file__, "-k", "test_attention_split_hand_off_matches_golden"],
+                       env=dict(os.environ, RT_GEMM_3XTF32="1"), capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
