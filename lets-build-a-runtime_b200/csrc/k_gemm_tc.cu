@@ -92,6 +92,7 @@ struct TcParams {
     CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;   // 3-D {K, rows, batches}
     float* c;
     const float* bias;
+    const float* res;             // non-null: residual [batches*M][N] added after the bias (first split)
     float alpha;
     int M, N, K, batches;
     int m_tiles, n_tiles, k_blocks, total_tiles;
@@ -114,6 +115,24 @@ __device__ __forceinline__ uint16_t bf16_bits(float x) {
     return __bfloat16_as_ushort(__float2bfloat16_rn(x));
 }
 
+// A folded residual (alpha == 1): on the first split, a full-width row's COLS
+// residual values go straight into the accumulator registers before the
+// tile's first TMEM chunk is awaited (the loads overlap the MMAs); the TMEM
+// chunks are then added to them.  Returns whether it did (otherwise store_row
+// adds the residual).
+template <int COLS>
+__device__ __forceinline__ bool load_residual(const TcParams& p, int64_t row, int bz, int col0, bool first_split,
+                                              float* acc) {
+    if (!first_split || row >= p.M || (p.N & 3) != 0 || col0 + COLS > p.N) return false;
+    const float* src = p.res + ((int64_t)bz * p.M + row) * p.N + col0;
+#pragma unroll
+    for (int j = 0; j < COLS; j += 4) {
+        const float4 v = *reinterpret_cast<const float4*>(src + j);
+        acc[j] = v.x; acc[j + 1] = v.y; acc[j + 2] = v.z; acc[j + 3] = v.w;
+    }
+    return true;
+}
+
 // One epilogue row: COLS consecutive columns from col0 of output row `row`
 // (within batch bz): alpha, bias (first split only), optional GELU, then C
 // (plain store, or float4 atomics under split-K) or, for PLANES kernels, the
@@ -121,8 +140,9 @@ __device__ __forceinline__ uint16_t bf16_bits(float x) {
 // otherwise cost every GEMM's epilogue).
 template <int COLS, bool PLANES>
 __device__ __forceinline__ void store_row(const TcParams& p, int64_t row, int bz, int col0, const float* acc,
-                                          bool first_split) {
+                                          bool first_split, bool res_in_acc) {
     const bool add_bias = p.bias && first_split;
+    const bool add_res = p.res && first_split && !res_in_acc;
     const int64_t r = (int64_t)bz * p.M + row;
     if (PLANES) {
         // N % 4 == 0 here (it is the K of the consuming GEMM); splits == 1
@@ -170,6 +190,10 @@ __device__ __forceinline__ void store_row(const TcParams& p, int64_t row, int bz
                 float4 bb = *reinterpret_cast<const float4*>(p.bias + col0 + j);
                 v.x += bb.x; v.y += bb.y; v.z += bb.z; v.w += bb.w;
             }
+            if (add_res) {   // alpha == 1 with a residual
+                const float4 rr = *reinterpret_cast<const float4*>(p.res + r * p.N + col0 + j);
+                v.x += rr.x; v.y += rr.y; v.z += rr.z; v.w += rr.w;
+            }
             if (p.act == 1) {
                 v.x = gelu_tanh(v.x); v.y = gelu_tanh(v.y); v.z = gelu_tanh(v.z); v.w = gelu_tanh(v.w);
             }
@@ -184,6 +208,7 @@ __device__ __forceinline__ void store_row(const TcParams& p, int64_t row, int bz
             if (col0 + j < p.N) {
                 float v = p.alpha * acc[j];
                 if (add_bias) v += p.bias[col0 + j];
+                if (add_res) v += p.res[r * p.N + col0 + j];   // alpha == 1 with a residual
                 if (p.act == 1) v = gelu_tanh(v);
                 if (p.splits > 1) atomicAdd(crow + col0 + j, v);
                 else crow[col0 + j] = v;
@@ -390,7 +415,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
             }
             if (!ok) break;
             const int64_t row = (int64_t)m_blk * BM + quarter * 32 + lane;
-            if (row < p.M) store_row<EPI_COLS, PLANES>(p, row, bz, n_blk * BN + half * EPI_COLS, acc, first_split);
+            if (row < p.M) store_row<EPI_COLS, PLANES>(p, row, bz, n_blk * BN + half * EPI_COLS, acc, first_split, false);
         }
     }
 
@@ -431,7 +456,7 @@ constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
 static_assert(P_SMEM_BYTES <= 232448, "shared memory budget");
 constexpr int P_EPI_COLS = 128;
 
-template <bool CROSS, bool PLANES>
+template <bool CROSS, bool PLANES, bool RES = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     tc_gemm_pair_kernel(const __grid_constant__ TcParams p) {
     extern __shared__ uint8_t smem_raw[];
@@ -595,6 +620,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             const int n_chunks = (kb_hi - kb_lo + p.kb_per_chunk - 1) / p.kb_per_chunk;
             const bool first_split = kb_lo == 0;
             float acc[P_EPI_COLS];
+            const int64_t row = (int64_t)m_blk * 256 + rank * 128 + quarter * 32 + lane;
+            // RES: a folded residual preloaded into the accumulator registers
+            // (zeros on a second split); the TMEM chunks add to it
+            const bool res_in_acc =
+                RES && load_residual<P_EPI_COLS>(p, row, bz, n_blk * 256 + half * P_EPI_COLS, first_split, acc);
+            if (RES && !res_in_acc)
+#pragma unroll
+                for (int j = 0; j < P_EPI_COLS; j++) acc[j] = 0.0f;
             for (int c = 0; c < n_chunks; c++, it++) {
                 const int b = it & 1;
                 const uint32_t acc_phase = (it >> 1) & 1;
@@ -615,16 +648,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                     ptx::tmem_ld_wait();
 #pragma unroll
                     for (int j = 0; j < 16; j++)
-                        acc[q * 16 + j] =
-                            c == 0 ? __uint_as_float(r[j]) : acc[q * 16 + j] + __uint_as_float(r[j]);
+                        acc[q * 16 + j] = c == 0 && !RES ? __uint_as_float(r[j])
+                                                         : acc[q * 16 + j] + __uint_as_float(r[j]);
                 }
                 ptx::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) ptx::mbar_arrive_cluster(acc_empty_leader0 + b * 8);
             }
             if (!ok) break;
-            const int64_t row = (int64_t)m_blk * 256 + rank * 128 + quarter * 32 + lane;
-            if (row < p.M) store_row<P_EPI_COLS, PLANES>(p, row, bz, n_blk * 256 + half * P_EPI_COLS, acc, first_split);
+            if (row < p.M)
+                store_row<P_EPI_COLS, PLANES>(p, row, bz, n_blk * 256 + half * P_EPI_COLS, acc, first_split, res_in_acc);
         }
     }
 
@@ -820,11 +853,13 @@ cudaError_t for_each_kernel(F f) {
         (const void*)tc_gemm_kernel<256, true, false>, (const void*)tc_gemm_kernel<256, false, false>,
         (const void*)tc_gemm_kernel<256, true, true>,  (const void*)tc_gemm_kernel<256, false, true>,
         (const void*)tc_gemm_kernel<128, true, false>, (const void*)tc_gemm_kernel<128, false, false>,
-        (const void*)tc_gemm_kernel<128, true, true>,  (const void*)tc_gemm_kernel<128, false, true>};
+        (const void*)tc_gemm_kernel<128, true, true>,  (const void*)tc_gemm_kernel<128, false, true>,
+        (const void*)tc_gemm_pair_kernel<true, false, true>, (const void*)tc_gemm_pair_kernel<false, false, true>};
     const int smem[] = {P_SMEM_BYTES, P_SMEM_BYTES, P_SMEM_BYTES, P_SMEM_BYTES,
                         GCfg<256>::SMEM_BYTES, GCfg<256>::SMEM_BYTES, GCfg<256>::SMEM_BYTES, GCfg<256>::SMEM_BYTES,
-                        GCfg<128>::SMEM_BYTES, GCfg<128>::SMEM_BYTES, GCfg<128>::SMEM_BYTES, GCfg<128>::SMEM_BYTES};
-    for (int i = 0; i < 12; i++) {
+                        GCfg<128>::SMEM_BYTES, GCfg<128>::SMEM_BYTES, GCfg<128>::SMEM_BYTES, GCfg<128>::SMEM_BYTES,
+                        P_SMEM_BYTES, P_SMEM_BYTES};
+    for (int i = 0; i < 14; i++) {
         cudaError_t e = f(ks[i], smem[i]);
         if (e != cudaSuccess) return e;
     }
@@ -833,7 +868,9 @@ cudaError_t for_each_kernel(F f) {
 
 template <bool CROSS, bool PLANES>
 void launch_tc_t(bool pair, int BN, int grid, const TcParams& prm, cudaStream_t st) {
-    if (pair)
+    if (pair && !PLANES && prm.res)
+        tc_gemm_pair_kernel<CROSS, false, true><<<2 * grid, THREADS, P_SMEM_BYTES, st>>>(prm);
+    else if (pair)
         tc_gemm_pair_kernel<CROSS, PLANES><<<2 * grid, THREADS, P_SMEM_BYTES, st>>>(prm);
     else if (BN == 128)
         tc_gemm_kernel<128, CROSS, PLANES><<<grid, THREADS, GCfg<128>::SMEM_BYTES, st>>>(prm);
@@ -982,6 +1019,7 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
     if (!(s = make_tmap(&prm.tb_lo, b_lo, p.K, p.N, p.batches, b_box, bk)).good()) return s;
     prm.c = f && f->out ? f->out : p.c;
     prm.bias = f && f->bias ? f->bias : p.bias;
+    prm.res = f ? f->res : nullptr;
     prm.alpha = p.alpha;
     prm.act = f ? f->act : 0;
     prm.plane_hi = f ? f->plane_hi : nullptr;
@@ -1006,7 +1044,20 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
     // persistent grid (two addends keep the fp32 sum order-independent).
     // (Not with a fused activation or split-plane output: both need the full sum.)
     prm.splits = 1;
-    const bool whole_sum = prm.act != 0 || prm.plane_hi != nullptr;
+    // A residual may be C itself (each element read, then written, by one
+    // thread) but not partly overlap it; in place it also rules out split-K
+    // (which zeroes C first).
+    bool res_in_c = false;
+    if (prm.res && prm.alpha != 1.0f) return Status::err(RT_ERR_ARGUMENT, "gemm: a residual needs alpha 1");
+    if (prm.res) {
+        const uintptr_t c0 = reinterpret_cast<uintptr_t>(prm.c), r0 = reinterpret_cast<uintptr_t>(prm.res);
+        const uintptr_t nb = (uintptr_t)p.batches * p.M * p.N * 4;
+        if (r0 < c0 + nb && c0 < r0 + nb) {
+            if (r0 != c0) return Status::err(RT_ERR_ARGUMENT, "gemm: residual partly overlaps the output");
+            res_in_c = true;
+        }
+    }
+    const bool whole_sum = prm.act != 0 || prm.plane_hi != nullptr || res_in_c;
     if (total < (int64_t)workers * 3 / 2 && prm.n_chunks >= 2 && split_k_enabled() && !whole_sum) {
         prm.splits = 2;
         RT_CUDA_CHECK(cudaMemsetAsync(prm.c, 0, (size_t)p.batches * p.M * p.N * 4, st));

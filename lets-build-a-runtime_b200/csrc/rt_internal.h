@@ -86,6 +86,7 @@ struct GemmFusion {
     const float* pre_hi = nullptr;  // this GEMM's A, already split
     const void* pre_x = nullptr;
     const float* bias = nullptr;    // bias to add (a node without one: a folded bias)
+    const float* res = nullptr;     // residual added after the bias (same layout as C): a folded ADD
 };
 Status launch_gemm(const OpNode& n, cudaStream_t st, Workspace ws, int* launches,
                    const GemmFusion* f = nullptr);
@@ -164,6 +165,7 @@ struct PlanItem {
     int64_t norm_planes_off = -1;  // LAYERNORM / RMSNORM: write the consumer GEMM's split A planes here
     int64_t attn_planes_off = -1;  // ATTENTION (merged-layout views): the same, from its O store
     int64_t epi_bias_off = -1;     // GEMM adds this merged bias (byte offset into the plan's bias buffer)
+    const void* epi_res = nullptr; // GEMM adds this residual (a folded same-shape ADD) and writes epi_out
     bool rope = false;             // this (ADD) node launches the fused norm + rotary kernel instead
     RopeFold rp{};
     bool gated = false;            // this GATED_ACT reads its inputs through `gv`

@@ -312,6 +312,7 @@ Status launch_item(Plan& p, size_t i, cudaStream_t st, int* launches) {
             f.act = it.epi_act;
             if (it.epi_bias_off >= 0) f.bias = reinterpret_cast<const float*>(p.bias + it.epi_bias_off);
             f.out = static_cast<float*>(it.epi_out);
+            f.res = static_cast<const float*>(it.epi_res);
             if (it.carry_off >= 0) {
                 f.plane_hi = reinterpret_cast<float*>(p.carry + it.carry_off);
                 f.plane_x = p.carry + it.carry_off + it.carry_plane_bytes;

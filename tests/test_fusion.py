@@ -189,3 +189,22 @@ def test_attention_writes_the_projection_split_operand(monkeypatch):
     monkeypatch.setenv("RT_FUSE_ATTN_SPLIT", "1")
     _, flags = report(prog, arr)
     assert [flags[i] for i in proj] == [4, 4]
+
+
+@pytest.mark.parametrize("name,adds", [("gpt2_b8", 4), ("qwen3_b8", 4), ("7b_b8", 2)])
+def test_residual_adds_fold_into_their_gemms(name, adds, monkeypatch):
+    """Each same-shape residual ADD right after a GEMM is skipped (flag 1) and
+    its GEMM (flag 3) adds the residual in the epilogue under
+    RT_FUSE_RESIDUAL=1; by default the ADDs run."""
+    monkeypatch.setenv("RT_FUSE_RESIDUAL", "1")
+    prog = Program.load(GOLDEN / f"{name}.json")
+    arr, _ = bind(prog)
+    _, flags = report(prog, arr)
+    ops = [nd.op for nd in prog.nodes]
+    res = [i for i, f in enumerate(flags) if f == 1 and ops[i] == OP["ADD"]]
+    assert len(res) == adds
+    assert all(prog.nodes[i].extra[0] == 1 and ops[i - 1] in (OP["MATMUL"], OP["MATMUL_ADD"]) and flags[i - 1] == 3
+               for i in res)
+    monkeypatch.delenv("RT_FUSE_RESIDUAL")
+    _, flags = report(prog, arr)
+    assert all(flags[i] == 0 for i in res)

@@ -105,10 +105,11 @@ def test_custom_block_bias_fold_unlocks_layout_fusion(name, gpu_executor_factory
         pytest.skip("no report")
     tc = flags[mm] == 3
     folded = [ops[i] for i, f in enumerate(flags) if f == 1]
+    bias_adds = [i for i, f in enumerate(flags) if f == 1 and ops[i] == OP["ADD"] and prog.nodes[i].extra[0] == 0]
     if not tc:   # GEMM below the tensor-core threshold: nothing to fold
         assert folded.count(OP["ADD"]) == 0
         return
-    assert folded.count(OP["ADD"]) == 3
+    assert len(bias_adds) == 3
     assert folded.count(OP["SLICE"]) == 3 and folded.count(OP["TRANSPOSE"]) == 4
     ins = prog.make_inputs(0)
     got = ex.run(ins)
@@ -142,15 +143,18 @@ def test_gated_activation_reads_slices_through_views(act, bias, gpu_executor_fac
     np.testing.assert_allclose(got, ref, rtol=2e-6, atol=2e-6)
 
 
+@pytest.mark.parametrize("residual", ["1", "0"])
 @pytest.mark.parametrize("attn_split", ["1", "0"])
-def test_attention_split_hand_off_matches_golden(attn_split, gpu_executor_factory, monkeypatch):
+def test_attention_split_hand_off_matches_golden(attn_split, residual, gpu_executor_factory, monkeypatch):
     """GPT-2 mini body at S = 300 (a partial last query block): the attention
     writes the projection GEMM's split A planes (RT_FUSE_ATTN_SPLIT=1) or its
-    plain output (0, the default) and the result matches the
-    reference executor's golden output."""
+    plain output (0, the default), with and without the residual ADDs folded
+    into the GEMMs, and the result matches the reference executor's golden
+    output."""
     from conftest import load_golden
     from test_gpu_programs import assert_parity
     monkeypatch.setenv("RT_FUSE_ATTN_SPLIT", attn_split)
+    monkeypatch.setenv("RT_FUSE_RESIDUAL", residual)   # with the residual fold the projection's flag is 3
     prog, ins, outs = load_golden("gpt2_mini_s300")
     ex = gpu_executor_factory(prog, prog.make_constants())
     got = ex.run(ins)
@@ -159,7 +163,10 @@ def test_attention_split_hand_off_matches_golden(attn_split, gpu_executor_factor
     flags = flags_of(ex, prog)
     ops = [nd.op for nd in prog.nodes]
     proj = [i for i, op in enumerate(ops) if op == OP["MATMUL_ADD"] and OP["ATTENTION"] in ops[max(0, i - 3):i]]
-    assert proj and all(flags[i] == (4 if attn_split == "1" else 0) for i in proj)
+    if residual == "0":
+        assert proj and all(flags[i] == (4 if attn_split == "1" else 0) for i in proj)
+    else:
+        assert proj and all(flags[i] == 3 and flags[i + 1] == 1 for i in proj)
 
 
 def test_attention_split_hand_off_3xtf32():
@@ -171,3 +178,42 @@ def test_attention_split_hand_off_3xtf32():
                         __file__, "-k", "test_attention_split_hand_off_matches_golden"],
                        env=dict(os.environ, RT_GEMM_3XTF32="1"), capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
+
+
+def residual_program(M, K, N, inplace, seed=0):
+    """x = c1 + c2 (arena) ; y = a @ w^T + b ; z = y + x -- z over x (inplace)
+    or in its own buffer.  The last ADD folds into the GEMM's epilogue."""
+    rng = np.random.default_rng(seed)
+    stored = {
+        "a": rng.standard_normal((M, K), dtype=np.float32),
+        "w": (rng.standard_normal((N, K)) * 0.05).astype(np.float32),
+        "b": rng.standard_normal(N).astype(np.float32) * 0.1,
+        "c1": rng.standard_normal((M, N), dtype=np.float32),
+        "c2": rng.standard_normal((M, N), dtype=np.float32),
+    }
+    consts = {k: ConstSpec(k, v.shape, "float32", {"kind": "stored"}) for k, v in stored.items()}
+    C = lambda n: Ref("const", n, 0)
+    A = lambda off: Ref("arena", None, off)
+    X, Y, Z = 0, M * N * 4, (0 if inplace else 2 * M * N * 4)
+    nodes = [ProgNode(OP["ADD"], [C("c1"), C("c2")], A(X), [M, N], 4, [1]),
+             ProgNode(OP["MATMUL_ADD"], [C("a"), C("w"), C("b")], A(Y), [M, N], 4, [K, 1, 1]),
+             ProgNode(OP["ADD"], [A(Y), A(X)], A(Z), [M, N], 4, [1])]
+    outs = {"z": {"shape": [M, N], "dtype": "float32", "ref": A(Z)}}
+    return Program(f"res{int(inplace)}", {}, 3 * M * N * 4, {}, outs, consts, nodes, stored)
+
+
+@pytest.mark.parametrize("inplace", [False, True])
+@pytest.mark.parametrize("M,K,N", [(1024, 768, 256), (300, 520, 192)])
+def test_residual_add_folded_into_gemm_matches_oracle(M, K, N, inplace, gpu_executor_factory, monkeypatch):
+    """With RT_FUSE_RESIDUAL=1 the GEMM adds the residual in its epilogue and
+    writes the ADD's output: into its own buffer (two-way split-K allowed:
+    the first split adds the residual) or over the residual itself (no
+    split-K), twice in a row."""
+    monkeypatch.setenv("RT_FUSE_RESIDUAL", "1")
+    prog = residual_program(M, K, N, inplace)
+    ex = gpu_executor_factory(prog, dict(prog.stored))
+    ref = oracle.run_program("restated", prog, dict(prog.stored), {})["z"]
+    for _ in range(2):
+        got = ex.run({})["z"]
+        np.testing.assert_allclose(got, ref, atol=1e-4, rtol=1e-3)
+    assert flags_of(ex, prog) == [0, 3, 1]
