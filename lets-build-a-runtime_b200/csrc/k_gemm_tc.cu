@@ -90,6 +90,8 @@ constexpr int ERR_PRODUCER = 0x101, ERR_MMA = 0x102, ERR_EPILOGUE = 0x103, ERR_D
 
 struct TcParams {
     CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;   // 3-D {K, rows, batches}
+    CUtensorMap tc;                           // C as 3-D {N, M, batches}, 32 x 32 boxes, 128-B swizzle
+    int c_tma;                                // pair kernel: C through shared memory and TMA stores
     float* c;
     const float* bias;
     const float* res;             // non-null: residual [batches*M][N] added after the bias (first split)
@@ -452,11 +454,13 @@ constexpr int P_BK = 32;
 constexpr int P_STAGES = 3;
 constexpr int P_TILE = 128 * P_BK * 4;                 // 16 KiB: one plane of 128 rows
 constexpr int P_STAGE_BYTES = 4 * P_TILE;              // A hi / A plane1 / B hi / B plane1
-constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
+constexpr int P_EPI_STAGE = 32 * 32 * 4;               // per epilogue warp: 32 rows x 32 columns of C
+constexpr int P_EPI_OFF = P_STAGES * P_STAGE_BYTES + 1024;   // after the barriers, 1024-aligned
+constexpr int P_SMEM_BYTES = P_EPI_OFF + 8 * P_EPI_STAGE + 1024;
 static_assert(P_SMEM_BYTES <= 232448, "shared memory budget");
 constexpr int P_EPI_COLS = 128;
 
-template <bool CROSS, bool PLANES, bool RES = false>
+template <bool CROSS, bool PLANES, bool RES = false, bool TMA = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     tc_gemm_pair_kernel(const __grid_constant__ TcParams p) {
     extern __shared__ uint8_t smem_raw[];
@@ -656,11 +660,47 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                 if (lane == 0) ptx::mbar_arrive_cluster(acc_empty_leader0 + b * 8);
             }
             if (!ok) break;
-            if (row < p.M)
+            if (TMA) {
+                // 32 columns at a time: this warp's 32 rows into its staging block
+                // (128-byte swizzle), then one TMA store (reduce-add under split-K)
+                uint8_t* stg = smem + P_EPI_OFF + (warp - 2) * P_EPI_STAGE;
+                const int col0 = n_blk * 256 + half * P_EPI_COLS;
+                const int row0 = m_blk * 256 + rank * 128 + quarter * 32;
+                const bool add_bias = p.bias && first_split;
+#pragma unroll
+                for (int c4 = 0; c4 < P_EPI_COLS / 32; c4++) {
+                    if (col0 + c4 * 32 >= p.N) continue;   // (not break: acc stays statically indexed)
+                    if (lane == 0) ptx::bulk_wait_read();   // the previous store has read the block
+                    __syncwarp();
+#pragma unroll
+                    for (int w = 0; w < 32; w += 4) {
+                        const int j = c4 * 32 + w, col = col0 + j;
+                        float4 v = make_float4(p.alpha * acc[j], p.alpha * acc[j + 1], p.alpha * acc[j + 2],
+                                               p.alpha * acc[j + 3]);
+                        if (add_bias && col < p.N) {   // N % 4 == 0 with a C tensor map
+                            const float4 bb = *reinterpret_cast<const float4*>(p.bias + col);
+                            v.x += bb.x; v.y += bb.y; v.z += bb.z; v.w += bb.w;
+                        }
+                        if (p.act == 1) {
+                            v.x = gelu_tanh(v.x); v.y = gelu_tanh(v.y); v.z = gelu_tanh(v.z); v.w = gelu_tanh(v.w);
+                        }
+                        *reinterpret_cast<float4*>(stg + lane * 128 + ((((w >> 2) ^ (lane & 7))) << 4)) = v;
+                    }
+                    ptx::fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        if (p.splits > 1) ptx::tma_reduce_add_3d(&p.tc, stg, col0 + c4 * 32, row0, bz);
+                        else ptx::tma_store_3d(&p.tc, stg, col0 + c4 * 32, row0, bz);
+                        ptx::bulk_commit();
+                    }
+                }
+            } else if (row < p.M) {
                 store_row<P_EPI_COLS, PLANES>(p, row, bz, n_blk * 256 + half * P_EPI_COLS, acc, first_split, res_in_acc);
+            }
         }
     }
 
+    if (TMA) ptx::bulk_wait_all();   // C stores done before the CTA's memory goes
     __syncthreads();
     if (threadIdx.x == 0 && leader && *abort_flag) {
         volatile int no_abort = 0;
@@ -854,12 +894,14 @@ cudaError_t for_each_kernel(F f) {
         (const void*)tc_gemm_kernel<256, true, true>,  (const void*)tc_gemm_kernel<256, false, true>,
         (const void*)tc_gemm_kernel<128, true, false>, (const void*)tc_gemm_kernel<128, false, false>,
         (const void*)tc_gemm_kernel<128, true, true>,  (const void*)tc_gemm_kernel<128, false, true>,
-        (const void*)tc_gemm_pair_kernel<true, false, true>, (const void*)tc_gemm_pair_kernel<false, false, true>};
+        (const void*)tc_gemm_pair_kernel<true, false, true>, (const void*)tc_gemm_pair_kernel<false, false, true>,
+        (const void*)tc_gemm_pair_kernel<true, false, false, true>,
+        (const void*)tc_gemm_pair_kernel<false, false, false, true>};
     const int smem[] = {P_SMEM_BYTES, P_SMEM_BYTES, P_SMEM_BYTES, P_SMEM_BYTES,
                         GCfg<256>::SMEM_BYTES, GCfg<256>::SMEM_BYTES, GCfg<256>::SMEM_BYTES, GCfg<256>::SMEM_BYTES,
                         GCfg<128>::SMEM_BYTES, GCfg<128>::SMEM_BYTES, GCfg<128>::SMEM_BYTES, GCfg<128>::SMEM_BYTES,
-                        P_SMEM_BYTES, P_SMEM_BYTES};
-    for (int i = 0; i < 14; i++) {
+                        P_SMEM_BYTES, P_SMEM_BYTES, P_SMEM_BYTES, P_SMEM_BYTES};
+    for (int i = 0; i < 16; i++) {
         cudaError_t e = f(ks[i], smem[i]);
         if (e != cudaSuccess) return e;
     }
@@ -870,6 +912,8 @@ template <bool CROSS, bool PLANES>
 void launch_tc_t(bool pair, int BN, int grid, const TcParams& prm, cudaStream_t st) {
     if (pair && !PLANES && prm.res)
         tc_gemm_pair_kernel<CROSS, false, true><<<2 * grid, THREADS, P_SMEM_BYTES, st>>>(prm);
+    else if (pair && !PLANES && prm.c_tma)
+        tc_gemm_pair_kernel<CROSS, false, false, true><<<2 * grid, THREADS, P_SMEM_BYTES, st>>>(prm);
     else if (pair)
         tc_gemm_pair_kernel<CROSS, PLANES><<<2 * grid, THREADS, P_SMEM_BYTES, st>>>(prm);
     else if (BN == 128)
@@ -1065,6 +1109,20 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
     // equal halves of the K blocks (each split accumulates its own TMEM chunks)
     prm.kb_split = (prm.k_blocks + prm.splits - 1) / prm.splits;
     prm.total_items = prm.total_tiles * prm.splits;
+    // Opt-in (RT_GEMM_TMA_STORE=1): C through shared memory and TMA stores
+    // (pair kernel, plain C output, no split-K).  Alone, the 8192 x 2304 and
+    // x 3072 (K = 768) GEMMs ran ~11 % faster than with per-row stores, but
+    // whole forwards did not move (GPT-2 1.398 / 1.397 ms, Qwen3 2.825 /
+    // 2.797, 7b 11.09 / 11.12), so per-row stores stay the default.
+    static const bool c_tma_on = [] {
+        const char* e = getenv("RT_GEMM_TMA_STORE");
+        return e && e[0] == '1';
+    }();
+    prm.c_tma = 0;
+    if (c_tma_on && pair && prm.splits == 1 && !prm.plane_hi && !prm.res && p.N % 4 == 0 && aligned16(prm.c)) {
+        if (!(s = encode_tmap_f32_3d(&prm.tc, prm.c, p.N, p.M, p.batches, 32, 32, 128)).good()) return s;
+        prm.c_tma = 1;
+    }
     prm.err = kernel_error_flag();
     const int grid = prm.total_items < workers ? prm.total_items : workers;
     launch_tc(pair, BN, cross_scheme(), prm.plane_hi != nullptr, grid, prm, st);

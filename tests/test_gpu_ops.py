@@ -255,6 +255,8 @@ def test_reshape_copy_and_embedding(gpu_executor_factory):
     {"RT_GEMM_3XTF32": "1"},                       # three tf32 MMAs (hi.hi + hi.lo + lo.hi)
     {"RT_GEMM_PAIR": "0"},                         # one-CTA kernel everywhere
     {"RT_GEMM_PAIR": "0", "RT_GEMM_3XTF32": "1"},
+    {"RT_GEMM_TMA_STORE": "1"},                    # C through shared memory and TMA stores
+    {"RT_GEMM_TMA_STORE": "1", "RT_GEMM_3XTF32": "1"},
 ], ids=lambda e: ",".join(f"{k}={v}" for k, v in e.items()))
 def test_matmul_variants(env):
     """The GEMM variants selected by environment switches (read once per
