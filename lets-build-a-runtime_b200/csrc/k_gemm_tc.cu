@@ -140,11 +140,11 @@ __device__ __forceinline__ bool load_residual(const TcParams& p, int64_t row, in
 // (plain store, or float4 atomics under split-K) or, for PLANES kernels, the
 // split A planes (a separate instantiation: the plane code's registers would
 // otherwise cost every GEMM's epilogue).
-template <int COLS, bool PLANES>
+template <int COLS, bool PLANES, bool RESID = true>
 __device__ __forceinline__ void store_row(const TcParams& p, int64_t row, int bz, int col0, const float* acc,
                                           bool first_split, bool res_in_acc) {
     const bool add_bias = p.bias && first_split;
-    const bool add_res = p.res && first_split && !res_in_acc;
+    const bool add_res = RESID && p.res && first_split && !res_in_acc;   // RESID: compiled in at all
     const int64_t r = (int64_t)bz * p.M + row;
     if (PLANES) {
         // N % 4 == 0 here (it is the K of the consuming GEMM); splits == 1
@@ -624,11 +624,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             const int n_chunks = (kb_hi - kb_lo + p.kb_per_chunk - 1) / p.kb_per_chunk;
             const bool first_split = kb_lo == 0;
             float acc[P_EPI_COLS];
-            const int64_t row = (int64_t)m_blk * 256 + rank * 128 + quarter * 32 + lane;
             // RES: a folded residual preloaded into the accumulator registers
             // (zeros on a second split); the TMEM chunks add to it
             const bool res_in_acc =
-                RES && load_residual<P_EPI_COLS>(p, row, bz, n_blk * 256 + half * P_EPI_COLS, first_split, acc);
+                RES && load_residual<P_EPI_COLS>(p, (int64_t)m_blk * 256 + rank * 128 + quarter * 32 + lane, bz,
+                                                 n_blk * 256 + half * P_EPI_COLS, first_split, acc);
             if (RES && !res_in_acc)
 #pragma unroll
                 for (int j = 0; j < P_EPI_COLS; j++) acc[j] = 0.0f;
@@ -694,8 +694,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                         ptx::bulk_commit();
                     }
                 }
-            } else if (row < p.M) {
-                store_row<P_EPI_COLS, PLANES>(p, row, bz, n_blk * 256 + half * P_EPI_COLS, acc, first_split, res_in_acc);
+            } else if (const int64_t row = (int64_t)m_blk * 256 + rank * 128 + quarter * 32 + lane; row < p.M) {
+                store_row<P_EPI_COLS, PLANES, RES>(p, row, bz, n_blk * 256 + half * P_EPI_COLS, acc, first_split,
+                                                   res_in_acc);
             }
         }
     }
