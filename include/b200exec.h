@@ -185,23 +185,38 @@ int rt_fusion_report(const OpNode* nodes, int n_nodes, int* flags);
 /* ---- allocation-free GEMM ------------------------------------------------ */
 /* No counterpart in the reference.  C[M,N] = alpha * A[M,K] . op(B) + bias
  * (bias may be NULL; op(B) = B^T when trans_b, B stored [N,K], else B [K,N]),
- * computed by the same 3xTF32 tensor-core kernel as MATMUL/MATMUL_ADD, for
- * callers that may not allocate device memory (host callbacks, allocator
- * hooks, plugins whose host owns every device allocation).  It allocates
- * nothing and needs no rt_init: it runs on the current device and `stream`
- * (a cudaStream_t; NULL = legacy default stream) and returns after C is
- * written.  Scratch: a fixed RT_NOALLOC_SCRATCH_BYTES device array inside
- * the library (held by every GPU that loads it), so 8*(M*K + N*K) bytes
- * must fit: larger problems return RT_ERR_OUT_OF_RANGE; K % 4 != 0 returns
- * RT_ERR_UNSUPPORTED.  The first call on each device performs a one-time
- * set-up (symbol address, kernel attribute): make it before any stream
- * capture.  All calls share the scratch: calls that overlap on the GPU race.
- * Returns an RT_* status (not recorded in rt_last_error). */
+ * computed by the same split-operand tensor-core kernel as MATMUL/MATMUL_ADD
+ * (tf32 hi.hi product plus bf16 cross terms), for callers that may not
+ * allocate device memory: plugins whose host application owns every device
+ * allocation through its own pool, and processes that must not grow their
+ * device footprint after start-up.  It allocates nothing and needs no
+ * rt_init: it runs on the current device and `stream` (a cudaStream_t;
+ * NULL = legacy default stream).  It is synchronous: it waits for `stream`
+ * and returns after C is written, so it is a host-thread call, not one for a
+ * CUDA host callback (which may not call CUDA).  Scratch: a fixed
+ * RT_NOALLOC_SCRATCH_BYTES device array inside the library (held by every
+ * GPU that loads it), so 8*(M*K + N*K) bytes must fit: larger problems
+ * return RT_ERR_OUT_OF_RANGE; K % 4 != 0 returns RT_ERR_UNSUPPORTED.  A C
+ * or bias off a 16-byte boundary is written / read with scalar accesses.
+ * The first call on each device performs a one-time set-up (symbol address,
+ * kernel attribute): make it before any stream capture.  All calls share
+ * the scratch: calls that overlap on the GPU race.  Launches are checked
+ * with cudaGetLastError, so an error left pending by earlier CUDA work of
+ * the caller is reported as this call's RT_ERR_CUDA.  Returns an RT_*
+ * status (not recorded in rt_last_error). */
 #define RT_NOALLOC_SCRATCH_BYTES (32u << 20)
 int rt_matmul_noalloc(const float* a, const float* b, const float* bias, float* c,
                       int M, int N, int K, int trans_b, float alpha, void* stream);
 
 /* ---- errors ------------------------------------------------------------- */
+/* No counterpart in the reference (which never waits on the device).  Runs
+ * one kernel whose single bounded mbarrier wait is never satisfied, with a
+ * limit of limit_ns (0 < limit_ns <= 1 s), through the same bounded-wait code
+ * as the tensor-core kernels.  Returns RT_ERR_KERNEL_TIMEOUT (and records
+ * it) when the timeout path works: the kernel records a code, returns, and
+ * the context stays usable.  No fault, trap or hang is involved. */
+int rt_check_wait_timeout(unsigned long long limit_ns);
+
 int rt_last_error(void);                  /* status of the last failing call; 0 if none */
 const char* rt_last_error_message(void);
 void rt_clear_error(void);

@@ -231,7 +231,11 @@ Status decode_attention(const OpNode& n, AttnParams* out, int64_t* BH_out, bool*
 }
 
 bool use_tc(const AttnParams& p, int64_t BH, bool has_mask) {
-    return attention_tc_applicable(p.S, p.D, has_mask, BH) && aligned16(p.q) && aligned16(p.o);
+    // K and V are read as 16-byte vectors by the pack pass, Q by a tensor map
+    // and O by vector stores: all four must start on a 16-byte boundary
+    // (planner offsets need not), else the CUDA-core kernel runs.
+    return attention_tc_applicable(p.S, p.D, has_mask, BH) && aligned16(p.q) && aligned16(p.o) &&
+           aligned16(p.k) && aligned16(p.v);
 }
 
 }  // namespace

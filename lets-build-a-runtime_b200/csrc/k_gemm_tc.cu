@@ -92,6 +92,7 @@ struct TcParams {
     CUtensorMap ta_hi, ta_lo, tb_hi, tb_lo;   // 3-D {K, rows, batches}
     CUtensorMap tc;                           // C as 3-D {N, M, batches}, 32 x 32 boxes, 128-B swizzle
     int c_tma;                                // pair kernel: C through shared memory and TMA stores
+    int vec_c;                                // 16-byte row accesses: N % 4 == 0 and C, bias, residual 16-byte aligned
     float* c;
     const float* bias;
     const float* res;             // non-null: residual [batches*M][N] added after the bias (first split)
@@ -125,7 +126,7 @@ __device__ __forceinline__ uint16_t bf16_bits(float x) {
 template <int COLS>
 __device__ __forceinline__ bool load_residual(const TcParams& p, int64_t row, int bz, int col0, bool first_split,
                                               float* acc) {
-    if (!first_split || row >= p.M || (p.N & 3) != 0 || col0 + COLS > p.N) return false;
+    if (!first_split || row >= p.M || !p.vec_c || col0 + COLS > p.N) return false;
     const float* src = p.res + ((int64_t)bz * p.M + row) * p.N + col0;
 #pragma unroll
     for (int j = 0; j < COLS; j += 4) {
@@ -183,7 +184,7 @@ __device__ __forceinline__ void store_row(const TcParams& p, int64_t row, int bz
         return;
     }
     float* crow = p.c + r * p.N;
-    if ((p.N & 3) == 0 && col0 + COLS <= p.N) {
+    if (p.vec_c && col0 + COLS <= p.N) {
 #pragma unroll
         for (int j = 0; j < COLS; j += 4) {
             float4 v = make_float4(p.alpha * acc[j], p.alpha * acc[j + 1], p.alpha * acc[j + 2],
@@ -1066,6 +1067,10 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
     prm.bias = f && f->bias ? f->bias : p.bias;
     prm.res = f ? f->res : nullptr;
     prm.alpha = p.alpha;
+    // Planner offsets are raw byte counts (first fit), so C, a bias or a
+    // residual may sit off a 16-byte boundary: those rows take scalar accesses.
+    prm.vec_c = p.N % 4 == 0 && aligned16(prm.c) && (!prm.bias || aligned16(prm.bias)) &&
+                (!prm.res || aligned16(prm.res));
     prm.act = f ? f->act : 0;
     prm.plane_hi = f ? f->plane_hi : nullptr;
     prm.plane_x = f ? static_cast<uint8_t*>(f->plane_x) : nullptr;
@@ -1120,7 +1125,7 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
         return e && e[0] == '1';
     }();
     prm.c_tma = 0;
-    if (c_tma_on && pair && prm.splits == 1 && !prm.plane_hi && !prm.res && p.N % 4 == 0 && aligned16(prm.c)) {
+    if (c_tma_on && pair && prm.splits == 1 && !prm.plane_hi && !prm.res && prm.vec_c) {
         if (!(s = encode_tmap_f32_3d(&prm.tc, prm.c, p.N, p.M, p.batches, 32, 32, 128)).good()) return s;
         prm.c_tma = 1;
     }
@@ -1138,12 +1143,14 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
 // rt_matmul_noalloc: the same tensor-core GEMM for callers that cannot
 // allocate device memory.
 //
-// Who needs it: code that runs where cudaMalloc is off limits -- inside a
-// host callback or an allocator hook, a plugin whose host application owns
-// all device memory through its own pool, or a process that must not grow
-// its footprint after start-up.  rt_execute plans a workspace per node array
-// (cudaMalloc), so those callers use this entry point instead.  It needs no
-// rt_init either: it works on the current device and the stream it is given.
+// Who needs it: code that runs where cudaMalloc is off limits -- a plugin
+// whose host application owns all device memory through its own pool, or a
+// process that must not grow its device footprint after start-up.
+// rt_execute plans a workspace per node array (cudaMalloc), so those callers
+// use this entry point instead.  It needs no rt_init either: it works on the
+// current device and the stream it is given.  It is synchronous (it waits
+// for that stream before returning), so it belongs on a host thread, not in
+// a CUDA host callback, which may not call CUDA at all.
 //
 // Its scratch (the hi/lo split copies of both operands) lives in the file-
 // scope device array below, NOALLOC_SCRATCH_BYTES (32 MiB) per GPU that loads
@@ -1154,8 +1161,11 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
 // that device is current -- that first call also sets the kernel's shared-
 // memory attribute, so make it before any stream capture.  Nothing in the
 // scratch has to start at zero (every word read is written first by the
-// same call).  All calls share the one array, so calls whose GPU work
-// overlaps (different streams, or host threads) race on it.
+// same call); the error word is cleared on the stream at the start of every
+// call.  All calls share the one array, so calls whose GPU work overlaps
+// (different streams, or host threads) race on it.  Each launch is checked
+// with cudaGetLastError, which also returns an error that earlier CUDA work
+// of the caller left pending: that is reported as this call's RT_ERR_CUDA.
 // ===========================================================================
 namespace rt {
 namespace {
@@ -1242,6 +1252,7 @@ extern "C" int rt_matmul_noalloc(const float* a, const float* b, const float* bi
     prm.c = c;
     prm.bias = bias;
     prm.alpha = alpha;
+    prm.vec_c = N % 4 == 0 && aligned16(c) && (!bias || aligned16(bias));
     prm.M = M;
     prm.N = N;
     prm.K = K;
@@ -1261,10 +1272,14 @@ extern "C" int rt_matmul_noalloc(const float* a, const float* b, const float* bi
     int grid = prm.total_tiles < d->sms ? prm.total_tiles : d->sms;
     tc_gemm_kernel<256, true, false><<<grid, THREADS, GCfg<256>::SMEM_BYTES, st>>>(prm);
     if (cudaGetLastError() != cudaSuccess) return RT_ERR_CUDA;
-    // synchronous: returns once C is written, and reports a kernel that gave up a wait
-    if (cudaStreamSynchronize(st) != cudaSuccess) return RT_ERR_CUDA;
+    // synchronous: returns once C is written, and reports a kernel that gave
+    // up a wait.  The error word comes back on the caller's stream (pageable
+    // destination: the copy completes before the synchronize returns), so
+    // the call never waits on work queued on other streams.
     int kerr = 0;
-    if (cudaMemcpyFromSymbol(&kerr, g_noalloc_error, sizeof(int)) != cudaSuccess) return RT_ERR_CUDA;
+    if (cudaMemcpyAsync(&kerr, d->error, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess)
+        return RT_ERR_CUDA;
+    if (cudaStreamSynchronize(st) != cudaSuccess) return RT_ERR_CUDA;
     return kerr ? RT_ERR_KERNEL_TIMEOUT : RT_OK;
 }
 

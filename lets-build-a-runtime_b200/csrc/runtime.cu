@@ -20,7 +20,9 @@
 #include <unordered_map>
 #include <vector>
 
+#include "gemm.h"
 #include "rt_internal.h"
+#include "sm100_ptx.h"
 
 namespace rt {
 
@@ -225,13 +227,33 @@ Status validate_node(const OpNode& n, int i) {
                 for (int k = 1; k < required; k++) need[k] = C * 4;
             }
             break;
-        case RT_OP_MATMUL: case RT_OP_MATMUL_ADD:
+        case RT_OP_MATMUL: case RT_OP_MATMUL_ADD: {
+            // A [batches][M][K], B [N][K] or [K][N] (one per batch unless
+            // b_is_2d), bias [N] -- csrc/executor.c:197-224, :312-346
             required = n.op == RT_OP_MATMUL ? 2 : 3;
+            GemmProblem g;
+            if (n.n_inputs >= required && decode_gemm(n, &g).good()) {
+                need[0] = (size_t)(g.batches * g.M * g.K) * 4;
+                need[1] = (size_t)(g.batches * g.N * g.K) * 4;
+                if (required == 3) need[2] = (size_t)g.N * 4;
+                if (g.M == 0) need[0] = 1;
+            }
             break;
-        case RT_OP_ATTENTION:
+        }
+        case RT_OP_ATTENTION: {
+            // Q/O [BH][S][D], K/V [BH/group][S][D], mask [BH][S][S] --
+            // csrc/executor.c:371-397, csrc/ops/attn.c:64-80, :238-253
             required = 3 + (n.extra[3] ? 1 : 0);
-            if (n.n_inputs >= 1) need[0] = out_bytes;
+            const int64_t S = n.extra[0], D = n.extra[1], group = n.extra[4] > 0 ? n.extra[4] : 1;
+            int64_t BH = 1;
+            for (int d = 0; d < n.n_dims - 2; d++) BH *= n.out_shape[d];
+            if (n.n_inputs >= required && S > 0 && D > 0 && BH % group == 0) {
+                need[0] = out_bytes;
+                need[1] = need[2] = (size_t)((BH / group) * S * D) * 4;
+                if (n.extra[3]) need[3] = (size_t)(BH * S * S) * 4;
+            }
             break;
+        }
         case RT_OP_CAT:
             required = n.n_inputs;
             break;
@@ -586,6 +608,24 @@ int take_kernel_error() {
     int v = *S().kerr_host;
     if (v) *S().kerr_host = 0;
     return v;
+}
+
+// A wait that nothing will ever complete: one thread waits on an mbarrier
+// that no thread arrives on, through the same bounded wait the tensor-core
+// kernels use.  After limit_ns it records ERR_PROBE in the error word and
+// returns; it exercises the timeout path without any fault.
+constexpr int ERR_PROBE = 0x301;
+__global__ void unsatisfied_wait_kernel(uint64_t limit_ns, int* err) {
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        ptx::mbar_init(&bar, 1);
+        abort_flag = 0;
+        ptx::fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) ptx::wait_bounded(&bar, 0, &abort_flag, err, ERR_PROBE, limit_ns);
+    __syncthreads();
 }
 
 }  // namespace rt
@@ -992,6 +1032,21 @@ int rt_fusion_report(const OpNode* nodes, int n, int* skipped) {
         count += items[i].skip;
     }
     return count;
+}
+
+int rt_check_wait_timeout(unsigned long long limit_ns) {
+    RT_GUARD;
+    RT_NEED_INIT;
+    if (limit_ns == 0 || limit_ns > 1000000000ull) return fail(RT_ERR_ARGUMENT, "limit_ns must be in (0, 1 s]");
+    cudaStream_t st = S().stream;
+    unsatisfied_wait_kernel<<<1, 32, 0, st>>>((uint64_t)limit_ns, kernel_error_flag());
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(RT_ERR_CUDA, std::string("launch: ") + cudaGetErrorString(e));
+    e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return fail(RT_ERR_CUDA, std::string("wait probe: ") + cudaGetErrorString(e));
+    if (int k = take_kernel_error())
+        return fail(RT_ERR_KERNEL_TIMEOUT, "a kernel abandoned a bounded wait, code " + std::to_string(k));
+    return RT_OK;
 }
 
 int rt_last_error(void) { return S().last_error; }

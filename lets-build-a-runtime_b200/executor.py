@@ -72,7 +72,7 @@ def load_library(path: str | Path | None = None) -> ctypes.CDLL:
         "rt_protect": ([vp, sz], i), "rt_unprotect_all": ([], i),
         "rt_release": ([ctypes.POINTER(COpNode), i], i), "rt_plan_count": ([], i),
         "rt_last_error": ([], i), "rt_last_error_message": ([], ctypes.c_char_p),
-        "rt_clear_error": ([], None),
+        "rt_clear_error": ([], None), "rt_check_wait_timeout": ([ctypes.c_ulonglong], i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)

@@ -25,10 +25,17 @@ RESTATED_SO = HERE / "_build" / "liboracle.so"
 REFERENCE_SO = HERE / "_ref" / "libexecutor.so"
 
 
+def reference_root() -> Path:
+    """The reference checkout: $REF_ROOT, else a `reference` directory beside
+    this repository (it is absent on machines that only run the tests)."""
+    env = os.environ.get("REF_ROOT")
+    return Path(env) if env else HERE.parent.parent / "reference"
+
+
 def build(reference_tree: str | None = None) -> None:
     """Compile the restatement, and the reference when its tree is present."""
     subprocess.run(["make", "-s", "-C", str(HERE), "restate"], check=True)
-    ref = reference_tree or os.environ.get("REF_CSRC", "/root/reference/csrc")
+    ref = reference_tree or os.environ.get("REF_CSRC") or str(reference_root() / "csrc")
     if Path(ref).is_dir():
         subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF_CSRC={ref}"], check=True)
 

@@ -1,6 +1,6 @@
 """Generate the committed program fixtures (test infrastructure).
 
-Run in a container that has the reference tree (default /root/reference,
+Run in a container that has the reference tree (default: `reference` beside the repo,
 override with REF_ROOT) and the oracle build of its C executor
 (``make -C oracle ref``):
 
@@ -38,7 +38,7 @@ import torch.nn.functional as F
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
-REF_ROOT = Path(os.environ.get("REF_ROOT", "/root/reference"))
+REF_ROOT = Path(os.environ.get("REF_ROOT") or REPO.parent / "reference")
 sys.path.insert(0, str(REF_ROOT))
 
 _spec = importlib.util.spec_from_file_location(

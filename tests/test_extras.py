@@ -9,7 +9,9 @@ import sys
 import numpy as np
 import pytest
 
-REF_ROOT = os.environ.get("REF_ROOT", "/root/reference")
+import oracle
+
+REF_ROOT = str(oracle.reference_root())
 if os.path.isdir(REF_ROOT) and REF_ROOT not in sys.path:
     sys.path.insert(0, REF_ROOT)
 runtime = pytest.importorskip("runtime")

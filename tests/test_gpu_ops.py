@@ -282,3 +282,27 @@ def test_attention_3xtf32_variant():
                         __file__, "-k", "test_attention and not variant"],
                        env=dict(os.environ, RT_ATTN_3XTF32="1"), capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
+
+
+@pytest.mark.parametrize("M,N,K,splitk", [(1024, 512, 256, False), (512, 256, 2048, True)])
+def test_matmul_add_misaligned_output_and_bias(M, N, K, splitk, gpu_executor_factory):
+    """The planner's first-fit offsets are raw byte counts (runtime/planner.py:
+    470-477): a MATMUL_ADD whose output and bias start 4 bytes past a 16-byte
+    boundary must run on the tensor-core kernel's scalar-store path and match
+    the oracle (the second shape takes split-K)."""
+    from lbr_b200.program import ConstSpec, ProgNode, Program, Ref
+    a = rand(M, K)
+    w = rand(N, K) * 0.05
+    bias_padded = rand(N + 1)
+    consts = {"a": ConstSpec("a", a.shape, "float32", {"kind": "stored"}),
+              "w": ConstSpec("w", w.shape, "float32", {"kind": "stored"}),
+              "bias": ConstSpec("bias", bias_padded.shape, "float32", {"kind": "stored"})}
+    node = ProgNode(OP["MATMUL_ADD"], [Ref("const", "a", 0), Ref("const", "w", 0), Ref("const", "bias", 4)],
+                    Ref("arena", None, 4), [M, N], 4, [K, 1, 1])
+    prog = Program("misaligned", {}, M * N * 4 + 256, {},
+                   {"y": {"shape": [M, N], "dtype": "float32", "ref": Ref("arena", None, 4)}},
+                   consts, [node], {"a": a, "w": w, "bias": bias_padded})
+    got, ref = run_both(gpu_executor_factory, prog)
+    np.testing.assert_allclose(got, ref, atol=1e-4, rtol=1e-3)
+    exact = a.astype(np.float64) @ w.astype(np.float64).T + bias_padded[1:]
+    np.testing.assert_allclose(got, exact, atol=1e-4, rtol=1e-3)

@@ -9,6 +9,7 @@ from pathlib import Path
 import numpy as np
 import pytest
 
+import oracle
 from conftest import GOLDEN, ROOT
 from lbr_b200.copnode import COpNode, HostBinding
 from lbr_b200.program import OP, Program
@@ -79,7 +80,7 @@ def test_host_binding_points_into_arena():
             assert hb.nodes[i].output == base + n.output.offset
 
 
-REF = Path(os.environ.get("REF_ROOT", "/root/reference"))
+REF = oracle.reference_root()
 
 
 @pytest.mark.skipif(not (REF / "runtime").is_dir(), reason="reference tree not present")

@@ -1,17 +1,19 @@
 """rt_matmul_noalloc: the tensor-core GEMM for callers that may not allocate.
 
-Some callers of this library cannot call cudaMalloc at all -- a host
-callback or allocator hook running inside the CUDA runtime, or a plugin whose
-host application owns every device allocation through its own pool.  For
-them rt_matmul_noalloc runs the same 3xTF32 tensor-core GEMM as a
+Some callers of this library cannot call cudaMalloc at all -- a plugin whose
+host application owns every device allocation through its own pool, or a
+process whose device footprint is fixed once it has started.  For them
+rt_matmul_noalloc runs the same split-operand tensor-core GEMM as a
 MATMUL / MATMUL_ADD node, with its scratch in a fixed 32 MiB device array
 inside the library instead of a workspace the runtime allocates.
 
-This test calls it through the C ABI twice in a row (different operands, so
-stale scratch from the first call would show) and compares each result with
-the existing entry point, `rt_execute` on a one-node array, within the
-tolerance the other GEMM tests use.  It lives in its own file, named to be
-collected last, and works in a fresh process as well as after the others.
+The first test calls it through the C ABI twice in a row (different
+operands, so stale scratch from the first call would show) and compares each
+result with the existing entry point, `rt_execute` on a one-node array,
+within the tolerance the other GEMM tests use.  Another runs it in a fresh
+child process that never calls rt_init, on a stream and device memory that
+PyTorch owns, with alpha != 1 and no bias, against an fp64 product.  The file
+is named to be collected last, and works alone as well as after the others.
 """
 
 import ctypes
@@ -99,3 +101,50 @@ def test_noalloc_rejects_oversize_and_ragged_k(lib):
     assert lib.rt_matmul_noalloc(dummy, dummy, None, dummy, 64, 64, 66, 1, 1.0, None) == \
         RT_ERR_UNSUPPORTED
     lib.rt_free(dummy)
+
+
+CHILD = r"""
+import ctypes, sys
+import numpy as np
+import torch
+sys.path.insert(0, sys.argv[1])
+from __graft_entry__ import load_package
+load_package()
+from lbr_b200.executor import load_library
+
+lib = load_library()          # no rt_init: the entry point must not need it
+f = lib.rt_matmul_noalloc
+f.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int] * 4 + [ctypes.c_float, ctypes.c_void_p]
+f.restype = ctypes.c_int
+torch.cuda.set_device(0)
+st = torch.cuda.Stream()
+g = torch.Generator().manual_seed(3)
+M, N, K, alpha = 520, 384, 640, 0.37
+for call in range(2):
+    a = torch.randn(M, K, generator=g)
+    b = torch.randn(K, N, generator=g) * 0.05
+    da, db = a.cuda(), b.cuda()          # torch's caching allocator owns these
+    dc = torch.full((M, N), float("nan"), device="cuda")
+    torch.cuda.synchronize()
+    rc = f(da.data_ptr(), db.data_ptr(), None, dc.data_ptr(), M, N, K, 0, alpha, st.cuda_stream)
+    assert rc == 0, f"status {rc}"
+    got = dc.cpu().numpy()
+    truth = alpha * (a.double().numpy() @ b.double().numpy())
+    err = float(np.abs(got - truth).max())
+    assert np.allclose(got, truth, atol=1e-4, rtol=1e-3), f"call {call}: max abs {err:.3e}"
+    print(f"call {call}: max abs vs fp64 {err:.3e}")
+print("ok")
+"""
+
+
+def test_noalloc_fresh_process_without_rt_init():
+    """A caller that never touched rt_init: current device, its own stream and
+    PyTorch-owned buffers; alpha != 1 and bias NULL, checked against fp64."""
+    if not has_gpu():
+        pytest.skip("no CUDA device")
+    import subprocess
+    import sys
+    from conftest import ROOT
+    r = subprocess.run([sys.executable, "-c", CHILD, str(ROOT)], capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
