@@ -2,6 +2,7 @@
 // (an activation applied in a GEMM epilogue and in the stand-alone kernel).
 #pragma once
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <stdint.h>
 
 namespace rt {
@@ -53,6 +54,41 @@ __device__ __forceinline__ void store_split4(float* hi_row, uint16_t* x_row, int
     uint16_t* blk = x_row + kb * 32;
     *reinterpret_cast<uint2*>(blk + j) = make_uint2(bf16_pair(h.x, h.y), bf16_pair(h.z, h.w));
     *reinterpret_cast<uint2*>(blk + w + j) = make_uint2(bf16_pair(l.x, l.y), bf16_pair(l.z, l.w));
+}
+
+// ---- fp16 split (the default GEMM operand form) -----------------------------
+// An operand row x is scaled by a power of two 2^e so that its largest
+// magnitude lies in [2^14, 2^15) (exact: only the exponent changes), then
+// written as h = fp16(x 2^e) and l = fp16(x 2^e - h): |x 2^e - h - l| <=
+// 2^-22 |x 2^e|, and the MMA products h.h, h.l, l.h are exact in fp32.  The
+// GEMM multiplies its result by 2^-e (per A row, per B tensor).  Elements far
+// below the row maximum lose relative precision once h or l turns subnormal,
+// but never more than ~2^-39 of the row maximum in absolute terms.
+//
+// e for a maximum magnitude m (0 when m is 0, subnormal-small or not finite).
+__device__ __forceinline__ int f16_scale_exp(float m) {
+    const uint32_t eb = (__float_as_uint(m) >> 23) & 0xffu;
+    if (!(m > 0.0f) || eb == 0xffu) return 0;
+    const int e = 141 - (int)eb;                 // m in [2^(eb-127), 2^(eb-126)) -> [2^14, 2^15)
+    return e < -120 ? -120 : (e > 120 ? 120 : e);
+}
+__device__ __forceinline__ float pow2i(int e) { return __uint_as_float((uint32_t)(127 + e) << 23); }
+__device__ __forceinline__ uint32_t f16_hl(float x, uint16_t* lo) {
+    const __half h = __float2half_rn(x);
+    *lo = __half_as_ushort(__float2half_rn(x - __half2float(h)));
+    return __half_as_ushort(h);
+}
+// Four consecutive elements k..k+3 (k % 4 == 0, already scaled) of a row into
+// its fp16 plane: per 16-wide K block 32 halves, [h(16) | l(16)] when
+// first_hi (A operands), [l(16) | h(16)] otherwise (B operands).
+__device__ __forceinline__ void store_f16x4(uint16_t* row, int64_t k, float4 v, bool first_hi) {
+    uint16_t l0, l1, l2, l3;
+    const uint32_t h0 = f16_hl(v.x, &l0), h1 = f16_hl(v.y, &l1), h2 = f16_hl(v.z, &l2), h3 = f16_hl(v.w, &l3);
+    const uint2 hh = make_uint2(h0 | (h1 << 16), h2 | (h3 << 16));
+    const uint2 ll = make_uint2((uint32_t)l0 | ((uint32_t)l1 << 16), (uint32_t)l2 | ((uint32_t)l3 << 16));
+    uint16_t* blk = row + (k >> 4) * 32 + (k & 15);
+    *reinterpret_cast<uint2*>(blk + (first_hi ? 0 : 16)) = hh;
+    *reinterpret_cast<uint2*>(blk + (first_hi ? 16 : 0)) = ll;
 }
 
 }  // namespace rt

@@ -802,7 +802,7 @@ void plan_gemm_chains(const Analysis& an, const Effective& e, std::vector<PlanIt
         if (dbg()) fprintf(stderr, "[fusion] gemm %d: GELU %d folded into the epilogue\n", g, u);
 
         const char* hv = getenv("RT_FUSE_HANDOFF");   // read per plan
-        if (!(hv && hv[0] == '1')) continue;
+        if (!(hv && hv[0] == '1') || !gemm_planes_from_epilogues()) continue;
         const int k = next_reader(u, U);
         if (k < 0) continue;
         const OpNode& kn = an.nodes[k];
@@ -1100,7 +1100,7 @@ std::vector<PlanItem> plan_fusions(const std::vector<OpNode>& nodes,
             if (fusion_enabled() && norm_handoff) plan_norm_handoffs(an, e, items, protect, carry_alloc);
             const char* av = getenv("RT_FUSE_ATTN_SPLIT");   // read per plan; opt-in (see plan_attn_handoffs)
             const bool attn_handoff = av && av[0] == '1';
-            if (fusion_enabled() && attn_handoff) plan_attn_handoffs(an, e, items, protect, carry_alloc);
+            if (fusion_enabled() && attn_handoff && gemm_planes_from_epilogues()) plan_attn_handoffs(an, e, items, protect, carry_alloc);
             if (carry_bytes) *carry_bytes = (size_t)carry_alloc.total;
             break;
         }

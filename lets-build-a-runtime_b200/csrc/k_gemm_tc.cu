@@ -57,6 +57,7 @@
 #include <cuda_bf16.h>
 #include <stdlib.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "dev_math.h"
@@ -74,16 +75,22 @@ constexpr int EPI_WARPS = 8;                          // 2 warps per TMEM lane q
 constexpr int THREADS = 64 + 32 * EPI_WARPS;          // producer + MMA + epilogue
 constexpr int A_TILE = BM * BK * 4;                   // 8 KiB
 
-// N tile 256 (4-stage ring of 48 KiB) or 128 (6 stages of 32 KiB); the host
-// picks per problem whichever fills the machine in fewer tile waves.
-template <int BN_>
+// Operand schemes (see the file comment): three tf32 MMAs, tf32 + bf16
+// cross terms, or three fp16 MMAs over one scaled fp16 plane per operand.
+constexpr int SCH_3XTF32 = 0, SCH_CROSS = 1, SCH_F16 = 2;
+
+// N tile 256 or 128.  tf32 schemes: two 4-byte planes per operand, a 4-stage
+// ring of 48 KiB (N 256) or 6 stages of 32 KiB; fp16: one plane, 8 stages of
+// 24 KiB or 12 of 16 KiB.  K per stage: 16 (64-byte rows, 64-byte swizzle).
+template <int BN_, int SCH>
 struct GCfg {
     static constexpr int BN = BN_;
-    static constexpr int STAGES = BN_ == 256 ? 4 : 6;
+    static constexpr bool F16 = SCH == SCH_F16;
+    static constexpr int STAGES = F16 ? (BN_ == 256 ? 8 : 12) : (BN_ == 256 ? 4 : 6);
     static constexpr int EPI_COLS = BN_ / 2;
     static constexpr int B_TILE = BN_ * BK * 4;
-    static constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+    static constexpr int STAGE_BYTES = (F16 ? 1 : 2) * (A_TILE + B_TILE);
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 512 /*barriers*/;
 };
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;     // 2 s per wait
 constexpr int ERR_PRODUCER = 0x101, ERR_MMA = 0x102, ERR_EPILOGUE = 0x103, ERR_DRAIN = 0x104;
@@ -103,6 +110,8 @@ struct TcParams {
     int splits, kb_split;         // split-K: work item = (tile, split); split s covers K blocks [s*kb_split, ...)
     int total_items;              // total_tiles * splits
     int act;                      // 1: tanh-GELU after alpha and bias
+    const float* a_scale;         // fp16 scheme: 2^-e per A row ([batches*M]); null = 1
+    const float* b_scale;         // fp16 scheme: 2^-e of the whole B operand (one float); null = 1
     float* plane_hi;              // non-null: write the result as split A planes (hi, plane 1) of a
     uint8_t* plane_x;             //   later GEMM instead of C (row-major [batches*M][N])
     int plane_mode;               //   plane 1: 0 = lo (fp32), 1 = cross (bf16 [hi | lo] per 16 block)
@@ -136,8 +145,19 @@ __device__ __forceinline__ bool load_residual(const TcParams& p, int64_t row, in
     return true;
 }
 
+// Factor applied to the accumulator of output row `row` (batch bz) as the
+// TMEM chunks are summed: alpha, times the fp16 scheme's 2^-e of the A row
+// and of the B operand.
+__device__ __forceinline__ float epi_factor(const TcParams& p, int64_t row, int bz) {
+    float f = p.alpha;
+    if (p.a_scale && row < p.M) f *= p.a_scale[(int64_t)bz * p.M + row];
+    if (p.b_scale) f *= *p.b_scale;
+    return f;
+}
+
 // One epilogue row: COLS consecutive columns from col0 of output row `row`
-// (within batch bz): alpha, bias (first split only), optional GELU, then C
+// (within batch bz), accumulator already scaled by epi_factor: bias (first
+// split only), optional GELU, then C
 // (plain store, or float4 atomics under split-K) or, for PLANES kernels, the
 // split A planes (a separate instantiation: the plane code's registers would
 // otherwise cost every GEMM's epilogue).
@@ -158,7 +178,7 @@ __device__ __forceinline__ void store_row(const TcParams& p, int64_t row, int bz
             float h[4], l[4];
 #pragma unroll
             for (int e = 0; e < 4; e++) {
-                float v = p.alpha * acc[j + e];
+                float v = acc[j + e];
                 if (add_bias) v += p.bias[col + e];
                 if (p.act == 1) v = gelu_tanh(v);
                 h[e] = tf32_hi(v);
@@ -187,8 +207,7 @@ __device__ __forceinline__ void store_row(const TcParams& p, int64_t row, int bz
     if (p.vec_c && col0 + COLS <= p.N) {
 #pragma unroll
         for (int j = 0; j < COLS; j += 4) {
-            float4 v = make_float4(p.alpha * acc[j], p.alpha * acc[j + 1], p.alpha * acc[j + 2],
-                                   p.alpha * acc[j + 3]);
+            float4 v = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
             if (add_bias) {
                 float4 bb = *reinterpret_cast<const float4*>(p.bias + col0 + j);
                 v.x += bb.x; v.y += bb.y; v.z += bb.z; v.w += bb.w;
@@ -209,7 +228,7 @@ __device__ __forceinline__ void store_row(const TcParams& p, int64_t row, int bz
 #pragma unroll
         for (int j = 0; j < COLS; j++) {
             if (col0 + j < p.N) {
-                float v = p.alpha * acc[j];
+                float v = acc[j];
                 if (add_bias) v += p.bias[col0 + j];
                 if (add_res) v += p.res[r * p.N + col0 + j];   // alpha == 1 with a residual
                 if (p.act == 1) v = gelu_tanh(v);
@@ -231,10 +250,12 @@ __device__ __forceinline__ void tile_coords(const TcParams& p, int item, int& m_
     kb_hi = min(p.k_blocks, kb_lo + p.kb_split);
 }
 
-template <int BN_, bool CROSS, bool PLANES>
+template <int BN_, int SCH, bool PLANES>
 __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_constant__ TcParams p) {
-    constexpr int BN = GCfg<BN_>::BN, STAGES = GCfg<BN_>::STAGES, EPI_COLS = GCfg<BN_>::EPI_COLS;
-    constexpr int B_TILE = GCfg<BN_>::B_TILE, STAGE_BYTES = GCfg<BN_>::STAGE_BYTES;
+    using G = GCfg<BN_, SCH>;
+    constexpr int BN = G::BN, STAGES = G::STAGES, EPI_COLS = G::EPI_COLS;
+    constexpr int B_TILE = G::B_TILE, STAGE_BYTES = G::STAGE_BYTES;
+    constexpr bool CROSS = SCH == SCH_CROSS, F16 = SCH == SCH_F16;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem =
         reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -292,10 +313,15 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
                     ptx::mbar_expect_tx(&full[stage], STAGE_BYTES);
                     issued_phase[stage] = (int)phase;
                     int k0 = kb * BK;
-                    ptx::tma_load_3d(st, &p.ta_hi, &full[stage], k0, m_blk * BM, bz);
-                    ptx::tma_load_3d(st + A_TILE, &p.ta_lo, &full[stage], k0, m_blk * BM, bz);
-                    ptx::tma_load_3d(st + 2 * A_TILE, &p.tb_hi, &full[stage], k0, n_blk * BN, bz);
-                    ptx::tma_load_3d(st + 2 * A_TILE + B_TILE, &p.tb_lo, &full[stage], k0, n_blk * BN, bz);
+                    if (F16) {   // one fp16 plane per operand: 2 halves per element of K
+                        ptx::tma_load_3d(st, &p.ta_hi, &full[stage], 2 * k0, m_blk * BM, bz);
+                        ptx::tma_load_3d(st + A_TILE, &p.tb_hi, &full[stage], 2 * k0, n_blk * BN, bz);
+                    } else {
+                        ptx::tma_load_3d(st, &p.ta_hi, &full[stage], k0, m_blk * BM, bz);
+                        ptx::tma_load_3d(st + A_TILE, &p.ta_lo, &full[stage], k0, m_blk * BM, bz);
+                        ptx::tma_load_3d(st + 2 * A_TILE, &p.tb_hi, &full[stage], k0, n_blk * BN, bz);
+                        ptx::tma_load_3d(st + 2 * A_TILE + B_TILE, &p.tb_lo, &full[stage], k0, n_blk * BN, bz);
+                    }
                     if (++stage == STAGES) {
                         stage = 0;
                         phase ^= 1;
@@ -308,6 +334,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
         if (lane == 0) {
             constexpr uint32_t idesc = ptx::idesc_tf32(BM, BN);
             constexpr uint32_t idesc_x = ptx::idesc_bf16(BM, BN);
+            constexpr uint32_t idesc_h = ptx::idesc_f16(BM, BN);
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
@@ -336,7 +363,16 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
                         ptx::tc_fence_after();
                         uint8_t* st = smem + stage * STAGE_BYTES;
                         const uint32_t acc0 = kb > kb0 ? 1u : 0u;
-                        if (CROSS) {
+                        if (F16) {
+                            // one 16-wide K block per stage: A row [h | l], B row [l | h]
+                            // (32 bytes each): h.h, h.l, l.h
+                            ptx::mma_bf16(d_tmem, ptx::smem_desc(st, 512, 4), ptx::smem_desc(st + A_TILE + 32, 512, 4),
+                                          idesc_h, acc0);
+                            ptx::mma_bf16(d_tmem, ptx::smem_desc(st, 512, 4), ptx::smem_desc(st + A_TILE, 512, 4),
+                                          idesc_h, 1u);
+                            ptx::mma_bf16(d_tmem, ptx::smem_desc(st + 32, 512, 4),
+                                          ptx::smem_desc(st + A_TILE + 32, 512, 4), idesc_h, 1u);
+                        } else if (CROSS) {
                             // hi.hi: two tf32 K=8 steps (+32 bytes each inside the 64-byte atom)
 #pragma unroll
                             for (int kk = 0; kk < 2; kk++)
@@ -389,6 +425,7 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
             tile_coords(p, t, m_blk, n_blk, bz, kb_lo, kb_hi);
             const int n_chunks = (kb_hi - kb_lo + p.kb_per_chunk - 1) / p.kb_per_chunk;
             const bool first_split = kb_lo == 0;
+            const float fac = epi_factor(p, (int64_t)m_blk * BM + quarter * 32 + lane, bz);
             float acc[EPI_COLS];
             for (int c = 0; c < n_chunks; c++, it++) {
                 int b = it & 1;
@@ -410,8 +447,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
                     ptx::tmem_ld_wait();
 #pragma unroll
                     for (int j = 0; j < 16; j++)
-                        acc[q * 16 + j] =
-                            c == 0 ? __uint_as_float(r[j]) : acc[q * 16 + j] + __uint_as_float(r[j]);
+                        acc[q * 16 + j] = c == 0 ? fac * __uint_as_float(r[j])
+                                                 : fmaf(fac, __uint_as_float(r[j]), acc[q * 16 + j]);
                 }
                 ptx::tc_fence_before();
                 ptx::mbar_arrive(&acc_empty[b]);
@@ -452,6 +489,16 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
 // K block of 32 fp32 = one 128-byte swizzle row: half the TMA requests per
 // byte of the 64-byte rows (the request path to L2 limits the 1-CTA kernel).
 constexpr int P_BK = 32;
+// Stage ring: tf32 schemes 3 stages of four planes (A hi / A plane 1 / B hi /
+// B plane 1, 64 KiB), the fp16 scheme 6 stages of two (A / B, 32 KiB).
+template <int SCH>
+struct PCfg {
+    static constexpr int STAGES = SCH == SCH_F16 ? 6 : 3;
+    static constexpr int STAGE_BYTES = (SCH == SCH_F16 ? 2 : 4) * 128 * 32 * 4;
+    static constexpr int EPI_OFF = STAGES * STAGE_BYTES + 1024;   // after the barriers, 1024-aligned
+    static constexpr int SMEM = EPI_OFF + 8 * 32 * 32 * 4 + 1024;
+    static_assert(SMEM <= 232448, "shared memory budget");
+};
 constexpr int P_STAGES = 3;
 constexpr int P_TILE = 128 * P_BK * 4;                 // 16 KiB: one plane of 128 rows
 constexpr int P_STAGE_BYTES = 4 * P_TILE;              // A hi / A plane1 / B hi / B plane1
@@ -461,9 +508,11 @@ constexpr int P_SMEM_BYTES = P_EPI_OFF + 8 * P_EPI_STAGE + 1024;
 static_assert(P_SMEM_BYTES <= 232448, "shared memory budget");
 constexpr int P_EPI_COLS = 128;
 
-template <bool CROSS, bool PLANES, bool RES = false, bool TMA = false>
+template <int SCH, bool PLANES, bool RES = false, bool TMA = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     tc_gemm_pair_kernel(const __grid_constant__ TcParams p) {
+    constexpr int P_STAGES = PCfg<SCH>::STAGES, P_STAGE_BYTES = PCfg<SCH>::STAGE_BYTES, P_EPI_OFF = PCfg<SCH>::EPI_OFF;
+    constexpr bool CROSS = SCH == SCH_CROSS, F16 = SCH == SCH_F16;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem =
         reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -529,10 +578,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                         issued_phase[stage] = (int)phase;
                     }
                     const int k0 = kb * P_BK;
-                    ptx::tma_load_3d_pair(st, &p.ta_hi, bar, k0, arow, bz);
-                    ptx::tma_load_3d_pair(st + P_TILE, &p.ta_lo, bar, k0, arow, bz);
-                    ptx::tma_load_3d_pair(st + 2 * P_TILE, &p.tb_hi, bar, k0, brow, bz);
-                    ptx::tma_load_3d_pair(st + 3 * P_TILE, &p.tb_lo, bar, k0, brow, bz);
+                    if (F16) {   // one fp16 plane per operand: 2 halves per element of K
+                        ptx::tma_load_3d_pair(st, &p.ta_hi, bar, 2 * k0, arow, bz);
+                        ptx::tma_load_3d_pair(st + P_TILE, &p.tb_hi, bar, 2 * k0, brow, bz);
+                    } else {
+                        ptx::tma_load_3d_pair(st, &p.ta_hi, bar, k0, arow, bz);
+                        ptx::tma_load_3d_pair(st + P_TILE, &p.ta_lo, bar, k0, arow, bz);
+                        ptx::tma_load_3d_pair(st + 2 * P_TILE, &p.tb_hi, bar, k0, brow, bz);
+                        ptx::tma_load_3d_pair(st + 3 * P_TILE, &p.tb_lo, bar, k0, brow, bz);
+                    }
                     if (++stage == P_STAGES) {
                         stage = 0;
                         phase ^= 1;
@@ -545,6 +599,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         if (leader && lane == 0) {
             constexpr uint32_t idesc = ptx::idesc_tf32(256, 256);
             constexpr uint32_t idesc_x = ptx::idesc_bf16(256, 256);
+            constexpr uint32_t idesc_h = ptx::idesc_f16(256, 256);
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
@@ -574,7 +629,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                         uint8_t* st = smem + stage * P_STAGE_BYTES;
                         const uint32_t acc0 = kb > kb0 ? 1u : 0u;
                         // K advance inside the 128-byte swizzle atom: +32 bytes per step
-                        if (CROSS) {
+                        if (F16) {
+                            // two 16-wide K blocks per 128-byte row: A [h | l], B [l | h]
+                            // (32 bytes each); per block h.h, h.l, l.h
+#pragma unroll
+                            for (int j = 0; j < 2; j++) {
+                                const uint8_t* a = st + j * 64;
+                                const uint8_t* bb = st + P_TILE + j * 64;
+                                ptx::mma_bf16_pair(d_tmem, ptx::smem_desc(a, 1024, 2), ptx::smem_desc(bb + 32, 1024, 2),
+                                                   idesc_h, (acc0 | j) ? 1u : 0u);
+                                ptx::mma_bf16_pair(d_tmem, ptx::smem_desc(a, 1024, 2), ptx::smem_desc(bb, 1024, 2),
+                                                   idesc_h, 1u);
+                                ptx::mma_bf16_pair(d_tmem, ptx::smem_desc(a + 32, 1024, 2),
+                                                   ptx::smem_desc(bb + 32, 1024, 2), idesc_h, 1u);
+                            }
+                        } else if (CROSS) {
 #pragma unroll
                             for (int kk = 0; kk < 4; kk++)
                                 ptx::mma_tf32_pair(d_tmem, ptx::smem_desc(st + kk * 32, 1024, 2),
@@ -624,6 +693,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             tile_coords(p, t, m_blk, n_blk, bz, kb_lo, kb_hi);
             const int n_chunks = (kb_hi - kb_lo + p.kb_per_chunk - 1) / p.kb_per_chunk;
             const bool first_split = kb_lo == 0;
+            const float fac = epi_factor(p, (int64_t)m_blk * 256 + rank * 128 + quarter * 32 + lane, bz);
             float acc[P_EPI_COLS];
             // RES: a folded residual preloaded into the accumulator registers
             // (zeros on a second split); the TMEM chunks add to it
@@ -653,8 +723,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                     ptx::tmem_ld_wait();
 #pragma unroll
                     for (int j = 0; j < 16; j++)
-                        acc[q * 16 + j] = c == 0 && !RES ? __uint_as_float(r[j])
-                                                         : acc[q * 16 + j] + __uint_as_float(r[j]);
+                        acc[q * 16 + j] = c == 0 && !RES ? fac * __uint_as_float(r[j])
+                                                         : fmaf(fac, __uint_as_float(r[j]), acc[q * 16 + j]);
                 }
                 ptx::tc_fence_before();
                 __syncwarp();
@@ -676,8 +746,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 #pragma unroll
                     for (int w = 0; w < 32; w += 4) {
                         const int j = c4 * 32 + w, col = col0 + j;
-                        float4 v = make_float4(p.alpha * acc[j], p.alpha * acc[j + 1], p.alpha * acc[j + 2],
-                                               p.alpha * acc[j + 3]);
+                        float4 v = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
                         if (add_bias && col < p.N) {   // N % 4 == 0 with a C tensor map
                             const float4 bb = *reinterpret_cast<const float4*>(p.bias + col);
                             v.x += bb.x; v.y += bb.y; v.z += bb.z; v.w += bb.w;
@@ -816,6 +885,137 @@ Status run_split(const float* x, float* hi, float* p1, int64_t batches, int64_t 
     return Status::ok();
 }
 
+// ---- fp16 split (SCH_F16): one plane per operand ---------------------------
+// Row r of an operand becomes 2*K16 halves (K16 = K rounded up to 16): per
+// 16-wide K block [h(16) | l(16)] for A, [l(16) | h(16)] for B, of x scaled by
+// 2^e (dev_math.h); k >= K is zero.  A: e per row (its 2^-e in scale[row]),
+// from the row's own maximum; B: one e for the whole operand, from the
+// maximum an absmax pass left in tensor_max (its 2^-e in scale[1]).
+
+__device__ __forceinline__ float warp_max_f(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// |x| maximum over n elements into *out (zeroed first) as float bits
+// (non-negative floats order like their bit patterns).
+__global__ void absmax_kernel(const float* __restrict__ x, int64_t n, unsigned* out) {
+    float m = 0.0f;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        m = fmaxf(m, fabsf(x[i]));
+    m = warp_max_f(m);
+    if ((threadIdx.x & 31) == 0) atomicMax(out, __float_as_uint(m));
+}
+
+// One warp per row: the row's maximum (unless tensor_max), then the plane.
+__global__ void split16_rows_kernel(const float* __restrict__ x, uint16_t* __restrict__ plane,
+                                    float* __restrict__ scale, int64_t rows, int K, int K16,
+                                    const float* __restrict__ tensor_max, bool first_hi, bool vec) {
+    const int lane = threadIdx.x & 31, wpb = blockDim.x >> 5;
+    if (tensor_max && blockIdx.x == 0 && threadIdx.x == 0) scale[1] = pow2i(-f16_scale_exp(*tensor_max));
+    for (int64_t row = (int64_t)blockIdx.x * wpb + (threadIdx.x >> 5); row < rows; row += (int64_t)gridDim.x * wpb) {
+        const float* xr = x + row * K;
+        float m;
+        if (tensor_max) {
+            m = *tensor_max;
+        } else {
+            m = 0.0f;
+            if (vec) {
+#pragma unroll 4
+                for (int c = lane; c < K / 4; c += 32) {
+                    const float4 v = reinterpret_cast<const float4*>(xr)[c];
+                    m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+                }
+            } else {
+                for (int k = lane; k < K; k += 32) m = fmaxf(m, fabsf(xr[k]));
+            }
+            m = warp_max_f(m);
+        }
+        const int e = f16_scale_exp(m);
+        const float sc = pow2i(e);
+        if (!tensor_max && lane == 0) scale[row] = pow2i(-e);
+        uint16_t* pr = plane + row * (2 * (int64_t)K16);
+#pragma unroll 4
+        for (int c = lane; c < K16 / 4; c += 32) {
+            const int k = 4 * c;
+            float4 v;
+            if (vec) {
+                v = k < K ? reinterpret_cast<const float4*>(xr)[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+            } else {
+                v.x = k < K ? xr[k] : 0.f;
+                v.y = k + 1 < K ? xr[k + 1] : 0.f;
+                v.z = k + 2 < K ? xr[k + 2] : 0.f;
+                v.w = k + 3 < K ? xr[k + 3] : 0.f;
+            }
+            store_f16x4(pr, k, make_float4(v.x * sc, v.y * sc, v.z * sc, v.w * sc), first_hi);
+        }
+    }
+}
+
+// [batches][K][N] -> plane rows of the transpose ([batches][N][2*K16]), one
+// scale for the whole operand (tensor_max).
+__global__ void split16_transpose_kernel(const float* __restrict__ x, uint16_t* __restrict__ plane, int K, int N,
+                                         int K16, const float* __restrict__ tensor_max, bool first_hi) {
+    __shared__ float tile[32][33];
+    const int64_t bz = blockIdx.z;
+    const float* xb = x + bz * (int64_t)K * N;
+    const float sc = pow2i(f16_scale_exp(*tensor_max));
+    const int k0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
+    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+        const int k = k0 + r, n = n0 + threadIdx.x;
+        tile[r][threadIdx.x] = (k < K && n < N) ? xb[(int64_t)k * N + n] : 0.0f;
+    }
+    __syncthreads();
+    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+        const int n = n0 + r, k = k0 + threadIdx.x;
+        if (n < N && k < K16) {
+            uint16_t lo;
+            const uint16_t hi = (uint16_t)f16_hl(tile[threadIdx.x][r] * sc, &lo);
+            uint16_t* blk = plane + (bz * N + n) * (2 * (int64_t)K16) + (k >> 4) * 32 + (k & 15);
+            blk[first_hi ? 0 : 16] = hi;
+            blk[first_hi ? 16 : 0] = lo;
+        }
+    }
+}
+
+int64_t k16_of(int64_t K) { return (K + 15) / 16 * 16; }
+
+// A operand: per-row scales into scale[batches*rows].
+Status run_split16_rows(const float* x, uint16_t* plane, float* scale, int64_t rows, int64_t K, cudaStream_t st) {
+    const bool vec = aligned16(x) && K % 4 == 0;
+    const int64_t blocks = (rows + 7) / 8;
+    const int grid = (int)std::min<int64_t>(blocks, (int64_t)g_num_sms * 8);
+    if (grid == 0) return Status::ok();
+    split16_rows_kernel<<<grid, 256, 0, st>>>(x, plane, scale, rows, (int)K, (int)k16_of(K), nullptr, true, vec);
+    RT_LAUNCH_CHECK();
+    return Status::ok();
+}
+
+// B operand ([batches][rows][K], or [batches][K][rows] when trans): one scale;
+// scalars[0] = the absmax (float bits), scalars[1] = 2^-e.
+Status run_split16_tensor(const float* x, uint16_t* plane, float* scalars, int64_t batches, int64_t rows, int64_t K,
+                          bool trans, cudaStream_t st) {
+    const int64_t n = batches * rows * K;
+    RT_CUDA_CHECK(cudaMemsetAsync(scalars, 0, 2 * sizeof(float), st));
+    absmax_kernel<<<grid_for(n, 256, 8), 256, 0, st>>>(x, n, reinterpret_cast<unsigned*>(scalars));
+    RT_LAUNCH_CHECK();
+    const int K16 = (int)k16_of(K);
+    if (!trans) {
+        const bool vec = aligned16(x) && K % 4 == 0;
+        const int64_t all = batches * rows;
+        const int grid = (int)std::min<int64_t>((all + 7) / 8, (int64_t)g_num_sms * 8);
+        split16_rows_kernel<<<grid, 256, 0, st>>>(x, plane, scalars, all, (int)K, K16, scalars, false, vec);
+    } else {
+        dim3 grid((unsigned)((rows + 31) / 32), (unsigned)((K16 + 31) / 32), (unsigned)batches);
+        split16_transpose_kernel<<<grid, dim3(32, 8), 0, st>>>(x, plane, (int)K, (int)rows, K16, scalars, false);
+        if (cudaPeekAtLastError() == cudaSuccess)   // scale[1] for the epilogue
+            split16_rows_kernel<<<1, 32, 0, st>>>(x, plane, scalars, 0, (int)K, K16, scalars, false, false);
+    }
+    RT_LAUNCH_CHECK();
+    return Status::ok();
+}
+
 // ---- tensor maps (driver entry point fetched through the runtime) --------
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -847,14 +1047,46 @@ Status make_tmap(CUtensorMap* m, const float* base, int64_t K, int64_t rows, int
     return Status::ok();
 }
 
+// fp16 plane tensor map: {2*K16 halves, rows, batches}, box {box_h, box_rows}.
+Status make_tmap16(CUtensorMap* m, const void* base, int64_t K16, int64_t rows, int64_t batches, int box_rows,
+                   int box_h) {
+    auto fn = encode_fn();
+    if (!fn) return Status::err(RT_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[3] = {(cuuint64_t)(2 * K16), (cuuint64_t)rows, (cuuint64_t)batches};
+    cuuint64_t strides[2] = {(cuuint64_t)K16 * 4, (cuuint64_t)(rows * K16 * 4)};
+    cuuint32_t box[3] = {(cuuint32_t)box_h, (cuuint32_t)box_rows, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    box_h * 2 == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return Status::err(RT_ERR_CUDA, "cuTensorMapEncodeTiled (f16) failed: " + std::to_string((int)r));
+    return Status::ok();
+}
+
+// Operand scheme: fp16 (default), RT_GEMM_SCHEME=cross for tf32 + bf16 cross
+// terms, RT_GEMM_SCHEME=3xtf32 (or RT_GEMM_3XTF32=1) for three tf32 MMAs.
+int scheme() {
+    static const int v = [] {
+        const char* e = getenv("RT_GEMM_SCHEME");
+        const char* t = getenv("RT_GEMM_3XTF32");
+        if (t && t[0] == '1') return SCH_3XTF32;
+        if (e && !strcmp(e, "3xtf32")) return SCH_3XTF32;
+        if (e && !strcmp(e, "cross")) return SCH_CROSS;
+        return SCH_F16;
+    }();
+    return v;
+}
+bool cross_scheme() { return scheme() == SCH_CROSS; }
+
 // K accumulated per TMEM chunk (see the file comment): 256 for the cross-
-// term scheme, 128 for 3xTF32 (three accumulating MMAs per K step instead of
-// two: its error at 256 exceeds the cross scheme's at 256).  RT_GEMM_KCHUNK
-// (a multiple of 32) overrides both.
-bool cross_scheme();
+// term and fp16 schemes, 128 for 3xTF32 (three accumulating MMAs per K step
+// instead of two: its error at 256 exceeds the cross scheme's at 256).
+// RT_GEMM_KCHUNK (a multiple of 32) overrides all.
 int k_chunk() {
     static int v = [] {
-        const int dflt = cross_scheme() ? 256 : 128;
+        const int dflt = scheme() == SCH_3XTF32 ? 128 : 256;
         const char* e = getenv("RT_GEMM_KCHUNK");
         int k = e ? atoi(e) : dflt;
         if (k < 32 || k % 32) k = dflt;
@@ -872,62 +1104,66 @@ bool split_k_enabled() {
     return on;
 }
 
-// Cross-term scheme (default) or RT_GEMM_3XTF32=1 for three tf32 MMAs.
-bool cross_scheme() {
-    static const bool on = [] {
-        const char* e = getenv("RT_GEMM_3XTF32");
-        return !(e && e[0] == '1');
-    }();
-    return on;
-}
 int a_mode() { return cross_scheme() ? 1 : 0; }
 int b_mode() { return cross_scheme() ? 2 : 0; }
 SplitKey b_key(const GemmProblem& p) {
-    return SplitKey{p.b, p.batches, p.N, p.K, (p.trans_b ? 0 : 1) | (cross_scheme() ? 2 : 0)};
+    return SplitKey{p.b, p.batches, p.N, p.K, (p.trans_b ? 0 : 1) | (scheme() << 1)};
 }
 
 // Every kernel instantiation with its dynamic shared memory size.
 template <class F>
 cudaError_t for_each_kernel(F f) {
+    constexpr int P0 = PCfg<SCH_3XTF32>::SMEM, P1 = PCfg<SCH_CROSS>::SMEM, P2 = PCfg<SCH_F16>::SMEM;
     const void* ks[] = {
-        (const void*)tc_gemm_pair_kernel<true, false>, (const void*)tc_gemm_pair_kernel<false, false>,
-        (const void*)tc_gemm_pair_kernel<true, true>,  (const void*)tc_gemm_pair_kernel<false, true>,
-        (const void*)tc_gemm_kernel<256, true, false>, (const void*)tc_gemm_kernel<256, false, false>,
-        (const void*)tc_gemm_kernel<256, true, true>,  (const void*)tc_gemm_kernel<256, false, true>,
-        (const void*)tc_gemm_kernel<128, true, false>, (const void*)tc_gemm_kernel<128, false, false>,
-        (const void*)tc_gemm_kernel<128, true, true>,  (const void*)tc_gemm_kernel<128, false, true>,
-        (const void*)tc_gemm_pair_kernel<true, false, true>, (const void*)tc_gemm_pair_kernel<false, false, true>,
-        (const void*)tc_gemm_pair_kernel<true, false, false, true>,
-        (const void*)tc_gemm_pair_kernel<false, false, false, true>};
-    const int smem[] = {P_SMEM_BYTES, P_SMEM_BYTES, P_SMEM_BYTES, P_SMEM_BYTES,
-                        GCfg<256>::SMEM_BYTES, GCfg<256>::SMEM_BYTES, GCfg<256>::SMEM_BYTES, GCfg<256>::SMEM_BYTES,
-                        GCfg<128>::SMEM_BYTES, GCfg<128>::SMEM_BYTES, GCfg<128>::SMEM_BYTES, GCfg<128>::SMEM_BYTES,
-                        P_SMEM_BYTES, P_SMEM_BYTES, P_SMEM_BYTES, P_SMEM_BYTES};
-    for (int i = 0; i < 16; i++) {
+        (const void*)tc_gemm_pair_kernel<SCH_3XTF32, false>, (const void*)tc_gemm_pair_kernel<SCH_CROSS, false>,
+        (const void*)tc_gemm_pair_kernel<SCH_F16, false>,
+        (const void*)tc_gemm_pair_kernel<SCH_3XTF32, true>, (const void*)tc_gemm_pair_kernel<SCH_CROSS, true>,
+        (const void*)tc_gemm_pair_kernel<SCH_3XTF32, false, true>, (const void*)tc_gemm_pair_kernel<SCH_CROSS, false, true>,
+        (const void*)tc_gemm_pair_kernel<SCH_F16, false, true>,
+        (const void*)tc_gemm_pair_kernel<SCH_3XTF32, false, false, true>,
+        (const void*)tc_gemm_pair_kernel<SCH_CROSS, false, false, true>,
+        (const void*)tc_gemm_pair_kernel<SCH_F16, false, false, true>,
+        (const void*)tc_gemm_kernel<256, SCH_3XTF32, false>, (const void*)tc_gemm_kernel<256, SCH_CROSS, false>,
+        (const void*)tc_gemm_kernel<256, SCH_F16, false>,
+        (const void*)tc_gemm_kernel<256, SCH_3XTF32, true>, (const void*)tc_gemm_kernel<256, SCH_CROSS, true>,
+        (const void*)tc_gemm_kernel<128, SCH_3XTF32, false>, (const void*)tc_gemm_kernel<128, SCH_CROSS, false>,
+        (const void*)tc_gemm_kernel<128, SCH_F16, false>,
+        (const void*)tc_gemm_kernel<128, SCH_3XTF32, true>, (const void*)tc_gemm_kernel<128, SCH_CROSS, true>};
+    const int smem[] = {P0, P1, P2, P0, P1, P0, P1, P2, P0, P1, P2,
+                        GCfg<256, SCH_3XTF32>::SMEM_BYTES, GCfg<256, SCH_CROSS>::SMEM_BYTES,
+                        GCfg<256, SCH_F16>::SMEM_BYTES, GCfg<256, SCH_3XTF32>::SMEM_BYTES,
+                        GCfg<256, SCH_CROSS>::SMEM_BYTES,
+                        GCfg<128, SCH_3XTF32>::SMEM_BYTES, GCfg<128, SCH_CROSS>::SMEM_BYTES,
+                        GCfg<128, SCH_F16>::SMEM_BYTES, GCfg<128, SCH_3XTF32>::SMEM_BYTES,
+                        GCfg<128, SCH_CROSS>::SMEM_BYTES};
+    static_assert(sizeof(ks) / sizeof(ks[0]) == sizeof(smem) / sizeof(smem[0]), "kernel table");
+    for (size_t i = 0; i < sizeof(ks) / sizeof(ks[0]); i++) {
         cudaError_t e = f(ks[i], smem[i]);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
 }
 
-template <bool CROSS, bool PLANES>
+template <int SCH, bool PLANES>
 void launch_tc_t(bool pair, int BN, int grid, const TcParams& prm, cudaStream_t st) {
+    constexpr int PS = PCfg<SCH>::SMEM;
     if (pair && !PLANES && prm.res)
-        tc_gemm_pair_kernel<CROSS, false, true><<<2 * grid, THREADS, P_SMEM_BYTES, st>>>(prm);
+        tc_gemm_pair_kernel<SCH, false, true><<<2 * grid, THREADS, PS, st>>>(prm);
     else if (pair && !PLANES && prm.c_tma)
-        tc_gemm_pair_kernel<CROSS, false, false, true><<<2 * grid, THREADS, P_SMEM_BYTES, st>>>(prm);
+        tc_gemm_pair_kernel<SCH, false, false, true><<<2 * grid, THREADS, PS, st>>>(prm);
     else if (pair)
-        tc_gemm_pair_kernel<CROSS, PLANES><<<2 * grid, THREADS, P_SMEM_BYTES, st>>>(prm);
+        tc_gemm_pair_kernel<SCH, PLANES><<<2 * grid, THREADS, PS, st>>>(prm);
     else if (BN == 128)
-        tc_gemm_kernel<128, CROSS, PLANES><<<grid, THREADS, GCfg<128>::SMEM_BYTES, st>>>(prm);
+        tc_gemm_kernel<128, SCH, PLANES><<<grid, THREADS, GCfg<128, SCH>::SMEM_BYTES, st>>>(prm);
     else
-        tc_gemm_kernel<256, CROSS, PLANES><<<grid, THREADS, GCfg<256>::SMEM_BYTES, st>>>(prm);
+        tc_gemm_kernel<256, SCH, PLANES><<<grid, THREADS, GCfg<256, SCH>::SMEM_BYTES, st>>>(prm);
 }
-void launch_tc(bool pair, int BN, bool cross, bool planes, int grid, const TcParams& prm, cudaStream_t st) {
-    if (cross && planes) launch_tc_t<true, true>(pair, BN, grid, prm, st);
-    else if (cross) launch_tc_t<true, false>(pair, BN, grid, prm, st);
-    else if (planes) launch_tc_t<false, true>(pair, BN, grid, prm, st);
-    else launch_tc_t<false, false>(pair, BN, grid, prm, st);
+void launch_tc(bool pair, int BN, int sch, bool planes, int grid, const TcParams& prm, cudaStream_t st) {
+    if (sch == SCH_F16) launch_tc_t<SCH_F16, false>(pair, BN, grid, prm, st);   // (no split-plane output)
+    else if (sch == SCH_CROSS && planes) launch_tc_t<SCH_CROSS, true>(pair, BN, grid, prm, st);
+    else if (sch == SCH_CROSS) launch_tc_t<SCH_CROSS, false>(pair, BN, grid, prm, st);
+    else if (planes) launch_tc_t<SCH_3XTF32, true>(pair, BN, grid, prm, st);
+    else launch_tc_t<SCH_3XTF32, false>(pair, BN, grid, prm, st);
 }
 
 // RT_GEMM_PAIR=0 keeps every GEMM on the one-CTA kernel.
@@ -946,7 +1182,7 @@ int pair_clusters() {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(2 * (g_num_sms / 2));
         cfg.blockDim = dim3(THREADS);
-        cfg.dynamicSmemBytes = P_SMEM_BYTES;
+        cfg.dynamicSmemBytes = PCfg<SCH_CROSS>::SMEM;
         cudaLaunchAttribute attr;
         attr.id = cudaLaunchAttributeClusterDimension;
         attr.val.clusterDim.x = 2;
@@ -955,7 +1191,8 @@ int pair_clusters() {
         cfg.attrs = &attr;
         cfg.numAttrs = 1;
         int c = 0;
-        if (cudaOccupancyMaxActiveClusters(&c, tc_gemm_pair_kernel<true, false>, &cfg) != cudaSuccess || c <= 0) {
+        if (cudaOccupancyMaxActiveClusters(&c, tc_gemm_pair_kernel<SCH_CROSS, false>, &cfg) != cudaSuccess ||
+            c <= 0) {
             cudaGetLastError();
             c = g_num_sms / 2;
         }
@@ -968,25 +1205,39 @@ bool b_is_constant(const GemmProblem& p) {
     return is_constant_range(p.b, (size_t)p.batches * p.N * p.K * 4);
 }
 
-size_t a_split_bytes(const GemmProblem& p) { return (size_t)p.batches * p.M * p.K * 4; }
-size_t b_split_bytes(const GemmProblem& p) { return (size_t)p.batches * p.N * p.K * 4; }
 size_t round256(size_t b) { return (b + 255) & ~(size_t)255; }
+// Bytes of one split plane: the tf32 schemes' fp32 planes hold K floats per
+// row, the fp16 plane 2*K16 halves (the same bytes when K % 16 == 0).
+size_t plane_bytes(int64_t batches, int64_t rows, int64_t K) {
+    return (size_t)batches * rows * (scheme() == SCH_F16 ? k16_of(K) : K) * 4;
+}
+// fp16 scheme: the per-row A scales / the B scalars
+size_t a_scale_bytes(const GemmProblem& p) { return round256((size_t)p.batches * p.M * 4); }
+constexpr size_t B_SCALARS = 256;
 
 }  // namespace
 
 bool gemm_cross_scheme() { return cross_scheme(); }
+int gemm_scheme() { return scheme(); }
+bool gemm_planes_from_epilogues() { return scheme() != SCH_F16; }
 
 bool tc_gemm_applicable(const GemmProblem& p) {
-    if (p.K % 4 != 0) return false;                                  // TMA row stride: 16-byte multiple
+    // tf32 planes keep K fp32 per row (TMA row stride a 16-byte multiple);
+    // the fp16 plane pads rows to 16-wide blocks
+    if (scheme() != SCH_F16 && p.K % 4 != 0) return false;
     if ((double)p.M * p.N * p.K < 8.0 * 1024 * 1024) return false;   // tiny: the CUDA-core GEMM wins
-    if (p.M > INT32_MAX / 2 || p.N > INT32_MAX / 2 || p.K > INT32_MAX / 2 || p.batches > 65535) return false;
+    if (p.M > INT32_MAX / 2 || p.N > INT32_MAX / 2 || p.K > INT32_MAX / 4 || p.batches > 65535) return false;
     return true;
 }
 
 size_t tc_gemm_workspace_bytes(const GemmProblem& p) {
     if (!tc_gemm_applicable(p)) return 0;
-    size_t b = 2 * round256(a_split_bytes(p));
-    if (!b_is_constant(p)) b += 2 * round256(b_split_bytes(p));
+    const bool f16 = scheme() == SCH_F16;
+    size_t b = f16 ? round256(plane_bytes(p.batches, p.M, p.K)) + a_scale_bytes(p)
+                   : 2 * round256(plane_bytes(p.batches, p.M, p.K));
+    if (!b_is_constant(p))
+        b += f16 ? round256(plane_bytes(p.batches, p.N, p.K)) + B_SCALARS
+                 : 2 * round256(plane_bytes(p.batches, p.N, p.K));
     return b;
 }
 
@@ -1004,7 +1255,13 @@ Status tc_gemm_prepare(const GemmProblem& p, cudaStream_t st) {
     SplitKey key = b_key(p);
     if (find_constant_split(key)) return Status::ok();
     SplitOperand s;
-    Status r = create_constant_split(key, (size_t)p.batches * p.N * p.K, &s);
+    if (scheme() == SCH_F16) {
+        Status r = create_constant_split(key, plane_bytes(p.batches, p.N, p.K) / 4, B_SCALARS / 4, &s);
+        if (!r.good()) return r;
+        return run_split16_tensor(p.b, reinterpret_cast<uint16_t*>(s.hi), s.lo, p.batches, p.N, p.K, !p.trans_b, st);
+    }
+    const size_t elems = (size_t)p.batches * p.N * p.K;
+    Status r = create_constant_split(key, elems, elems, &s);
     if (!r.good()) return r;
     return run_split(p.b, s.hi, s.lo, p.batches, p.N, p.K, !p.trans_b, b_mode(), st);
 }
@@ -1014,37 +1271,51 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
     if (p.M == 0) return Status::ok();
     if (ws.bytes < tc_gemm_workspace_bytes(p)) return Status::err(RT_ERR_ARGUMENT, "gemm: workspace too small");
     if (f && f->plane_hi && p.N % 4 != 0) return Status::err(RT_ERR_ARGUMENT, "gemm: split-plane output needs N % 4 == 0");
-    const size_t abytes = round256(a_split_bytes(p));
-    const float *a_hi, *a_lo;
-    const float *b_hi, *b_lo;
+    const int sch = scheme();
+    const bool f16 = sch == SCH_F16;
+    if (f16 && f && f->plane_hi)
+        return Status::err(RT_ERR_ARGUMENT, "gemm: the fp16 scheme takes no split-plane output");
+    const size_t abytes = round256(plane_bytes(p.batches, p.M, p.K));
+    const size_t a2bytes = f16 ? a_scale_bytes(p) : abytes;   // second A region: scales or plane 1
+    const void *a_hi, *a_lo;
+    const void *b_hi, *b_lo;
+    const float* a_scale = nullptr;
+    const float* b_scale = nullptr;
     Status s;
-    if (f && f->pre_hi) {   // A split by the producing GEMM's epilogue
+    if (f && f->pre_hi) {   // A split by its producer (a norm: planes, or plane + row scales)
         a_hi = f->pre_hi;
-        a_lo = static_cast<const float*>(f->pre_x);
+        a_lo = f->pre_x;
     } else {
-        float* ah = reinterpret_cast<float*>(ws.base);
-        float* al = reinterpret_cast<float*>(ws.base + abytes);
-        s = run_split(p.a, ah, al, p.batches, p.M, p.K, false, a_mode(), st);
+        char* ah = ws.base;
+        char* al = ws.base + abytes;
+        s = f16 ? run_split16_rows(p.a, reinterpret_cast<uint16_t*>(ah), reinterpret_cast<float*>(al),
+                                   p.batches * p.M, p.K, st)
+                : run_split(p.a, reinterpret_cast<float*>(ah), reinterpret_cast<float*>(al), p.batches, p.M, p.K,
+                            false, a_mode(), st);
         if (!s.good()) return s;
         *launches += 1;
         a_hi = ah;
         a_lo = al;
     }
+    if (f16) a_scale = static_cast<const float*>(a_lo);
     if (b_is_constant(p)) {
         const SplitOperand* so = find_constant_split(b_key(p));
         if (!so) return Status::err(RT_ERR_ARGUMENT, "gemm: constant operand not prepared");
         b_hi = so->hi;
         b_lo = so->lo;
     } else {
-        const size_t bbytes = round256(b_split_bytes(p));
-        float* bh = reinterpret_cast<float*>(ws.base + 2 * abytes);
-        float* bl = reinterpret_cast<float*>(ws.base + 2 * abytes + bbytes);
-        s = run_split(p.b, bh, bl, p.batches, p.N, p.K, !p.trans_b, b_mode(), st);
+        char* bh = ws.base + abytes + a2bytes;
+        char* bl = bh + round256(plane_bytes(p.batches, p.N, p.K));
+        s = f16 ? run_split16_tensor(p.b, reinterpret_cast<uint16_t*>(bh), reinterpret_cast<float*>(bl), p.batches,
+                                     p.N, p.K, !p.trans_b, st)
+                : run_split(p.b, reinterpret_cast<float*>(bh), reinterpret_cast<float*>(bl), p.batches, p.N, p.K,
+                            !p.trans_b, b_mode(), st);
         if (!s.good()) return s;
-        *launches += 1;
+        *launches += f16 ? 2 : 1;
         b_hi = bh;
         b_lo = bl;
     }
+    if (f16) b_scale = static_cast<const float*>(b_lo) + 1;
     TcParams prm;
     memset(&prm, 0, sizeof prm);
     // N tile: 256 -- measured faster than 128 at every BASELINE shape, N=768
@@ -1059,10 +1330,20 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
     const bool pair = BN == 256 && p.M > BM && pair_enabled();
     const int b_box = pair ? 128 : BN;
     const int bk = pair ? P_BK : BK;
-    if (!(s = make_tmap(&prm.ta_hi, a_hi, p.K, p.M, p.batches, BM, bk)).good()) return s;
-    if (!(s = make_tmap(&prm.ta_lo, a_lo, p.K, p.M, p.batches, BM, bk)).good()) return s;
-    if (!(s = make_tmap(&prm.tb_hi, b_hi, p.K, p.N, p.batches, b_box, bk)).good()) return s;
-    if (!(s = make_tmap(&prm.tb_lo, b_lo, p.K, p.N, p.batches, b_box, bk)).good()) return s;
+    if (f16) {
+        const int64_t K16 = k16_of(p.K);
+        if (!(s = make_tmap16(&prm.ta_hi, a_hi, K16, p.M, p.batches, BM, 2 * bk)).good()) return s;
+        if (!(s = make_tmap16(&prm.tb_hi, b_hi, K16, p.N, p.batches, b_box, 2 * bk)).good()) return s;
+    } else {
+        const float *ah = static_cast<const float*>(a_hi), *al = static_cast<const float*>(a_lo);
+        const float *bh = static_cast<const float*>(b_hi), *bl = static_cast<const float*>(b_lo);
+        if (!(s = make_tmap(&prm.ta_hi, ah, p.K, p.M, p.batches, BM, bk)).good()) return s;
+        if (!(s = make_tmap(&prm.ta_lo, al, p.K, p.M, p.batches, BM, bk)).good()) return s;
+        if (!(s = make_tmap(&prm.tb_hi, bh, p.K, p.N, p.batches, b_box, bk)).good()) return s;
+        if (!(s = make_tmap(&prm.tb_lo, bl, p.K, p.N, p.batches, b_box, bk)).good()) return s;
+    }
+    prm.a_scale = a_scale;
+    prm.b_scale = b_scale;
     prm.c = f && f->out ? f->out : p.c;
     prm.bias = f && f->bias ? f->bias : p.bias;
     prm.res = f ? f->res : nullptr;
@@ -1131,7 +1412,7 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
     }
     prm.err = kernel_error_flag();
     const int grid = prm.total_items < workers ? prm.total_items : workers;
-    launch_tc(pair, BN, cross_scheme(), prm.plane_hi != nullptr, grid, prm, st);
+    launch_tc(pair, BN, sch, prm.plane_hi != nullptr, grid, prm, st);
     RT_LAUNCH_CHECK();
     *launches += 1;
     return Status::ok();
@@ -1198,8 +1479,8 @@ int noalloc_setup(int device, NoallocDevice** out) {
             cudaGetLastError();
             return RT_ERR_CUDA;
         }
-        if (cudaFuncSetAttribute(tc_gemm_kernel<256, true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 GCfg<256>::SMEM_BYTES) !=
+        if (cudaFuncSetAttribute(tc_gemm_kernel<256, SCH_CROSS, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 GCfg<256, SCH_CROSS>::SMEM_BYTES) !=
             cudaSuccess) {
             cudaGetLastError();
             return RT_ERR_CUDA;
@@ -1270,7 +1551,7 @@ extern "C" int rt_matmul_noalloc(const float* a, const float* b, const float* bi
     prm.err = d->error;
     if (cudaMemsetAsync(d->error, 0, sizeof(int), st) != cudaSuccess) return RT_ERR_CUDA;
     int grid = prm.total_tiles < d->sms ? prm.total_tiles : d->sms;
-    tc_gemm_kernel<256, true, false><<<grid, THREADS, GCfg<256>::SMEM_BYTES, st>>>(prm);
+    tc_gemm_kernel<256, SCH_CROSS, false><<<grid, THREADS, GCfg<256, SCH_CROSS>::SMEM_BYTES, st>>>(prm);
     if (cudaGetLastError() != cudaSuccess) return RT_ERR_CUDA;
     // synchronous: returns once C is written, and reports a kernel that gave
     // up a wait.  The error word comes back on the caller's stream (pageable

@@ -49,8 +49,10 @@ __device__ __forceinline__ float block_reduce(float v, float* sh) {
 // thread holds VPT floats of the row: elements (v*THREADS + t)*4 .. +3 when
 // VEC (C % 4 == 0, aligned), else elements v*THREADS + t.
 // PLANES: the row is a GEMM's A operand; write its split planes (hi to y,
-// plane 1 to `x1`, mode `cross`) instead of the fp32 row.
-template <int KIND, int THREADS, int VPT, bool VEC, bool PLANES = false>
+// plane 1 to `x1`, mode `cross`) instead of the fp32 row -- or, with F16P,
+// its fp16 plane to y (2*C halves per row, C % 16 == 0) and its 2^-e scale
+// to ((float*)x1)[row], from the maximum of the normalised row.
+template <int KIND, int THREADS, int VPT, bool VEC, bool PLANES = false, bool F16P = false>
 __global__ void __launch_bounds__(256) row_kernel(const float* __restrict__ x,
                                                   const float* __restrict__ g,
                                                   const float* __restrict__ b,
@@ -121,7 +123,30 @@ __global__ void __launch_bounds__(256) row_kernel(const float* __restrict__ x,
             scale = s;  // divided below, as the reference does (reduce.c:95)
             shift = 0.0f;
         }
-        if (VEC) {
+        if (VEC && PLANES && F16P) {
+            float m = 0.0f;
+#pragma unroll
+            for (int i = 0; i < VPT; i++) {
+                const int c = ((i / 4) * THREADS + t) * 4 + (i % 4);
+                float val = v[i];
+                if (KIND == N_LAYER) val = val * scale * (c < C ? g[c] : 0.f) + (c < C ? b[c] : 0.f);
+                else val = val * scale * (c < C ? g[c] : 0.f);
+                v[i] = val;
+                if (c < C) m = fmaxf(m, fabsf(val));
+            }
+            m = block_reduce<THREADS, true>(m, sh);
+            const int e = f16_scale_exp(m);
+            const float sc = pow2i(e);
+            if (t == 0) reinterpret_cast<float*>(x1)[row] = pow2i(-e);
+            uint16_t* pr = reinterpret_cast<uint16_t*>(y) + row * C * 2;
+#pragma unroll
+            for (int i = 0; i < VPT / 4; i++) {
+                const int c = (i * THREADS + t) * 4;
+                if (c < C)
+                    store_f16x4(pr, c, make_float4(v[4 * i] * sc, v[4 * i + 1] * sc, v[4 * i + 2] * sc,
+                                                   v[4 * i + 3] * sc), true);
+            }
+        } else if (VEC) {
 #pragma unroll
             for (int i = 0; i < VPT / 4; i++) {
                 int c = (i * THREADS + t) * 4;
@@ -193,25 +218,31 @@ __global__ void __launch_bounds__(256) row_loop_kernel(const float* __restrict__
     }
 }
 
-template <int KIND, int THREADS, int VPT, bool VEC, bool PLANES = false>
+template <int KIND, int THREADS, int VPT, bool VEC, bool PLANES = false, bool F16P = false>
 void launch_rows(const float* x, const float* g, const float* b, float* y, int64_t rows, int C,
                  float eps, cudaStream_t st, uint16_t* x1 = nullptr, bool cross = true) {
     constexpr int GROUPS = 256 / THREADS;
     int64_t blocks = (rows + GROUPS - 1) / GROUPS;
     int64_t cap = (int64_t)g_num_sms * (THREADS == 32 ? 8 : 4) * 4;
     int grid = (int)(blocks < cap ? blocks : cap);
-    row_kernel<KIND, THREADS, VPT, VEC, PLANES><<<grid, 256, 0, st>>>(x, g, b, y, rows, C, eps, x1, cross);
+    row_kernel<KIND, THREADS, VPT, VEC, PLANES, F16P><<<grid, 256, 0, st>>>(x, g, b, y, rows, C, eps, x1, cross);
 }
 
+template <int KIND, bool F16P>
+void run_rows_planes_t(const float* x, const float* g, const float* b, float* hi, uint16_t* x1, int64_t rows,
+                       int C, float eps, bool cross, cudaStream_t st) {
+    if (C <= 128) launch_rows<KIND, 32, 4, true, true, F16P>(x, g, b, hi, rows, C, eps, st, x1, cross);
+    else if (C <= 256) launch_rows<KIND, 32, 8, true, true, F16P>(x, g, b, hi, rows, C, eps, st, x1, cross);
+    else if (C <= 512) launch_rows<KIND, 32, 16, true, true, F16P>(x, g, b, hi, rows, C, eps, st, x1, cross);
+    else if (C <= 1024) launch_rows<KIND, 32, 32, true, true, F16P>(x, g, b, hi, rows, C, eps, st, x1, cross);
+    else if (C <= 2048) launch_rows<KIND, 256, 8, true, true, F16P>(x, g, b, hi, rows, C, eps, st, x1, cross);
+    else launch_rows<KIND, 256, 16, true, true, F16P>(x, g, b, hi, rows, C, eps, st, x1, cross);
+}
 template <int KIND>
 void run_rows_planes(const float* x, const float* g, const float* b, float* hi, uint16_t* x1, int64_t rows,
-                     int C, float eps, bool cross, cudaStream_t st) {
-    if (C <= 128) launch_rows<KIND, 32, 4, true, true>(x, g, b, hi, rows, C, eps, st, x1, cross);
-    else if (C <= 256) launch_rows<KIND, 32, 8, true, true>(x, g, b, hi, rows, C, eps, st, x1, cross);
-    else if (C <= 512) launch_rows<KIND, 32, 16, true, true>(x, g, b, hi, rows, C, eps, st, x1, cross);
-    else if (C <= 1024) launch_rows<KIND, 32, 32, true, true>(x, g, b, hi, rows, C, eps, st, x1, cross);
-    else if (C <= 2048) launch_rows<KIND, 256, 8, true, true>(x, g, b, hi, rows, C, eps, st, x1, cross);
-    else launch_rows<KIND, 256, 16, true, true>(x, g, b, hi, rows, C, eps, st, x1, cross);
+                     int C, float eps, int scheme, cudaStream_t st) {
+    if (scheme == 2) run_rows_planes_t<KIND, true>(x, g, b, hi, x1, rows, C, eps, false, st);
+    else run_rows_planes_t<KIND, false>(x, g, b, hi, x1, rows, C, eps, scheme == 1, st);
 }
 
 template <int KIND>
@@ -370,11 +401,12 @@ Status launch_norm_rope(const RopeFold& r, cudaStream_t st, int* launches) {
 // go out as that GEMM's split planes (see row_kernel PLANES).
 bool norm_planes_supported(const OpNode& n) {
     const int C = last_dim(n);
+    // (fp16 scheme: whole 16-wide K blocks, so the plane is exactly 4 bytes per element)
     return (n.op == RT_OP_LAYERNORM || n.op == RT_OP_RMSNORM) && n.elem_size == 4 && C > 0 && C <= 4096 &&
-           C % 4 == 0 && aligned16(n.inputs[0]);
+           C % (gemm_scheme() == 2 ? 16 : 4) == 0 && aligned16(n.inputs[0]);
 }
 
-Status launch_norm_planes(const OpNode& nd, float* hi, void* x1, bool cross, cudaStream_t st, int* launches) {
+Status launch_norm_planes(const OpNode& nd, float* hi, void* x1, int scheme, cudaStream_t st, int* launches) {
     const int C = last_dim(nd);
     const int64_t rows = total_elements(nd) / C;
     if (rows == 0) return Status::ok();
@@ -383,9 +415,9 @@ Status launch_norm_planes(const OpNode& nd, float* hi, void* x1, bool cross, cud
     uint16_t* xp = static_cast<uint16_t*>(x1);
     if (nd.op == RT_OP_LAYERNORM)
         run_rows_planes<N_LAYER>(x, (const float*)nd.inputs[1], (const float*)nd.inputs[2], hi, xp, rows, C, eps,
-                                 cross, st);
+                                 scheme, st);
     else
-        run_rows_planes<N_RMS>(x, (const float*)nd.inputs[1], nullptr, hi, xp, rows, C, eps, cross, st);
+        run_rows_planes<N_RMS>(x, (const float*)nd.inputs[1], nullptr, hi, xp, rows, C, eps, scheme, st);
     RT_LAUNCH_CHECK();
     *launches += 1;
     return Status::ok();

@@ -68,9 +68,9 @@ struct SplitKey {
 };
 // Returns the cached split of `key`, or null.
 const SplitOperand* find_constant_split(const SplitKey& key);
-// Allocates (device, zeroed) and registers an empty split of `elems` floats
-// per part; the caller fills it.
-Status create_constant_split(const SplitKey& key, size_t elems, SplitOperand* out);
+// Allocates (device) and registers an empty split of `hi_elems` / `lo_elems`
+// floats; the caller fills it.
+Status create_constant_split(const SplitKey& key, size_t hi_elems, size_t lo_elems, SplitOperand* out);
 // True when [p, p+bytes) lies inside a range marked with rt_mark_constant.
 bool is_constant_range(const void* p, size_t bytes);
 
@@ -93,8 +93,13 @@ Status launch_gemm(const OpNode& n, cudaStream_t st, Workspace ws, int* launches
 // Whether a GEMM node can take a GemmFusion (tensor-core path).
 bool gemm_fusable(const OpNode& n);
 bool gemm_cross_scheme();   // plane 1 of split operands: cross (true) or lo (false)
+int gemm_scheme();          // 0 3xTF32, 1 tf32 + bf16 cross terms, 2 fp16 (one scaled plane + row scales)
+bool gemm_planes_from_epilogues();   // GEMM / attention epilogues may write a GEMM's split A operand
 bool norm_planes_supported(const OpNode& n);
-Status launch_norm_planes(const OpNode& n, float* hi, void* x1, bool cross, cudaStream_t st, int* launches);
+// The split A operand of the GEMM reading this norm's output: for schemes
+// 0/1 the hi plane at `hi` and plane 1 at `x1`; for the fp16 scheme (2) the
+// fp16 plane at `hi` and the per-row 2^-e scales at `x1`.
+Status launch_norm_planes(const OpNode& n, float* hi, void* x1, int scheme, cudaStream_t st, int* launches);
 Status prepare_gemm(const OpNode& n, cudaStream_t st);   // constant splits, before capture
 
 Status launch_attention(const OpNode& n, cudaStream_t st, Workspace ws, int* launches);

@@ -316,7 +316,7 @@ Status launch_item(Plan& p, size_t i, cudaStream_t st, int* launches) {
         if (p.items[i].norm_planes_off >= 0) {
             char* base = p.carry + p.items[i].norm_planes_off;
             return launch_norm_planes(p.nodes[i], reinterpret_cast<float*>(base), base + p.items[i].carry_plane_bytes,
-                                      gemm_cross_scheme(), st, launches);
+                                      gemm_scheme(), st, launches);
         }
         if (p.items[i].views) {
             AttnViews v = p.items[i].attn;
@@ -582,10 +582,10 @@ const SplitOperand* find_constant_split(const SplitKey& key) {
     return it == S().splits.end() ? nullptr : &it->second;
 }
 
-Status create_constant_split(const SplitKey& key, size_t elems, SplitOperand* out) {
+Status create_constant_split(const SplitKey& key, size_t hi_elems, size_t lo_elems, SplitOperand* out) {
     SplitOperand s;
-    if (cudaMalloc(&s.hi, elems * sizeof(float)) != cudaSuccess ||
-        cudaMalloc(&s.lo, elems * sizeof(float)) != cudaSuccess) {
+    if (cudaMalloc(&s.hi, hi_elems * sizeof(float)) != cudaSuccess ||
+        cudaMalloc(&s.lo, lo_elems * sizeof(float)) != cudaSuccess) {
         cudaGetLastError();
         if (s.hi) cudaFree(s.hi);
         return Status::err(RT_ERR_OOM, "split operand allocation failed");

@@ -234,6 +234,15 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
            | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// Instruction descriptor for kind::f16 with fp16 A and B, fp32 accumulation,
+// both operands K-major, tile M x N.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+    return (1u << 4)                 // D format: F32
+           | (0u << 7)               // A format: F16
+           | (0u << 10)              // B format: F16
+           | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
 // ---- CTA pairs (cluster of 2, tcgen05 cta_group::2) ------------------------
 __device__ __forceinline__ uint32_t cluster_ctarank() {
     uint32_t r;

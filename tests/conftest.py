@@ -20,6 +20,21 @@ load_package()
 from lbr_b200.program import ConstSpec, ProgNode, Program, Ref  # noqa: E402
 
 
+def gemm_scheme() -> str:
+    """The GEMM operand scheme the library selects from the environment
+    (read once per process, like the library does)."""
+    import os
+    if os.environ.get("RT_GEMM_3XTF32") == "1" or os.environ.get("RT_GEMM_SCHEME") == "3xtf32":
+        return "3xtf32"
+    return "cross" if os.environ.get("RT_GEMM_SCHEME") == "cross" else "f16"
+
+
+# Split-plane hand-offs from a GEMM or attention epilogue (RT_FUSE_HANDOFF,
+# RT_FUSE_ATTN_SPLIT) exist for the tf32 plane schemes only; under the fp16
+# scheme they are never planned.
+PLANE_HANDOFFS = gemm_scheme() != "f16"
+
+
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200)")
     config.addinivalue_line("markers", "slow: full-size programs")

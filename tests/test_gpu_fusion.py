@@ -8,6 +8,7 @@ import numpy as np
 import pytest
 
 import oracle
+from conftest import PLANE_HANDOFFS
 from lbr_b200.program import OP, ConstSpec, ProgNode, Program, Ref
 
 pytestmark = pytest.mark.gpu
@@ -55,7 +56,7 @@ def test_fused_chain_matches_oracle(M, D, F, kind, handoff, gpu_executor_factory
     flags = flags_of(ex, prog)
     assert flags[:2] == [3, 1]                       # GELU folded into the first GEMM
     if kind == 2:
-        assert flags[2] == (4 if handoff == "1" else 0)   # A operand handed over: no split pass
+        assert flags[2] == (4 if handoff == "1" and PLANE_HANDOFFS else 0)   # A operand handed over: no split pass
     ref = oracle.run_program("restated", prog, dict(prog.stored), {})[name]
     np.testing.assert_allclose(got, ref, atol=1e-4, rtol=1e-3)
 
@@ -73,7 +74,7 @@ def test_freed_executor_outputs_do_not_block_fusion(gpu_executor_factory):
         ex.close()
 
 
-@pytest.mark.parametrize("env", [{"RT_GEMM_3XTF32": "1"}, {"RT_GEMM_PAIR": "0"}],
+@pytest.mark.parametrize("env", [{"RT_GEMM_3XTF32": "1"}, {"RT_GEMM_PAIR": "0"}, {"RT_GEMM_SCHEME": "cross"}],
                          ids=lambda e: ",".join(f"{k}={v}" for k, v in e.items()))
 def test_fused_chain_variants(env):
     """Chains under the other GEMM variants (3xTF32 planes: hi + fp32 lo; the
@@ -164,19 +165,22 @@ def test_attention_split_hand_off_matches_golden(attn_split, residual, gpu_execu
     ops = [nd.op for nd in prog.nodes]
     proj = [i for i, op in enumerate(ops) if op == OP["MATMUL_ADD"] and OP["ATTENTION"] in ops[max(0, i - 3):i]]
     if residual == "0":
-        assert proj and all(flags[i] == (4 if attn_split == "1" else 0) for i in proj)
+        assert proj and all(flags[i] == (4 if attn_split == "1" and PLANE_HANDOFFS else 0) for i in proj)
     else:
         assert proj and all(flags[i] == 3 and flags[i + 1] == 1 for i in proj)
 
 
-def test_attention_split_hand_off_3xtf32():
-    """The same hand-off with the 3xTF32 plane layout (hi + fp32 lo), in a fresh process."""
+@pytest.mark.parametrize("env", [{"RT_GEMM_3XTF32": "1"}, {"RT_GEMM_SCHEME": "cross"}],
+                         ids=lambda e: ",".join(f"{k}={v}" for k, v in e.items()))
+def test_attention_split_hand_off_plane_schemes(env):
+    """The same hand-off with the tf32 plane layouts (3xTF32: hi + fp32 lo;
+    cross: hi + bf16 cross plane), each in a fresh process."""
     import os
     import subprocess
     import sys
     r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", "-m", "gpu", "-p", "no:cacheprovider",
                         __file__, "-k", "test_attention_split_hand_off_matches_golden"],
-                       env=dict(os.environ, RT_GEMM_3XTF32="1"), capture_output=True, text=True, timeout=600)
+                       env=dict(os.environ, **env), capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
 
 

@@ -253,6 +253,9 @@ def test_reshape_copy_and_embedding(gpu_executor_factory):
 @pytest.mark.gpu
 @pytest.mark.parametrize("env", [
     {"RT_GEMM_3XTF32": "1"},                       # three tf32 MMAs (hi.hi + hi.lo + lo.hi)
+    {"RT_GEMM_SCHEME": "cross"},                   # tf32 hi.hi + bf16 cross terms
+    {"RT_GEMM_SCHEME": "cross", "RT_GEMM_PAIR": "0"},
+    {"RT_GEMM_SCHEME": "cross", "RT_GEMM_TMA_STORE": "1"},
     {"RT_GEMM_PAIR": "0"},                         # one-CTA kernel everywhere
     {"RT_GEMM_PAIR": "0", "RT_GEMM_3XTF32": "1"},
     {"RT_GEMM_TMA_STORE": "1"},                    # C through shared memory and TMA stores
