@@ -12,7 +12,7 @@ data path (the only collectives are the timing barrier and max-reduction).
 
 `value` = sequences/s of the whole job with inputs already resident in HBM;
 `e2e` = the same through the public run() with pinned host inputs: PipelinedExecutor
-(two row chunks, copies overlapped with kernels) where a half-batch program exists,
+(row chunks, copies overlapped with kernels) where a chunk program exists,
 else CudaCompiledExecutor; the single-graph figure is reported beside it
 and outputs (host->device and device->host copies inside the timed region).
 The reference arm (--impl reference) times the reference's own C executor
@@ -53,6 +53,9 @@ CONFIGS = {
     "toy": "toy block d64 h4 ff256, B1 S32, fp32",
 }
 GLOBAL_BATCH = {"gpt2": 8, "qwen3": 8, "7b": 8, "1b8k": 8, "toy": 1}
+# Row chunks of the pipelined e2e run: the long 1b8k forward hides more of its
+# PCIe copies behind kernels with smaller chunks.
+E2E_CHUNKS = {"gpt2": 2, "qwen3": 2, "7b": 2, "1b8k": 4}
 # Batch of the host-side sample timed for the CPU baseline / reference arm.
 CPU_SAMPLE_BATCH = {"gpt2": 8, "qwen3": 8, "7b": 1, "1b8k": 1, "toy": 1}
 
@@ -189,6 +192,8 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=15.0,
                     help="seconds of host time for the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-chunks", type=int, default=0,
+                    help="row chunks of the pipelined e2e run (0: the per-config default)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -264,13 +269,17 @@ def main():
     barrier()
     e2e_ms = 1e3 * sum(e2e_times) / len(e2e_times)
     e2e_single_ms = e2e_ms
-    # The same through PipelinedExecutor: the batch as two row chunks (graphs
-    # planned for half the rows) whose host copies overlap each other's kernels.
+    # The same through PipelinedExecutor: the batch as row chunks (graphs
+    # planned for b_local / chunks rows) whose host copies overlap each other's kernels.
     pipe = None
-    half = program_name(args.config, b_local // 2) if b_local % 2 == 0 else None
-    if half and (GOLDEN / f"{half}.json").exists():
+    chunks = args.e2e_chunks or E2E_CHUNKS.get(args.config, 2)
+    while chunks > 1 and (b_local % chunks or
+                          not (GOLDEN / f"{program_name(args.config, b_local // chunks)}.json").exists()):
+        chunks //= 2
+    if chunks > 1:
         from lbr_b200.pipeline import PipelinedExecutor
-        pipe = PipelinedExecutor(Program.load(GOLDEN / f"{half}.json"), 2, consts, device=local_rank)
+        cprog = Program.load(GOLDEN / f"{program_name(args.config, b_local // chunks)}.json")
+        pipe = PipelinedExecutor(cprog, chunks, consts, device=local_rank)
         p_in = {k: pipe.input_buffer(k) for k in prog.inputs}
         for k, v in inputs.items():
             p_in[k][...] = v
@@ -314,7 +323,7 @@ def main():
             "latency_ms": round(ms, 4),
             "e2e": {"value": round(gb / (e2e_ms / 1e3), 3), "unit": unit, "latency_ms": round(e2e_ms, 4),
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-                    "api": ("PipelinedExecutor.run (2 row chunks, copies overlapped with kernels)"
+                    "api": (f"PipelinedExecutor.run ({chunks} row chunks, copies overlapped with kernels)"
                             if pipe is not None else "CudaCompiledExecutor.run"),
                     "single_graph_value": round(gb / (e2e_single_ms / 1e3), 3)},
             "gpu_launches": launches * args.steps,

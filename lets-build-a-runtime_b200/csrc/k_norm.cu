@@ -235,7 +235,7 @@ void run_rows_planes_t(const float* x, const float* g, const float* b, float* hi
     else if (C <= 256) launch_rows<KIND, 32, 8, true, true, F16P>(x, g, b, hi, rows, C, eps, st, x1, cross);
     else if (C <= 512) launch_rows<KIND, 32, 16, true, true, F16P>(x, g, b, hi, rows, C, eps, st, x1, cross);
     else if (C <= 1024) launch_rows<KIND, 32, 32, true, true, F16P>(x, g, b, hi, rows, C, eps, st, x1, cross);
-    else if (C <= 2048) launch_rows<KIND, 256, 8, true, true, F16P>(x, g, b, hi, rows, C, eps, st, x1, cross);
+    else if (C <= 2048) launch_rows<KIND, 32, 64, true, true, F16P>(x, g, b, hi, rows, C, eps, st, x1, cross);
     else launch_rows<KIND, 256, 16, true, true, F16P>(x, g, b, hi, rows, C, eps, st, x1, cross);
 }
 template <int KIND>
@@ -255,7 +255,7 @@ Status run_rows(const float* x, const float* g, const float* b, float* y, int64_
         else if (C <= 256) launch_rows<KIND, 32, 8, true>(x, g, b, y, rows, C, eps, st);
         else if (C <= 512) launch_rows<KIND, 32, 16, true>(x, g, b, y, rows, C, eps, st);
         else if (C <= 1024) launch_rows<KIND, 32, 32, true>(x, g, b, y, rows, C, eps, st);
-        else if (C <= 2048) launch_rows<KIND, 256, 8, true>(x, g, b, y, rows, C, eps, st);
+        else if (C <= 2048) launch_rows<KIND, 32, 64, true>(x, g, b, y, rows, C, eps, st);
         else if (C <= 4096) launch_rows<KIND, 256, 16, true>(x, g, b, y, rows, C, eps, st);
         else vec = false;
     }
