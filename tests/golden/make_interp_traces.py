@@ -13,7 +13,7 @@ reference's own ``InterpretedExecutor`` with its numpy backend on the same
 weights and inputs and stores that result next to the trace.
 
 Weights and inputs are those of the committed programs (``<name>.json`` /
-``<name>.golden.npz``), so the replay is also checked against the reference
+``<name>.golden.npz``; the traces go to ``interp/<name>.json`` / ``.npz``), so the replay is also checked against the reference
 C executor's golden output.
 
     python tests/golden/make_interp_traces.py
@@ -96,8 +96,8 @@ def trace(name):
     interp = ex.run(inputs)
     doc = {"name": name, "graph_inputs": list(graph.inputs), "graph_outputs": list(graph.outputs),
            "generator": "tests/golden/make_interp_traces.py", "steps": steps}
-    (HERE / f"{name}.interp.json").write_text(json.dumps(doc, indent=0))
-    np.savez_compressed(HERE / f"{name}.interp.npz", **{f"out__{k}": v for k, v in interp.items()})
+    (HERE / "interp" / f"{name}.json").write_text(json.dumps(doc, indent=0))
+    np.savez_compressed(HERE / "interp" / f"{name}.npz", **{f"out__{k}": v for k, v in interp.items()})
     ref = {k[5:]: gold[k] for k in gold.files if k.startswith("out__")}
     err = max(float(np.abs(interp[k] - ref[k]).max()) for k in ref)
     print(f"{name}: {len(steps)} steps ({sum(s['alias'] for s in steps)} aliases), "

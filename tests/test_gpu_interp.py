@@ -59,9 +59,9 @@ def replay(backend, doc, consts, inputs):
 
 @pytest.mark.parametrize("name", NAMES)
 def test_interpreted_replay_matches_reference(name, backend):
-    doc = json.loads((GOLDEN / f"{name}.interp.json").read_text())
+    doc = json.loads((GOLDEN / "interp" / f"{name}.json").read_text())
     gold = np.load(GOLDEN / f"{name}.golden.npz")
-    interp = np.load(GOLDEN / f"{name}.interp.npz")
+    interp = np.load(GOLDEN / "interp" / f"{name}.npz")
     consts = Program.load(GOLDEN / f"{name}.json").make_constants(0)
     inputs = {k[4:]: gold[k] for k in gold.files if k.startswith("in__")}
     got, calls = replay(backend, doc, consts, inputs)
