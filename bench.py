@@ -55,7 +55,7 @@ CONFIGS = {
 GLOBAL_BATCH = {"gpt2": 8, "qwen3": 8, "7b": 8, "1b8k": 8, "toy": 1}
 # Row chunks of the pipelined e2e run: the long 1b8k forward hides more of its
 # PCIe copies behind kernels with smaller chunks.
-E2E_CHUNKS = {"gpt2": 2, "qwen3": 2, "7b": 2, "1b8k": 4}
+E2E_CHUNKS = {"gpt2": 2, "qwen3": 2, "7b": 2, "1b8k": 8}
 # Batch of the host-side sample timed for the CPU baseline / reference arm.
 CPU_SAMPLE_BATCH = {"gpt2": 8, "qwen3": 8, "7b": 1, "1b8k": 1, "toy": 1}
 
