@@ -22,6 +22,38 @@ __device__ __forceinline__ float gelu_tanh(float x) {
     return 0.5f * x * (1.0f + t);
 }
 
+// ---- element-wise arithmetic shared by the element-wise kernels and the
+// small-graph kernel (csrc/ops/elementwise.c, csrc/ops/shape.c:46-51) ----
+enum UnaryKind { U_RELU, U_EXP, U_TANH, U_POW, U_GELU, U_RSQRT, U_SILU, U_NEG, U_COS, U_SIN };
+
+__device__ __forceinline__ float silu(float v) { return v / (1.0f + expf(-v)); }
+
+template <int K>
+__device__ __forceinline__ float unary_op(float v, float p) {
+    if (K == U_RELU) return v > 0.0f ? v : 0.0f;
+    if (K == U_EXP) return expf(v);
+    if (K == U_TANH) return tanhf(v);
+    if (K == U_POW) return powf(v, p);
+    if (K == U_GELU) return gelu_tanh(v);
+    if (K == U_RSQRT) return 1.0f / sqrtf(v);
+    if (K == U_SILU) return silu(v);
+    if (K == U_NEG) return -v;
+    if (K == U_COS) return cosf(v);
+    return sinf(v);
+}
+
+enum BinKind { B_ADD = 0, B_SUB = 1, B_MUL = 2, B_DIV = 3, B_ADD_RELU = 4 };
+
+template <int K>
+__device__ __forceinline__ float bin_op(float a, float b) {
+    if (K == B_ADD) return a + b;
+    if (K == B_SUB) return a - b;
+    if (K == B_MUL) return a * b;
+    if (K == B_DIV) return a / b;
+    float v = a + b;
+    return v > 0.0f ? v : 0.0f;
+}
+
 // Operand split shared by the GEMM's split pass and producers that write a
 // GEMM's split A operand directly: hi = x rounded to tf32 (nearest, ties away),
 // lo = x - hi, and bf16 (round to nearest even) bit patterns.

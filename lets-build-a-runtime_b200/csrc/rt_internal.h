@@ -103,6 +103,16 @@ Status launch_norm_planes(const OpNode& n, float* hi, void* x1, int scheme, cuda
 Status prepare_gemm(const OpNode& n, cudaStream_t st);   // constant splits, before capture
 
 Status launch_attention(const OpNode& n, cudaStream_t st, Workspace ws, int* launches);
+
+// Small graphs (k_tiny.cu): the whole node array in one cluster launch.
+struct TinyPlan {
+    OpNode* dev_nodes = nullptr;   // device copy of the node array
+    int n = 0;                     // 0: not used by this plan
+};
+bool tiny_graph_applicable(const std::vector<OpNode>& nodes);
+Status tiny_graph_build(const std::vector<OpNode>& nodes, TinyPlan* out);   // before any capture
+Status launch_tiny(const TinyPlan& t, cudaStream_t st, int* launches);
+void free_tiny(TinyPlan& t);
 // Strided operands of a fused attention: element (b, h, s, d) of X lives at
 // X + b*X_sb + h*X_sh + s*X_ss + d.  Produced by the plan's layout fusion.
 struct AttnViews {

@@ -50,6 +50,8 @@ struct Plan {
     size_t carry_bytes = 0;
     char* bias = nullptr;          // merged biases of folded bias ADDs
     BiasPlan bias_plan;
+    TinyPlan tiny;                 // set: the graph runs as one small-graph launch (per-node
+                                   // profiling still launches the nodes one by one)
 };
 
 struct State {
@@ -357,6 +359,7 @@ Status launch_item(Plan& p, size_t i, cudaStream_t st, int* launches) {
 }
 
 Status launch_all(Plan& p, cudaStream_t st, int* launches) {
+    if (p.tiny.n) return launch_tiny(p.tiny, st, launches);
     for (size_t i = 0; i < p.nodes.size(); i++) {
         Status s = launch_item(p, i, st, launches);
         if (!s.good()) {
@@ -372,6 +375,7 @@ void free_plan(Plan& p) {
     if (p.ws) cudaFree(p.ws);
     if (p.carry) cudaFree(p.carry);
     if (p.bias) cudaFree(p.bias);
+    free_tiny(p.tiny);
     p.exec = nullptr;
     p.ws = nullptr;
     p.carry = nullptr;
@@ -450,6 +454,13 @@ Status build_plan(const OpNode* nodes, int n, bool capture, Plan** out) {
                 free_plan(*plan);
                 return s;
             }
+        }
+    }
+    if (tiny_graph_applicable(plan->nodes)) {
+        Status s = tiny_graph_build(plan->nodes, &plan->tiny);
+        if (!s.good()) {
+            free_plan(*plan);
+            return s;
         }
     }
     if (capture) {
