@@ -66,6 +66,8 @@ constexpr int CHUNK = 32 * 1024;                      // ring stage / packed chu
 constexpr uint64_t WAIT_NS = 2000000000ull;
 constexpr int ERR_A_PROD = 0x201, ERR_A_MMA = 0x202, ERR_A_SOFT = 0x203, ERR_A_DRAIN = 0x204;
 constexpr uint32_t COL_S = 0, COL_PH = 128, COL_PL = 256, COL_O = 384;
+constexpr int FOLD_EVERY = 3;              // P.V tiles accumulated in TMEM between register folds
+constexpr float RESCALE_LOG2 = 8.0f;       // a row keeps its reference max until a tile max exceeds it by this
 
 template <int D>
 struct AttnTcCfg {
@@ -280,7 +282,8 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     int* issued = const_cast<int*>(abort_flag) + 1;    // [STAGES + 1] phase of the last load (ring, Q), -1 none
     volatile int* items = issued + STAGES + 1;         // [4] item ring: item r in slot r % 4, -1 = no more
-    static_assert(NBAR * 8 + 8 + 4 * (STAGES + 1) + 16 <= C::BAR_BYTES, "barrier area");
+    volatile int* pv_fresh = items + 4;                // [2] per tile parity: P.V starts a new O accumulator
+    static_assert(NBAR * 8 + 8 + 4 * (STAGES + 1) + 16 + 8 <= C::BAR_BYTES, "barrier area");
     float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + C::BAR_BYTES);   // [2][2][128]
     if ((smem - smem_raw) + C::BODY > C::SMEM) {   // dynamic shared memory less aligned than assumed
         if (threadIdx.x == 0 && p.err) atomicCAS(p.err, 0, 0x205);
@@ -411,7 +414,7 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
                 }
                 if (ok) ptx::mma_commit(s_full);
             };
-            auto issue_pv = [&]() {
+            auto issue_pv = [&](bool fresh) {
                 for (int c = 0; c < C::V_CHUNKS; c++) {
                     uint8_t* buf = pop();
                     if (!buf) return;
@@ -421,7 +424,8 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
                     for (int kk = 0; kk < C::V_KEYS / 8; kk++) {
                         const uint64_t off = (uint64_t)((((kk >> 2) * D * 128) + (kk & 3) * 32) >> 4);
                         const uint32_t kc = c * C::V_KEYS + kk * 8;
-                        ptx::mma_tf32_ts(tmem + COL_O, tmem + COL_PH + kc, bh0 + off, idesc_o, (c | kk) ? 1u : 0u);
+                        ptx::mma_tf32_ts(tmem + COL_O, tmem + COL_PH + kc, bh0 + off, idesc_o,
+                                         (c | kk | !fresh) ? 1u : 0u);
                         if (CROSS) {
                             // doubled K: 8 columns = 16 bf16 of P plane 1 per step, 32 bytes of V plane 1
                             ptx::mma_bf16_ts(tmem + COL_O, tmem + COL_PL + kc, bl0 + off, idesc_ox, 1u);
@@ -460,7 +464,7 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
                     if (!ok) break;
                     if (!(ok = ptx::wait_bounded(p_full, T & 1, abort_flag, p.err, ERR_A_MMA, WAIT_NS))) break;
                     ptx::tc_fence_after();
-                    issue_pv();
+                    issue_pv(pv_fresh[T & 1] != 0);
                 }
             }
             ptx::mma_commit(drain);
@@ -516,6 +520,7 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
             }
             const int q = it.q0 + row;
             float m = -FLT_MAX, l = 0.0f;   // m in log2 units; -FLT_MAX as the reference's initial max
+            int pend = 0;                   // P.V tiles accumulated in TMEM since the last fold
             float o[DH];
 #pragma unroll
             for (int i = 0; i < DH; i++) o[i] = 0.0f;
@@ -552,17 +557,29 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
                 red[((T & 1) * 2 + half) * BQ + row] = mt;
                 if (!(ok = pair_sync(T & 1, (T >> 1) & 1))) break;
                 mt = fmaxf(mt, red[((T & 1) * 2 + (half ^ 1)) * BQ + row]);
-                const float m_new = mt > m ? mt : m;
+                // Lazy rescaling: the row's reference max m stays put until a
+                // tile's max exceeds it by more than 2^RESCALE_LOG2 (P <= 2^8
+                // meanwhile), and O accumulates in TMEM over up to FOLD_EVERY
+                // tiles before it is folded into registers (the same bounded
+                // accumulation length as the GEMM's K chunks).  A row that does
+                // rescale between folds scales its pending TMEM O in place.
+                const bool first = j == 0;
+                const bool fold = !first && pend >= FOLD_EVERY;   // uniform: one accumulator per tile
+                float m_new = m;
+                if (first || mt > m + RESCALE_LOG2 || (fold && mt > m)) m_new = mt > m ? mt : m;
                 float lt = 0.0f;
 #pragma unroll
                 for (int i = 0; i < KH; i++) {
                     sv[i] = ex2_approx(sv[i] - m_new);   // masked: 2^-inf = 0
                     lt += sv[i];
                 }
-                if (j > 0) {   // O tile j-1 (relative to the old max): fold, freeing the tile and P
+                const float corr = m_new > m ? ex2_approx(m - m_new) : 1.0f;
+                if (!first) {   // PV of tile j-1 done: P may be overwritten, pending O is complete
                     if (!(ok = ptx::wait_bounded(pv_full, (T - 1) & 1, abort_flag, p.err, ERR_A_SOFT, WAIT_NS)))
                         break;
                     ptx::tc_fence_after();
+                }
+                if (fold) {   // pending O (relative to the old max) into registers
 #pragma unroll
                     for (int g = 0; g < DH / 32; g++) {   // 32 columns per batch keeps registers in bounds
                         uint32_t rr[32];
@@ -574,15 +591,30 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
 #pragma unroll
                         for (int i = 0; i < 32; i++) o[g * 32 + i] += __uint_as_float(rr[i]);
                     }
+                } else if (!first && __any_sync(0xffffffffu, m_new > m)) {
+                    // rescale this warp's rows of the pending TMEM O (warp-collective;
+                    // corr is 1 for the rows that keep their max)
+#pragma unroll
+                    for (int g = 0; g < DH / 16; g++) {
+                        uint32_t rr[16];
+                        const uint32_t at = tmem + lane_off + COL_O + half * DH + g * 16;
+                        ptx::tmem_ld16(at, rr);
+                        ptx::tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 16; i++) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * corr);
+                        ptx::tmem_st16(at, rr);
+                    }
+                    ptx::tmem_st_wait();
                 }
-                if (m_new > m) {   // running max grew: rescale (corr would be 1 otherwise)
-                    const float corr = ex2_approx(m - m_new);
+                if (m_new > m) {   // running max grew: rescale the folded part (corr would be 1 otherwise)
                     l *= corr;
 #pragma unroll
                     for (int i = 0; i < DH; i++) o[i] *= corr;
                     m = m_new;
                 }
                 l += lt;
+                pend = (first || fold) ? 1 : pend + 1;
+                if (threadIdx.x == 128) pv_fresh[T & 1] = (first || fold) ? 1 : 0;   // PV_j starts a new accumulator
 #pragma unroll
                 for (int c16 = 0; c16 < KH / 16; c16++) {
                     uint32_t ph[16], pl[16];
