@@ -105,22 +105,33 @@ __device__ __forceinline__ int f16_scale_exp(float m) {
     return e < -120 ? -120 : (e > 120 ? 120 : e);
 }
 __device__ __forceinline__ float pow2i(int e) { return __uint_as_float((uint32_t)(127 + e) << 23); }
-__device__ __forceinline__ uint32_t f16_hl(float x, uint16_t* lo) {
-    const __half h = __float2half_rn(x);
-    *lo = __half_as_ushort(__float2half_rn(x - __half2float(h)));
-    return __half_as_ushort(h);
+// h = x rounded to 11 significant bits (ties away) by integer arithmetic on
+// its bits -- the fp16 value of x for |x| in the fp16 normal range -- and
+// l = x - h, exact.  The conversion instructions then only pack: one
+// cvt.rn.f16x2 per two values (exact for h; l keeps 11 bits of the residual).
+__device__ __forceinline__ float round11(float x) {
+    return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
+}
+__device__ __forceinline__ uint32_t f16x2_rn(float lo, float hi) {   // lo in the low half
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
 }
 // Four consecutive elements k..k+3 (k % 4 == 0, already scaled) of a row into
 // its fp16 plane: per 16-wide K block 32 halves, [h(16) | l(16)] when
 // first_hi (A operands), [l(16) | h(16)] otherwise (B operands).
 __device__ __forceinline__ void store_f16x4(uint16_t* row, int64_t k, float4 v, bool first_hi) {
-    uint16_t l0, l1, l2, l3;
-    const uint32_t h0 = f16_hl(v.x, &l0), h1 = f16_hl(v.y, &l1), h2 = f16_hl(v.z, &l2), h3 = f16_hl(v.w, &l3);
-    const uint2 hh = make_uint2(h0 | (h1 << 16), h2 | (h3 << 16));
-    const uint2 ll = make_uint2((uint32_t)l0 | ((uint32_t)l1 << 16), (uint32_t)l2 | ((uint32_t)l3 << 16));
+    const float h0 = round11(v.x), h1 = round11(v.y), h2 = round11(v.z), h3 = round11(v.w);
+    const uint2 hh = make_uint2(f16x2_rn(h0, h1), f16x2_rn(h2, h3));
+    const uint2 ll = make_uint2(f16x2_rn(v.x - h0, v.y - h1), f16x2_rn(v.z - h2, v.w - h3));
     uint16_t* blk = row + (k >> 4) * 32 + (k & 15);
     *reinterpret_cast<uint2*>(blk + (first_hi ? 0 : 16)) = hh;
     *reinterpret_cast<uint2*>(blk + (first_hi ? 16 : 0)) = ll;
+}
+// One element: its h and l halves (h in the low 16 bits of the result).
+__device__ __forceinline__ uint32_t f16_hl(float x) {
+    const float h = round11(x);
+    return f16x2_rn(h, x - h);
 }
 
 }  // namespace rt

@@ -970,8 +970,8 @@ __global__ void split16_transpose_kernel(const float* __restrict__ x, uint16_t* 
     for (int r = threadIdx.y; r < 32; r += blockDim.y) {
         const int n = n0 + r, k = k0 + threadIdx.x;
         if (n < N && k < K16) {
-            uint16_t lo;
-            const uint16_t hi = (uint16_t)f16_hl(tile[threadIdx.x][r] * sc, &lo);
+            const uint32_t hl = f16_hl(tile[threadIdx.x][r] * sc);
+            const uint16_t hi = (uint16_t)(hl & 0xffffu), lo = (uint16_t)(hl >> 16);
             uint16_t* blk = plane + (bz * N + n) * (2 * (int64_t)K16) + (k >> 4) * 32 + (k & 15);
             blk[first_hi ? 0 : 16] = hi;
             blk[first_hi ? 16 : 0] = lo;

