@@ -47,7 +47,7 @@ __device__ __forceinline__ float block_reduce(float v, float* sh) {
 
 // One row per group of THREADS threads (a warp or the whole CTA); each
 // thread holds VPT floats of the row: elements (v*THREADS + t)*4 .. +3 when
-// VEC (C % 4 == 0, aligned), else elements v*THREADS + t.
+// VEC (C % 4 == 0; x, y, gamma, beta 16-byte aligned), else elements v*THREADS + t.
 // PLANES: the row is a GEMM's A operand; write its split planes (hi to y,
 // plane 1 to `x1`, mode `cross`) instead of the fp32 row -- or, with F16P,
 // its fp16 plane to y (2*C halves per row, C % 16 == 0) and its 2^-e scale
@@ -126,13 +126,21 @@ __global__ void __launch_bounds__(256) row_kernel(const float* __restrict__ x,
         if (VEC && PLANES && F16P) {
             float m = 0.0f;
 #pragma unroll
-            for (int i = 0; i < VPT; i++) {
-                const int c = ((i / 4) * THREADS + t) * 4 + (i % 4);
-                float val = v[i];
-                if (KIND == N_LAYER) val = val * scale * (c < C ? g[c] : 0.f) + (c < C ? b[c] : 0.f);
-                else val = val * scale * (c < C ? g[c] : 0.f);
-                v[i] = val;
-                if (c < C) m = fmaxf(m, fabsf(val));
+            for (int i = 0; i < VPT / 4; i++) {
+                const int c = (i * THREADS + t) * 4;
+                if (c < C) {   // gamma / beta as 16-byte vectors (aligned on this path)
+                    const float4 g4 = *reinterpret_cast<const float4*>(g + c);
+                    const float4 b4 = KIND == N_LAYER ? *reinterpret_cast<const float4*>(b + c)
+                                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+                    const float gg[4] = {g4.x, g4.y, g4.z, g4.w}, bv[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        float val = v[4 * i + k] * scale * gg[k];
+                        if (KIND == N_LAYER) val += bv[k];
+                        v[4 * i + k] = val;
+                        m = fmaxf(m, fabsf(val));
+                    }
+                }
             }
             m = block_reduce<THREADS, true>(m, sh);
             const int e = f16_scale_exp(m);
@@ -153,11 +161,15 @@ __global__ void __launch_bounds__(256) row_kernel(const float* __restrict__ x,
                 if (c < C) {
                     float4 o;
                     float* op = &o.x;
+                    float4 g4 = make_float4(0.f, 0.f, 0.f, 0.f), b4 = g4;
+                    if (KIND != N_SOFTMAX) g4 = *reinterpret_cast<const float4*>(g + c);   // aligned on this path
+                    if (KIND == N_LAYER) b4 = *reinterpret_cast<const float4*>(b + c);
+                    const float gg[4] = {g4.x, g4.y, g4.z, g4.w}, bv[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
                     for (int k = 0; k < 4; k++) {
                         float val = v[4 * i + k];
-                        if (KIND == N_LAYER) val = val * scale * g[c + k] + b[c + k];
-                        else if (KIND == N_RMS) val = val * scale * g[c + k];
+                        if (KIND == N_LAYER) val = val * scale * gg[k] + bv[k];
+                        else if (KIND == N_RMS) val = val * scale * gg[k];
                         else val = val / scale;
                         op[k] = val + shift;
                     }
@@ -249,7 +261,7 @@ template <int KIND>
 Status run_rows(const float* x, const float* g, const float* b, float* y, int64_t rows, int C,
                 float eps, cudaStream_t st) {
     if (rows == 0 || C == 0) return Status::ok();
-    bool vec = C % 4 == 0 && aligned16(x) && aligned16(y);
+    bool vec = C % 4 == 0 && aligned16(x) && aligned16(y) && (!g || aligned16(g)) && (!b || aligned16(b));
     if (vec) {
         if (C <= 128) launch_rows<KIND, 32, 4, true>(x, g, b, y, rows, C, eps, st);
         else if (C <= 256) launch_rows<KIND, 32, 8, true>(x, g, b, y, rows, C, eps, st);
@@ -403,7 +415,8 @@ bool norm_planes_supported(const OpNode& n) {
     const int C = last_dim(n);
     // (fp16 scheme: whole 16-wide K blocks, so the plane is exactly 4 bytes per element)
     return (n.op == RT_OP_LAYERNORM || n.op == RT_OP_RMSNORM) && n.elem_size == 4 && C > 0 && C <= 4096 &&
-           C % (gemm_scheme() == 2 ? 16 : 4) == 0 && aligned16(n.inputs[0]);
+           C % (gemm_scheme() == 2 ? 16 : 4) == 0 && aligned16(n.inputs[0]) && aligned16(n.inputs[1]) &&
+           (n.op != RT_OP_LAYERNORM || aligned16(n.inputs[2]));
 }
 
 Status launch_norm_planes(const OpNode& nd, float* hi, void* x1, int scheme, cudaStream_t st, int* launches) {
