@@ -59,6 +59,9 @@ namespace {
 // warpgroups 1-2: the softmax.  Launched at 168 registers a thread (384 x 168
 // fit the SM's 64 Ki), then rebalanced: warpgroup 0 down to REG_CTRL, the
 // softmax up to REG_SOFT (128 x 120 + 256 x 192 = 384 x 168).
+#ifndef RT_ATTN_RING128
+#define RT_ATTN_RING128 3   // ring stages at head_dim 128 (what the shared memory left by Q allows)
+#endif
 constexpr int BQ = 128, BKV = 128, SOFT_WARPS = 8, ATHREADS = 128 + 32 * SOFT_WARPS;
 constexpr int REG_CTRL = 120, REG_SOFT = 192;
 static_assert(128 * REG_CTRL + 32 * SOFT_WARPS * REG_SOFT <= ATHREADS * 168, "register split");
@@ -76,7 +79,7 @@ struct AttnTcCfg {
     static constexpr int V_KEYS = D == 128 ? 32 : 64;           // keys per V chunk (D x keys, hi | lo)
     static constexpr int V_CHUNKS = BKV / V_KEYS;
     static constexpr int TILE_BYTES = (K_CHUNKS + V_CHUNKS) * CHUNK;
-    static constexpr int STAGES = D == 128 ? 3 : 5;
+    static constexpr int STAGES = D == 128 ? RT_ATTN_RING128 : 5;
     static constexpr int BAR_BYTES = 384;                       // mbarriers, TMEM slot, flags, item ring
     static constexpr int BODY = 2 * Q_BYTES + STAGES * CHUNK + BAR_BYTES + 4 * BQ * 4 /*row exchange*/;
     static constexpr int SMEM = 232448;                         // the per-CTA maximum; BODY + alignment slack

@@ -7,7 +7,8 @@
 // TC CTAs that walks the node array on the device, node after node, with a
 // cluster barrier (barrier.cluster release / acquire: every global write of a
 // node is visible to the whole cluster before the next node starts) between
-// nodes.  Each node's work is spread over the cluster's threads.
+// nodes.  Each node's work is spread over the cluster's threads.  By default
+// the "cluster" is a single CTA (RT_TINY_CTAS=8 selects eight).
 //
 // Semantics are the reference's dispatch (csrc/executor.c:54-397), node for
 // node, on the same OpNode array the other kernels run:
@@ -28,15 +29,16 @@ namespace rt {
 namespace {
 
 constexpr int TT = 512;                 // threads per CTA
-constexpr int TC = 8;                   // CTAs per cluster (portable maximum)
-constexpr int TSMEM = 64 * 1024;        // dynamic shared memory per CTA (attention scores, GEMM tiles)
+constexpr int TC = 8;                   // CTAs per cluster (portable maximum) of the cluster form
+constexpr int TSMEM = 80 * 1024;        // dynamic shared memory per CTA (attention scores, GEMM tiles)
+constexpr int KC = 256;                 // K per GEMM shared-memory chunk: the toy's GEMMs load A and B once
 constexpr int ATT_S_MAX = 128;          // S x S fp32 scores of one head fit TSMEM
 constexpr int64_t MAX_NODE_ELEMS = (int64_t)1 << 18;
 constexpr int64_t MAX_NODE_MACS = (int64_t)1 << 22;
 constexpr int64_t MAX_TOTAL_MACS = (int64_t)1 << 23;
 
 struct Th {
-    int rank, tid, g, G;   // CTA rank in the cluster, thread in the CTA, thread in the cluster, cluster threads
+    int rank, C, tid, g, G;   // CTA rank, CTAs, thread in the CTA, thread over all CTAs, all threads
 };
 
 __device__ __forceinline__ int64_t numel_d(const OpNode& n) {
@@ -148,8 +150,8 @@ __device__ void rows_d(const OpNode& n, const Th& t) {
 }
 
 // C[b] = alpha * A[b] . op(B[b]) (+ bias): 32 x 32 output tiles spread over
-// the cluster's CTAs; per CTA A and B chunks of 64 along K in shared memory,
-// two outputs per thread.
+// the CTAs; per CTA A and B chunks of up to KC along K in shared memory (one
+// chunk for K <= KC: all loads in flight at once), two outputs per thread.
 __device__ void gemm_d(const OpNode& n, const Th& t, float* sm) {
     const bool with_bias = n.op == RT_OP_MATMUL_ADD;
     const int64_t N = n.out_shape[n.n_dims - 1], K = n.extra[0];
@@ -167,32 +169,34 @@ __device__ void gemm_d(const OpNode& n, const Th& t, float* sm) {
     const float* B = (const float*)n.inputs[1];
     const float* bias = with_bias ? (const float*)n.inputs[2] : nullptr;
     float* Cp = (float*)n.output;
-    float(*As)[33] = reinterpret_cast<float(*)[33]>(sm);             // [64 k][32 m]
-    float(*Bs)[33] = reinterpret_cast<float(*)[33]>(sm + 64 * 33);   // [64 k][32 n]
+    float(*As)[33] = reinterpret_cast<float(*)[33]>(sm);             // [KC k][32 m]
+    float(*Bs)[33] = reinterpret_cast<float(*)[33]>(sm + KC * 33);   // [KC k][32 n]
     const int64_t mt = (M + 31) / 32, nt = (N + 31) / 32, tiles = batches * mt * nt;
     const int ty = t.tid >> 4, tx = (t.tid & 15) * 2;
-    for (int64_t tile = t.rank; tile < tiles; tile += TC) {
+    for (int64_t tile = t.rank; tile < tiles; tile += t.C) {
         const int64_t bz = tile / (mt * nt), rem = tile % (mt * nt);
         const int64_t m0 = (rem / nt) * 32, n0 = (rem % nt) * 32;
         const float* Ab = A + bz * M * K;
         const float* Bb = B + (b2d ? 0 : bz * N * K);
         float acc0 = 0.f, acc1 = 0.f;
-        for (int64_t k0 = 0; k0 < K; k0 += 64) {
-            for (int e = t.tid; e < 64 * 32; e += TT) {
-                const int k = e & 63, r = e >> 6;   // A: consecutive threads walk K of one row
+        for (int64_t k0 = 0; k0 < K; k0 += KC) {
+#pragma unroll 4
+            for (int e = t.tid; e < KC * 32; e += TT) {
+                const int k = e % KC, r = e / KC;   // A: consecutive threads walk K of one row
                 const int64_t gm = m0 + r, gk = k0 + k;
                 As[k][r] = (gm < M && gk < K) ? Ab[gm * K + gk] : 0.f;
                 const int64_t gn = n0 + r;
                 if (tb) Bs[k][r] = (gn < N && gk < K) ? Bb[gn * K + gk] : 0.f;
             }
             if (!tb)
-                for (int e = t.tid; e < 64 * 32; e += TT) {
+#pragma unroll 4
+                for (int e = t.tid; e < KC * 32; e += TT) {
                     const int c = e & 31, k = e >> 5;   // B [K][N]: consecutive threads walk N
                     const int64_t gn = n0 + c, gk = k0 + k;
                     Bs[k][c] = (gn < N && gk < K) ? Bb[gk * N + gn] : 0.f;
                 }
             __syncthreads();
-            const int kmax = (int)min((int64_t)64, K - k0);
+            const int kmax = (int)min((int64_t)KC, K - k0);
             for (int k = 0; k < kmax; k++) {
                 const float a = As[k][ty];
                 acc0 = fmaf(a, Bs[k][tx], acc0);
@@ -222,7 +226,7 @@ __device__ void attention_d(const OpNode& n, const Th& t, float* sm) {
     float* O = (float*)n.output;
     const float scale = 1.0f / sqrtf((float)D);
     const int lane = t.tid & 31, warp = t.tid >> 5;
-    for (int64_t bh = t.rank; bh < BH; bh += TC) {
+    for (int64_t bh = t.rank; bh < BH; bh += t.C) {
         const float* q = Q + bh * S * D;
         const float* k = Kp + (bh / group) * S * D;
         const float* v = V + (bh / group) * S * D;
@@ -376,18 +380,33 @@ __device__ void run_node(const OpNode& n, const Th& t, float* sm) {
     }
 }
 
-__global__ void __cluster_dims__(TC, 1, 1) __launch_bounds__(TT, 1)
-    tiny_graph_kernel(const OpNode* __restrict__ nodes, int n_nodes) {
+// NC == 1: one CTA, a CTA barrier between nodes; NC > 1: a cluster of NC
+// CTAs (launched with the cluster attribute), a cluster barrier.
+template <int NC>
+__global__ void __launch_bounds__(TT, 1) tiny_graph_kernel(const OpNode* __restrict__ nodes, int n_nodes) {
     extern __shared__ float sm[];
     Th t;
-    t.rank = (int)ptx::cluster_ctarank();
+    t.rank = NC > 1 ? (int)ptx::cluster_ctarank() : 0;
+    t.C = NC;
     t.tid = threadIdx.x;
     t.g = t.rank * TT + t.tid;
-    t.G = TC * TT;
+    t.G = NC * TT;
     for (int i = 0; i < n_nodes; i++) {
         run_node(nodes[i], t, sm);
-        ptx::cluster_sync();   // release / acquire at cluster scope: node i's writes before node i+1
+        if (NC > 1) ptx::cluster_sync();   // release / acquire at cluster scope: node i's writes before node i+1
+        else __syncthreads();              // CTA scope
     }
+}
+
+// RT_TINY_CTAS=8 runs the cluster form; one CTA by default (measured faster
+// on the toy: a CTA barrier and L1-resident operands against a cluster
+// barrier per node).
+int tiny_ctas() {
+    static const int v = [] {
+        const char* e = getenv("RT_TINY_CTAS");
+        return e && atoi(e) == TC ? TC : 1;
+    }();
+    return v;
 }
 
 int64_t numel_h(const OpNode& n) { return total_elements(n); }
@@ -454,7 +473,9 @@ Status tiny_graph_build(const std::vector<OpNode>& nodes, TinyPlan* out) {
     RT_CUDA_CHECK(cudaMalloc(&t.dev_nodes, bytes));
     cudaError_t e = cudaMemcpy(t.dev_nodes, nodes.data(), bytes, cudaMemcpyHostToDevice);
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(tiny_graph_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TSMEM);
+        e = cudaFuncSetAttribute(tiny_graph_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, TSMEM);
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(tiny_graph_kernel<TC>, cudaFuncAttributeMaxDynamicSharedMemorySize, TSMEM);
     if (e != cudaSuccess) {
         cudaGetLastError();
         cudaFree(t.dev_nodes);
@@ -466,7 +487,23 @@ Status tiny_graph_build(const std::vector<OpNode>& nodes, TinyPlan* out) {
 }
 
 Status launch_tiny(const TinyPlan& t, cudaStream_t st, int* launches) {
-    tiny_graph_kernel<<<TC, TT, TSMEM, st>>>(t.dev_nodes, t.n);
+    if (tiny_ctas() == 1) {
+        tiny_graph_kernel<1><<<1, TT, TSMEM, st>>>(t.dev_nodes, t.n);
+    } else {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(TC);
+        cfg.blockDim = dim3(TT);
+        cfg.dynamicSmemBytes = TSMEM;
+        cfg.stream = st;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = TC;
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        RT_CUDA_CHECK(cudaLaunchKernelEx(&cfg, tiny_graph_kernel<TC>, (const OpNode*)t.dev_nodes, t.n));
+    }
     RT_LAUNCH_CHECK();
     *launches += 1;
     return Status::ok();
