@@ -178,7 +178,8 @@ int rt_unprotect_all(void);
  * the fused kernel), 6 for a gated activation reading its inputs through
  * strided views of the tensor its folded SLICEs took them from, 8 for a
  * LAYERNORM / RMSNORM writing the split A operand of the GEMM reading it
- * (that GEMM: 4), 0 otherwise.  Returns the number of folded nodes.  Host only: needs no
+ * (that GEMM: 4), 7 for a GEMM whose epilogue applies a folded gated
+ * activation (SLICE, SLICE, GATED_ACT of its output: 1 each), 0 otherwise.  Returns the number of folded nodes.  Host only: needs no
  * device and no rt_init.  RT_FUSE=0 turns all fusion off. */
 int rt_fusion_report(const OpNode* nodes, int n_nodes, int* flags);
 

@@ -22,6 +22,7 @@
 #include <stdio.h>
 #include <stdlib.h>
 
+#include <algorithm>
 #include <vector>
 
 #include "gemm.h"
@@ -669,6 +670,82 @@ void plan_rope_folds(const std::vector<OpNode>& nodes, const std::vector<Range>&
 }
 
 
+// Gated GEMM fold: MATMUL G = A . W^T (W a constant [2N, K] weight, alpha 1)
+// -> SLICE x = G[..., :N] -> SLICE up = G[..., N:] -> GATED_ACT(x, up) (no
+// bias).  The GEMM takes W's rows in the gated order (per 256-row tile: 64
+// gate rows, their 64 up rows, the next 64 gate rows, their up rows) so that
+// each epilogue thread holds matching gate and up columns, applies the
+// activation and writes the GATED_ACT's output directly (N columns); the
+// slices and the GATED_ACT are not launched.  Conditions: G and the slices'
+// outputs are read by nobody else (and are not graph outputs), the GATED_ACT
+// output overlaps none of the GEMM's operands, and no node between the GEMM
+// and the GATED_ACT touches that output (the GEMM now writes it earlier).
+// The GATED_ACT arithmetic is the same fp32 function of the same fp32 values.
+void plan_gated_gemm_folds(const std::vector<OpNode>& nodes, const std::vector<Range>& protect,
+                           std::vector<PlanItem>& items, std::vector<bool>& gone) {
+    static const bool on = [] {
+        const char* v = getenv("RT_FUSE_GATED_GEMM");
+        const char* bn = getenv("RT_GEMM_BN");
+        return !(v && v[0] == '0') && !(bn && atoi(bn) == 128);   // the gated order assumes 256-wide N tiles
+    }();
+    if (!on) return;
+    Analysis an(nodes, &gone);
+    const int n = (int)nodes.size();
+    for (int g = 0; g < n; g++) {
+        const OpNode& ga = nodes[g];
+        if (gone[g] || ga.op != RT_OP_GATED_ACT || ga.elem_size != 4 || ga.extra[0] != 0 ||
+            (ga.extra[1] != 0 && ga.extra[1] != 1))
+            continue;
+        const int64_t N = last_dim(ga), rows = N ? total_elements(ga) / N : 0;
+        if (N % 128 != 0 || rows == 0) continue;
+        const size_t half_bytes = (size_t)(rows * N) * 4;
+        const int sx = an.last_writer(rng(ga.inputs[0], half_bytes), g);
+        const int su = an.last_writer(rng(ga.inputs[1], half_bytes), g);
+        if (sx < 0 || su < 0 || sx == su || gone[sx] || gone[su]) continue;
+        const OpNode& X = nodes[sx];
+        const OpNode& U = nodes[su];
+        auto is_half = [&](const OpNode& s, int64_t start, const void* out) {
+            return s.op == RT_OP_SLICE && s.elem_size == 4 && s.output == out && s.extra[0] == rows &&
+                   s.extra[1] == 2 * N && s.extra[2] == start && s.extra[3] == N && s.extra[4] == 1;
+        };
+        if (!is_half(X, 0, ga.inputs[0]) || !is_half(U, N, ga.inputs[1]) || X.inputs[0] != U.inputs[0]) continue;
+        const void* G = X.inputs[0];
+        const Range GR = rng(G, (size_t)(rows * 2 * N) * 4);
+        const int m = an.last_writer(GR, std::min(sx, su));
+        if (m < 0 || gone[m]) continue;
+        const OpNode& gm = nodes[m];
+        GemmProblem p;
+        if (gm.op != RT_OP_MATMUL || gm.output != G || gm.extra[3] != 0 || !decode_gemm(gm, &p).good() ||
+            !p.trans_b || p.batches * p.M != rows || p.N != 2 * N || !gemm_fusable(gm) ||
+            !is_constant_range(p.b, (size_t)(p.N * p.K) * 4) || items[m].views || items[m].epi_out)
+            continue;
+        // G read only by the two slices; their outputs only by the GATED_ACT
+        bool ok = true;
+        for (int j = m + 1; j < n && ok; j++) {
+            if (j == sx || j == su) continue;
+            for (const Range& r : an.reads[j]) ok &= !overlaps(r, GR);
+            if (overlaps(an.writes[j], GR)) break;   // recycled
+        }
+        for (const Range& pr : protect) ok &= !overlaps(pr, GR);
+        ok = ok && dead_output(an, sx, g, protect) && dead_output(an, su, g, protect);
+        const Range O = an.writes[g];
+        for (const Range& r : an.reads[m]) ok &= !overlaps(r, O);
+        for (int j = m + 1; j < g && ok; j++) {
+            if (j == sx || j == su || gone[j]) continue;
+            ok &= !overlaps(an.writes[j], O);
+            for (const Range& r : an.reads[j]) ok &= !overlaps(r, O);
+        }
+        if (!ok) continue;
+        items[m].epi_gate = 1 + ga.extra[1];
+        items[m].epi_out = ga.output;
+        for (int k : {sx, su, g}) {
+            items[k].skip = true;
+            gone[k] = true;
+        }
+        if (dbg()) fprintf(stderr, "[fusion] gemm %d applies GATED_ACT %d in its epilogue (slices %d, %d)\n", m, g, sx, su);
+    }
+}
+
 // Gated-MLP fold: GATED_ACT whose x and/or up input is a last-dim SLICE of a
 // wider tensor (Qwen3: the merged gate/up projection) reads that tensor through
 // a row-strided view; the SLICE is not launched.  Conditions as for the
@@ -1029,6 +1106,7 @@ std::vector<PlanItem> plan_fusions(const std::vector<OpNode>& nodes,
     if (fusion_enabled()) {
         plan_bias_folds(nodes, protect, items, gone, bias_plan ? bias_plan : &local_bp);
         plan_rope_folds(nodes, protect, items, gone, reads_of);
+        plan_gated_gemm_folds(nodes, protect, items, gone);
         plan_gated_folds(nodes, protect, items, gone, reads_of);
     }
     Analysis an(nodes, &gone, &reads_of);

@@ -23,7 +23,7 @@ Status launch_simt_gemm(const GemmProblem& p, cudaStream_t st);
 // tcgen05 3xTF32 path (k_gemm_tc.cu)
 bool tc_gemm_applicable(const GemmProblem& p);
 size_t tc_gemm_workspace_bytes(const GemmProblem& p);
-Status tc_gemm_prepare(const GemmProblem& p, cudaStream_t st);
+Status tc_gemm_prepare(const GemmProblem& p, cudaStream_t st, int gate = 0);
 Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* launches,
                       const GemmFusion* f = nullptr);
 

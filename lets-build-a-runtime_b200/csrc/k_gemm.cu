@@ -155,11 +155,11 @@ size_t gemm_workspace_bytes(const OpNode& n) {
     return tc_gemm_workspace_bytes(p);
 }
 
-Status prepare_gemm(const OpNode& n, cudaStream_t st) {
+Status prepare_gemm(const OpNode& n, cudaStream_t st, int gate) {
     GemmProblem p;
     Status s = decode_gemm(n, &p);
     if (!s.good()) return s;
-    return tc_gemm_prepare(p, st);
+    return tc_gemm_prepare(p, st, gate);
 }
 
 bool gemm_fusable(const OpNode& n) {

@@ -110,6 +110,8 @@ struct TcParams {
     int splits, kb_split;         // split-K: work item = (tile, split); split s covers K blocks [s*kb_split, ...)
     int total_items;              // total_tiles * splits
     int act;                      // 1: tanh-GELU after alpha and bias
+    int gate;                     // 1 / 2: gated output (B rows in the gated order): C[r][j] = act(g) * u,
+                                  //   act SiLU / tanh-GELU, C has N / 2 columns
     const float* a_scale;         // fp16 scheme: 2^-e per A row ([batches*M]); null = 1
     const float* b_scale;         // fp16 scheme: 2^-e of the whole B operand (one float); null = 1
     float* plane_hi;              // non-null: write the result as split A planes (hi, plane 1) of a
@@ -199,6 +201,29 @@ __device__ __forceinline__ void store_row(const TcParams& p, int64_t row, int bz
             } else {
                 *reinterpret_cast<float4*>(reinterpret_cast<float*>(xrow) + col) =
                     make_float4(l[0], l[1], l[2], l[3]);
+            }
+        }
+        return;
+    }
+    if (!PLANES && p.gate) {
+        // this thread's COLS columns: COLS/2 gate values, then their COLS/2 up values
+        constexpr int H = COLS / 2;
+        const int64_t ldc = p.N / 2, c0 = col0 / 2;
+        float* orow = p.c + r * ldc + c0;
+#pragma unroll
+        for (int j = 0; j < H; j += 4) {
+            float o[4];
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const float g = acc[j + e], u = acc[H + j + e];
+                o[e] = (p.gate == 1 ? silu(g) : gelu_tanh(g)) * u;
+            }
+            if (p.vec_c && c0 + j + 4 <= ldc) {
+                *reinterpret_cast<float4*>(orow + j) = make_float4(o[0], o[1], o[2], o[3]);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 4; e++)
+                    if (c0 + j + e < ldc) orow[j + e] = o[e];
             }
         }
         return;
@@ -1109,8 +1134,22 @@ bool split_k_enabled() {
 
 int a_mode() { return cross_scheme() ? 1 : 0; }
 int b_mode() { return cross_scheme() ? 2 : 0; }
-SplitKey b_key(const GemmProblem& p) {
-    return SplitKey{p.b, p.batches, p.N, p.K, (p.trans_b ? 0 : 1) | (scheme() << 1)};
+SplitKey b_key(const GemmProblem& p, int gate = 0) {
+    return SplitKey{p.b, p.batches, p.N, p.K, (p.trans_b ? 0 : 1) | (scheme() << 1) | (gate ? 8 : 0)};
+}
+
+// B rows ([N][K], N % 256 == 0) in the gated order read by a gated epilogue:
+// per 256-row tile t and half h, 64 gate rows t*128 + h*64 + w (w < 64), then
+// their up rows N/2 + t*128 + h*64 + w.
+__global__ void gate_order_rows_kernel(const float* __restrict__ src, float* __restrict__ dst, int64_t N,
+                                       int64_t K) {
+    const int64_t Nh = N / 2;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < N * K; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t q = i / K, k = i - q * K;
+        const int64_t t = q / 256, h = (q % 256) / 128, w = q % 128;
+        const int64_t row = (w < 64 ? 0 : Nh) + t * 128 + h * 64 + (w & 63);
+        dst[i] = src[row * K + k];
+    }
 }
 
 // Every kernel instantiation with its dynamic shared memory size.
@@ -1244,7 +1283,7 @@ size_t tc_gemm_workspace_bytes(const GemmProblem& p) {
     return b;
 }
 
-Status tc_gemm_prepare(const GemmProblem& p, cudaStream_t st) {
+Status tc_gemm_prepare(const GemmProblem& p, cudaStream_t st, int gate) {
     if (!tc_gemm_applicable(p)) return Status::ok();
     static bool attr_set = false;
     if (!attr_set) {
@@ -1254,19 +1293,37 @@ Status tc_gemm_prepare(const GemmProblem& p, cudaStream_t st) {
         attr_set = true;
         pair_clusters();   // occupancy query outside any stream capture
     }
-    if (!b_is_constant(p)) return Status::ok();
-    SplitKey key = b_key(p);
-    if (find_constant_split(key)) return Status::ok();
-    SplitOperand s;
-    if (scheme() == SCH_F16) {
-        Status r = create_constant_split(key, plane_bytes(p.batches, p.N, p.K) / 4, B_SCALARS / 4, &s);
-        if (!r.good()) return r;
-        return run_split16_tensor(p.b, reinterpret_cast<uint16_t*>(s.hi), s.lo, p.batches, p.N, p.K, !p.trans_b, st);
+    if (!b_is_constant(p)) {
+        if (gate) return Status::err(RT_ERR_ARGUMENT, "gemm: a gated epilogue needs a constant B");
+        return Status::ok();
     }
-    const size_t elems = (size_t)p.batches * p.N * p.K;
-    Status r = create_constant_split(key, elems, elems, &s);
-    if (!r.good()) return r;
-    return run_split(p.b, s.hi, s.lo, p.batches, p.N, p.K, !p.trans_b, b_mode(), st);
+    SplitKey key = b_key(p, gate);
+    if (find_constant_split(key)) return Status::ok();
+    const float* src = p.b;
+    float* tmp = nullptr;
+    if (gate) {   // B in the gated row order, split once like any constant B
+        if (!p.trans_b || p.batches != 1 || p.N % 256 != 0)
+            return Status::err(RT_ERR_ARGUMENT, "gemm: a gated epilogue needs B [N][K], N % 256 == 0");
+        RT_CUDA_CHECK(cudaMalloc(&tmp, (size_t)p.N * p.K * 4));
+        gate_order_rows_kernel<<<grid_for(p.N * p.K, 256), 256, 0, st>>>(p.b, tmp, p.N, p.K);
+        src = tmp;
+    }
+    SplitOperand s;
+    Status r;
+    if (scheme() == SCH_F16) {
+        r = create_constant_split(key, plane_bytes(p.batches, p.N, p.K) / 4, B_SCALARS / 4, &s);
+        if (r.good())
+            r = run_split16_tensor(src, reinterpret_cast<uint16_t*>(s.hi), s.lo, p.batches, p.N, p.K, !p.trans_b, st);
+    } else {
+        const size_t elems = (size_t)p.batches * p.N * p.K;
+        r = create_constant_split(key, elems, elems, &s);
+        if (r.good()) r = run_split(src, s.hi, s.lo, p.batches, p.N, p.K, !p.trans_b, b_mode(), st);
+    }
+    if (tmp) {
+        if (cudaStreamSynchronize(st) != cudaSuccess && r.good()) r = Status::err(RT_ERR_CUDA, "gemm: gated B order");
+        cudaFree(tmp);
+    }
+    return r;
 }
 
 Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* launches,
@@ -1301,8 +1358,11 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
         a_lo = al;
     }
     if (f16) a_scale = static_cast<const float*>(a_lo);
+    const int gate = f ? f->gate : 0;
+    if (gate && (!b_is_constant(p) || p.N % 256 != 0))
+        return Status::err(RT_ERR_ARGUMENT, "gemm: a gated epilogue needs a constant B with N % 256 == 0");
     if (b_is_constant(p)) {
-        const SplitOperand* so = find_constant_split(b_key(p));
+        const SplitOperand* so = find_constant_split(b_key(p, gate));
         if (!so) return Status::err(RT_ERR_ARGUMENT, "gemm: constant operand not prepared");
         b_hi = so->hi;
         b_lo = so->lo;
@@ -1329,6 +1389,7 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
         return e ? atoi(e) : 0;
     }();
     const int BN = bn_force == 128 ? 128 : 256;
+    if (gate && BN != 256) return Status::err(RT_ERR_ARGUMENT, "gemm: a gated epilogue needs 256-wide N tiles");
     // CTA pairs (256x256 tiles) whenever A has more than one 128-row block.
     const bool pair = BN == 256 && p.M > BM && pair_enabled();
     const int b_box = pair ? 128 : BN;
@@ -1353,9 +1414,12 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
     prm.alpha = p.alpha;
     // Planner offsets are raw byte counts (first fit), so C, a bias or a
     // residual may sit off a 16-byte boundary: those rows take scalar accesses.
-    prm.vec_c = p.N % 4 == 0 && aligned16(prm.c) && (!prm.bias || aligned16(prm.bias)) &&
+    prm.vec_c = (gate ? p.N / 2 : p.N) % 4 == 0 && aligned16(prm.c) && (!prm.bias || aligned16(prm.bias)) &&
                 (!prm.res || aligned16(prm.res));
     prm.act = f ? f->act : 0;
+    prm.gate = gate;
+    if (gate && (prm.bias || prm.res || prm.alpha != 1.0f || prm.act || (f && f->plane_hi)))
+        return Status::err(RT_ERR_ARGUMENT, "gemm: a gated epilogue takes no bias, residual, alpha or other activation");
     prm.plane_hi = f ? f->plane_hi : nullptr;
     prm.plane_x = f ? static_cast<uint8_t*>(f->plane_x) : nullptr;
     prm.plane_mode = a_mode();
@@ -1391,7 +1455,7 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
             res_in_c = true;
         }
     }
-    const bool whole_sum = prm.act != 0 || prm.plane_hi != nullptr || res_in_c;
+    const bool whole_sum = prm.act != 0 || prm.gate != 0 || prm.plane_hi != nullptr || res_in_c;
     if (total < (int64_t)workers * 3 / 2 && prm.n_chunks >= 2 && split_k_enabled() && !whole_sum) {
         prm.splits = 2;
         RT_CUDA_CHECK(cudaMemsetAsync(prm.c, 0, (size_t)p.batches * p.M * p.N * 4, st));
@@ -1409,7 +1473,7 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
         return e && e[0] == '1';
     }();
     prm.c_tma = 0;
-    if (c_tma_on && pair && prm.splits == 1 && !prm.plane_hi && !prm.res && prm.vec_c) {
+    if (c_tma_on && pair && prm.splits == 1 && !prm.plane_hi && !prm.res && !prm.gate && prm.vec_c) {
         if (!(s = encode_tmap_f32_3d(&prm.tc, prm.c, p.N, p.M, p.batches, 32, 32, 128)).good()) return s;
         prm.c_tma = 1;
     }

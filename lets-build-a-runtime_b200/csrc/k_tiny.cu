@@ -7,8 +7,8 @@
 // TC CTAs that walks the node array on the device, node after node, with a
 // cluster barrier (barrier.cluster release / acquire: every global write of a
 // node is visible to the whole cluster before the next node starts) between
-// nodes.  Each node's work is spread over the cluster's threads.  By default
-// the "cluster" is a single CTA (RT_TINY_CTAS=8 selects eight).
+// nodes.  Each node's work is spread over the cluster's threads
+// (RT_TINY_CTAS=1: a single CTA instead).
 //
 // Semantics are the reference's dispatch (csrc/executor.c:54-397), node for
 // node, on the same OpNode array the other kernels run:
@@ -398,13 +398,14 @@ __global__ void __launch_bounds__(TT, 1) tiny_graph_kernel(const OpNode* __restr
     }
 }
 
-// RT_TINY_CTAS=8 runs the cluster form; one CTA by default (measured faster
-// on the toy: a CTA barrier and L1-resident operands against a cluster
-// barrier per node).
+// The cluster of TC CTAs by default; RT_TINY_CTAS=1 runs one CTA with CTA
+// barriers.  Measured on the toy block: 88 us per forward with 8 CTAs, 162 us
+// with one (the GEMM and attention nodes need the extra SMs; every node
+// costs ~2 us either way, its L2 round trips and the barrier).
 int tiny_ctas() {
     static const int v = [] {
         const char* e = getenv("RT_TINY_CTAS");
-        return e && atoi(e) == TC ? TC : 1;
+        return e && atoi(e) == 1 ? 1 : TC;
     }();
     return v;
 }

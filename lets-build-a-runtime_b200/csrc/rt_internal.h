@@ -87,6 +87,8 @@ struct GemmFusion {
     const void* pre_x = nullptr;
     const float* bias = nullptr;    // bias to add (a node without one: a folded bias)
     const float* res = nullptr;     // residual added after the bias (same layout as C): a folded ADD
+    int gate = 0;                   // 1 / 2: a folded GATED_ACT (SiLU / tanh-GELU): B's rows are taken in
+                                    // the gated order and `out` receives act(gate) * up, N / 2 columns
 };
 Status launch_gemm(const OpNode& n, cudaStream_t st, Workspace ws, int* launches,
                    const GemmFusion* f = nullptr);
@@ -100,7 +102,8 @@ bool norm_planes_supported(const OpNode& n);
 // 0/1 the hi plane at `hi` and plane 1 at `x1`; for the fp16 scheme (2) the
 // fp16 plane at `hi` and the per-row 2^-e scales at `x1`.
 Status launch_norm_planes(const OpNode& n, float* hi, void* x1, int scheme, cudaStream_t st, int* launches);
-Status prepare_gemm(const OpNode& n, cudaStream_t st);   // constant splits, before capture
+// constant splits, before capture (gate: the node's B in the gated row order, see GemmFusion)
+Status prepare_gemm(const OpNode& n, cudaStream_t st, int gate = 0);
 
 Status launch_attention(const OpNode& n, cudaStream_t st, Workspace ws, int* launches);
 
@@ -183,6 +186,7 @@ struct PlanItem {
     const void* epi_res = nullptr; // GEMM adds this residual (a folded same-shape ADD) and writes epi_out
     bool rope = false;             // this (ADD) node launches the fused norm + rotary kernel instead
     RopeFold rp{};
+    int epi_gate = 0;              // GEMM: a folded GATED_ACT, 1 + its act (see GemmFusion::gate); writes epi_out
     bool gated = false;            // this GATED_ACT reads its inputs through `gv`
     GatedViews gv{};
 };

@@ -331,9 +331,11 @@ Status launch_item(Plan& p, size_t i, cudaStream_t st, int* launches) {
             return launch_attention_views(p.nodes[i], v, st, ws, launches);
         }
         const PlanItem& it = p.items[i];
-        if (it.epi_act || it.epi_out || it.carry_off >= 0 || it.presplit_off >= 0 || it.epi_bias_off >= 0) {
+        if (it.epi_act || it.epi_out || it.carry_off >= 0 || it.presplit_off >= 0 || it.epi_bias_off >= 0 ||
+            it.epi_gate) {
             GemmFusion f;
             f.act = it.epi_act;
+            f.gate = it.epi_gate;
             if (it.epi_bias_off >= 0) f.bias = reinterpret_cast<const float*>(p.bias + it.epi_bias_off);
             f.out = static_cast<float*>(it.epi_out);
             f.res = static_cast<const float*>(it.epi_res);
@@ -449,7 +451,9 @@ Status build_plan(const OpNode* nodes, int n, bool capture, Plan** out) {
     cudaStream_t st = S().stream;
     for (int i = 0; i < n; i++) {
         if (family_of(nodes[i].op) == F_GEMM || family_of(nodes[i].op) == F_ATTN) {
-            Status s = family_of(nodes[i].op) == F_GEMM ? prepare_gemm(nodes[i], st) : prepare_attention(nodes[i]);
+            Status s = family_of(nodes[i].op) == F_GEMM
+                           ? prepare_gemm(nodes[i], st, i < (int)plan->items.size() ? plan->items[i].epi_gate : 0)
+                           : prepare_attention(nodes[i]);
             if (!s.good()) {
                 free_plan(*plan);
                 return s;
@@ -1036,6 +1040,7 @@ int rt_fusion_report(const OpNode* nodes, int n, int* skipped) {
                 : it.rope ? 5
                 : it.gated ? 6
                 : it.norm_planes_off >= 0 ? 8
+                : it.epi_gate ? 7
                 : (it.epi_act || it.epi_out || it.carry_off >= 0 || it.epi_bias_off >= 0) ? 3
                 : it.presplit_off >= 0 ? 4
                                         : 0;

@@ -221,3 +221,35 @@ def test_residual_add_folded_into_gemm_matches_oracle(M, K, N, inplace, gpu_exec
         got = ex.run({})["z"]
         np.testing.assert_allclose(got, ref, atol=1e-4, rtol=1e-3)
     assert flags_of(ex, prog) == [0, 3, 1]
+
+
+@pytest.mark.parametrize("name", ["qwen3_mini_s272"])
+def test_gated_activation_folds_into_the_gate_up_gemm(name, gpu_executor_factory, monkeypatch):
+    """Qwen3's MLP: merged gate/up MATMUL -> SLICE, SLICE -> GATED_ACT(SiLU).
+    The GEMM takes the weight rows in the gated order and applies the
+    activation in its epilogue (flag 7); slices and GATED_ACT are not
+    launched (flag 1).  Output against the reference executor's golden, and
+    against the unfused plan (RT_FUSE_GATED_GEMM=0, read once per process: a
+    fresh process)."""
+    from conftest import load_golden
+    from test_gpu_programs import assert_parity
+    prog, ins, outs = load_golden(name)
+    ex = gpu_executor_factory(prog, prog.make_constants())
+    got = ex.run(ins)
+    flags = flags_of(ex, prog)
+    ops = [nd.op for nd in prog.nodes]
+    gated = [i for i, op in enumerate(ops) if op == OP["GATED_ACT"]]
+    assert gated and all(flags[i] == 1 for i in gated)
+    assert flags.count(7) == len(gated)
+    for k, ref in outs.items():
+        assert_parity(got[k], ref, f"{name}:{k} (gated epilogue)")
+
+
+def test_gated_gemm_fold_off_matches():
+    import os
+    import subprocess
+    import sys
+    r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", "-m", "gpu", "-p", "no:cacheprovider",
+                        os.path.join(os.path.dirname(__file__), "test_gpu_programs.py"), "-k", "qwen3_mini"],
+                       env=dict(os.environ, RT_FUSE_GATED_GEMM="0"), capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and " passed" in r.stdout, r.stdout[-3000:] + r.stderr[-2000:]
