@@ -678,7 +678,9 @@ void plan_rope_folds(const std::vector<OpNode>& nodes, const std::vector<Range>&
 // activation and writes the GATED_ACT's output directly (N columns); the
 // slices and the GATED_ACT are not launched.  Conditions: G and the slices'
 // outputs are read by nobody else (and are not graph outputs), the GATED_ACT
-// output overlaps none of the GEMM's operands, and no node between the GEMM
+// output overlaps none of the GEMM's operands but A (which the tensor-core GEMM
+// reads only through its split planes, written before it starts), and no node
+// between the GEMM
 // and the GATED_ACT touches that output (the GEMM now writes it earlier).
 // The GATED_ACT arithmetic is the same fp32 function of the same fp32 values.
 void plan_gated_gemm_folds(const std::vector<OpNode>& nodes, const std::vector<Range>& protect,
@@ -701,41 +703,65 @@ void plan_gated_gemm_folds(const std::vector<OpNode>& nodes, const std::vector<R
         const size_t half_bytes = (size_t)(rows * N) * 4;
         const int sx = an.last_writer(rng(ga.inputs[0], half_bytes), g);
         const int su = an.last_writer(rng(ga.inputs[1], half_bytes), g);
-        if (sx < 0 || su < 0 || sx == su || gone[sx] || gone[su]) continue;
+        auto why = [&](const char* m) {
+            if (dbg()) fprintf(stderr, "[fusion] gated GEMM fold at %d: %s\n", g, m);
+        };
+        if (sx < 0 || su < 0 || sx == su || gone[sx] || gone[su]) { why("inputs not written by two slices"); continue; }
         const OpNode& X = nodes[sx];
         const OpNode& U = nodes[su];
         auto is_half = [&](const OpNode& s, int64_t start, const void* out) {
             return s.op == RT_OP_SLICE && s.elem_size == 4 && s.output == out && s.extra[0] == rows &&
                    s.extra[1] == 2 * N && s.extra[2] == start && s.extra[3] == N && s.extra[4] == 1;
         };
-        if (!is_half(X, 0, ga.inputs[0]) || !is_half(U, N, ga.inputs[1]) || X.inputs[0] != U.inputs[0]) continue;
+        if (!is_half(X, 0, ga.inputs[0]) || !is_half(U, N, ga.inputs[1]) || X.inputs[0] != U.inputs[0]) {
+            why("not the two halves of one tensor");
+            continue;
+        }
         const void* G = X.inputs[0];
         const Range GR = rng(G, (size_t)(rows * 2 * N) * 4);
         const int m = an.last_writer(GR, std::min(sx, su));
-        if (m < 0 || gone[m]) continue;
+        if (m < 0 || gone[m]) { why("no producer of the sliced tensor"); continue; }
         const OpNode& gm = nodes[m];
         GemmProblem p;
         if (gm.op != RT_OP_MATMUL || gm.output != G || gm.extra[3] != 0 || !decode_gemm(gm, &p).good() ||
-            !p.trans_b || p.batches * p.M != rows || p.N != 2 * N || !gemm_fusable(gm) ||
-            !is_constant_range(p.b, (size_t)(p.N * p.K) * 4) || items[m].views || items[m].epi_out)
+            !p.trans_b || p.batches * p.M != rows || p.N != 2 * N || !gemm_fusable(gm) || items[m].views ||
+            items[m].epi_out) {
+            why("producer is not a plain MATMUL of the right shape");
             continue;
-        // G read only by the two slices; their outputs only by the GATED_ACT
+        }
+        // G read only by the two slices (a read of x before node j sees G's
+        // contents if, walking back, m writes the overlap before any node
+        // covering x does); their outputs only by the GATED_ACT
+        auto covers = [](Range w, Range x) { return w.lo <= x.lo && x.hi <= w.hi; };
+        auto sees_g = [&](Range x, int before) {
+            if (!overlaps(x, GR)) return false;
+            for (int i = before - 1; i >= m; i--) {
+                if (!overlaps(an.writes[i], x)) continue;
+                if (i == m) return true;
+                if (covers(an.writes[i], x)) return false;
+            }
+            return false;
+        };
         bool ok = true;
         for (int j = m + 1; j < n && ok; j++) {
             if (j == sx || j == su) continue;
-            for (const Range& r : an.reads[j]) ok &= !overlaps(r, GR);
-            if (overlaps(an.writes[j], GR)) break;   // recycled
+            for (const Range& r : an.reads[j]) ok &= !sees_g(r, j);
+            if (!ok) why(("G read by node " + std::to_string(j)).c_str());
         }
-        for (const Range& pr : protect) ok &= !overlaps(pr, GR);
-        ok = ok && dead_output(an, sx, g, protect) && dead_output(an, su, g, protect);
+        for (const Range& pr : protect) ok &= !sees_g(pr, n);
+        if (!ok) { why("G read elsewhere or a graph output"); continue; }
+        if (!dead_output(an, sx, g, protect) || !dead_output(an, su, g, protect)) { why("a slice output is read elsewhere"); continue; }
         const Range O = an.writes[g];
-        for (const Range& r : an.reads[m]) ok &= !overlaps(r, O);
+        // A may overlap O: the tensor-core GEMM reads A only through its split
+        // planes, written by a pre-pass (or a norm's hand-off) before it starts
+        for (size_t i = 1; i < an.reads[m].size(); i++) ok &= !overlaps(an.reads[m][i], O);
         for (int j = m + 1; j < g && ok; j++) {
             if (j == sx || j == su || gone[j]) continue;
             ok &= !overlaps(an.writes[j], O);
             for (const Range& r : an.reads[j]) ok &= !overlaps(r, O);
         }
-        if (!ok) continue;
+        if (!ok) { why("a buffer is read elsewhere or overlaps"); continue; }
+        if (!is_constant_range(p.b, (size_t)(p.N * p.K) * 4)) { why("weight is not a marked constant"); continue; }
         items[m].epi_gate = 1 + ga.extra[1];
         items[m].epi_out = ga.output;
         for (int k : {sx, su, g}) {
@@ -1105,8 +1131,8 @@ std::vector<PlanItem> plan_fusions(const std::vector<OpNode>& nodes,
     std::vector<std::pair<int, std::vector<Range>>> reads_of;
     if (fusion_enabled()) {
         plan_bias_folds(nodes, protect, items, gone, bias_plan ? bias_plan : &local_bp);
+        plan_gated_gemm_folds(nodes, protect, items, gone);   // before the rotary folds: it sees every node
         plan_rope_folds(nodes, protect, items, gone, reads_of);
-        plan_gated_gemm_folds(nodes, protect, items, gone);
         plan_gated_folds(nodes, protect, items, gone, reads_of);
     }
     Analysis an(nodes, &gone, &reads_of);
