@@ -764,10 +764,15 @@ void plan_gated_gemm_folds(const std::vector<OpNode>& nodes, const std::vector<R
         if (!is_constant_range(p.b, (size_t)(p.N * p.K) * 4)) { why("weight is not a marked constant"); continue; }
         items[m].epi_gate = 1 + ga.extra[1];
         items[m].epi_out = ga.output;
-        for (int k : {sx, su, g}) {
+        // The slices vanish from later analyses; the GATED_ACT is not launched
+        // but stays in them as the writer of its output (the GEMM now writes
+        // it, earlier), so their dead / recycled reasoning about that region
+        // holds.
+        for (int k : {sx, su}) {
             items[k].skip = true;
             gone[k] = true;
         }
+        items[g].skip = true;
         if (dbg()) fprintf(stderr, "[fusion] gemm %d applies GATED_ACT %d in its epilogue (slices %d, %d)\n", m, g, sx, su);
     }
 }
