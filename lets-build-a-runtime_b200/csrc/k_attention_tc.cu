@@ -46,6 +46,7 @@
 
 #include <algorithm>
 
+#include "dev_math.h"
 #include "gemm.h"
 #include "sm100_ptx.h"
 
@@ -68,20 +69,30 @@ static_assert(128 * REG_CTRL + 32 * SOFT_WARPS * REG_SOFT <= ATHREADS * 168, "re
 constexpr int CHUNK = 32 * 1024;                      // ring stage / packed chunk
 constexpr uint64_t WAIT_NS = 2000000000ull;
 constexpr int ERR_A_PROD = 0x201, ERR_A_MMA = 0x202, ERR_A_SOFT = 0x203, ERR_A_DRAIN = 0x204;
-constexpr uint32_t COL_S = 0, COL_PH = 128, COL_PL = 256, COL_O = 384;
+constexpr uint32_t COL_S = 0, COL_PH = 128, COL_PL = 256, COL_O = 384;   // fp16 mode: P (h | l) at COL_PH
+// Operand modes: three tf32 MMAs, tf32 + bf16 cross terms, or scaled fp16
+// hi / lo (three kind::f16 MMAs, one plane per operand: see below).
+constexpr int AM_3XTF32 = 0, AM_CROSS = 1, AM_F16 = 2;
 constexpr int FOLD_EVERY = 3;              // P.V tiles accumulated in TMEM between register folds
 constexpr float RESCALE_LOG2 = 8.0f;       // a row keeps its reference max until a tile max exceeds it by this
 
-template <int D>
+// Tiles: tf32 modes -- Q hi and plane 1 (two Q_BYTES), K chunks of 32
+// features x 128 keys (hi | plane 1), V^T chunks of D x V_KEYS keys (hi |
+// plane 1); fp16 mode -- one Q plane, K chunks of 64 features x 128 keys,
+// V^T chunks of D x 64 (D = 128) or D x 128 (D = 64) keys, each a 128-byte
+// swizzled row per 32 elements of K holding [h | l] / [l | h] per 16.
+template <int D, bool F16 = false>
 struct AttnTcCfg {
-    static constexpr int Q_BYTES = D * BQ * 4;                  // one of Q_hi / Q_lo: D/32 x [128][128 B]
-    static constexpr int K_CHUNKS = D / 32;                     // 32 features x 128 keys, hi | lo
-    static constexpr int V_KEYS = D == 128 ? 32 : 64;           // keys per V chunk (D x keys, hi | lo)
+    static constexpr int Q_BYTES = D * BQ * 4;                  // one Q plane: D/32 x [128][128 B]
+    static constexpr int Q_PLANES = F16 ? 1 : 2;
+    static constexpr int K_CHUNKS = F16 ? D / 64 : D / 32;
+    static constexpr int V_KEYS = F16 ? (D == 128 ? 64 : 128) : (D == 128 ? 32 : 64);   // keys per V chunk
     static constexpr int V_CHUNKS = BKV / V_KEYS;
     static constexpr int TILE_BYTES = (K_CHUNKS + V_CHUNKS) * CHUNK;
-    static constexpr int STAGES = D == 128 ? RT_ATTN_RING128 : 5;
+    static constexpr int STAGES = F16 ? (D == 128 ? 4 : 5) : (D == 128 ? RT_ATTN_RING128 : 5);
     static constexpr int BAR_BYTES = 384;                       // mbarriers, TMEM slot, flags, item ring
-    static constexpr int BODY = 2 * Q_BYTES + STAGES * CHUNK + BAR_BYTES + 4 * BQ * 4 /*row exchange*/;
+    static constexpr int BODY = Q_PLANES * Q_BYTES + STAGES * CHUNK + BAR_BYTES +
+                                (F16 ? 6 : 4) * BQ * 4 /*row exchange: maxima / sums (+ Q maxima)*/;
     static constexpr int SMEM = 232448;                         // the per-CTA maximum; BODY + alignment slack
     static_assert(BODY + 512 <= SMEM, "shared memory budget");
     static_assert(COL_O + D <= 512, "TMEM budget");
@@ -92,6 +103,8 @@ struct AttnTcParams {
     int q_rows_dim;      // which tensor-map dim (1 or 2) runs over rows; the other over heads
     const uint8_t* kv;   // packed tiles [BHkv][n_kv][K chunks | V chunks]
     int n_kv;            // key tiles per head
+    const float* kscale; // fp16 mode: 2^-e per 32-key group [BHkv][n_kv][4]
+    const unsigned* vmax;   // fp16 mode: |V| maximum per kv head (float bits) [BHkv]
     const float* q;
     float* o;
     int64_t q_sb, q_sh, q_ss;   // element strides of Q: batch, head, sequence (features contiguous)
@@ -231,6 +244,99 @@ __global__ void __launch_bounds__(256) pack_kv_kernel(KvViews kv, uint8_t* __res
     }
 }
 
+// ---- fp16 mode: K / V packing --------------------------------------------
+// Byte `b` (0..127) of row `row` of a [rows][128 B] block as the 128-byte
+// swizzle mode reads it.
+__device__ __forceinline__ uint32_t swzb(int row, int b) {
+    return (uint32_t)row * 128 + ((((uint32_t)b >> 4) ^ ((uint32_t)row & 7)) << 4) + ((uint32_t)b & 15);
+}
+// Four consecutive K-dim elements e..e+3 (e % 4 == 0, e < 32: position in a
+// 128-byte row of 32 elements), already scaled, as fp16 h / l into a B-role
+// row ([l(16) | h(16)] per 16).
+__device__ __forceinline__ void put_f16_b4(uint8_t* blk, int row, int e, float4 x) {
+    const float h0 = round11(x.x), h1 = round11(x.y), h2 = round11(x.z), h3 = round11(x.w);
+    const int b = (e >> 4) * 64 + (e & 15) * 2;
+    *reinterpret_cast<uint2*>(blk + swzb(row, b)) =
+        make_uint2(f16x2_rn(x.x - h0, x.y - h1), f16x2_rn(x.z - h2, x.w - h3));
+    *reinterpret_cast<uint2*>(blk + swzb(row, b + 32)) = make_uint2(f16x2_rn(h0, h1), f16x2_rn(h2, h3));
+}
+
+// |V| maximum per kv head into vmax[h] (zeroed first; float bits).
+__global__ void __launch_bounds__(256) v_absmax_kernel(KvViews kv, int S, int D, unsigned* __restrict__ vmax) {
+    const int h = blockIdx.y, bb = h / kv.Hkv, hh = h % kv.Hkv;
+    const float* vb = kv.v + bb * kv.v_sb + hh * kv.v_sh;
+    float m = 0.0f;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < (int64_t)S * D / 4;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t key = i / (D / 4), d = (i % (D / 4)) * 4;
+        const float4 x = *reinterpret_cast<const float4*>(vb + key * kv.v_ss + d);
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) atomicMax(vmax + h, __float_as_uint(m));
+}
+
+// K (as K chunks of 64 features x 128 keys: two [128 keys][128 B] blocks) and
+// V^T (V chunks of D x V_KEYS keys: [D][128 B] per 32 keys) of one 128-key
+// tile in the fp16 mode.  K is scaled per 32 keys (this block's keys; its
+// 2^-e to kscale), V per head (from vmax).  Keys past S are zero.
+template <int D>
+__global__ void __launch_bounds__(256) pack_kv16_kernel(KvViews kv, uint8_t* __restrict__ out, int S, int n_kv,
+                                                        int* counter, float* __restrict__ kscale,
+                                                        const unsigned* __restrict__ vmax) {
+    using C = AttnTcCfg<D, true>;
+    if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *counter = 0;   // the attention kernel's item counter
+    constexpr int PER = 32 * D / 4 / 256;   // 4-element units per thread, of K and of V
+    __shared__ float sv[32][D + 1];
+    __shared__ float wmax[8];
+    const int j = blockIdx.x >> 2, sub = blockIdx.x & 3, h = blockIdx.y;
+    const int k0 = j * BKV + sub * 32;
+    uint8_t* tile = out + ((size_t)h * n_kv + j) * C::TILE_BYTES;
+    const int bb = h / kv.Hkv, hh = h % kv.Hkv;
+    const float* kb = kv.k + bb * kv.k_sb + hh * kv.k_sh;
+    const float* vb = kv.v + bb * kv.v_sb + hh * kv.v_sh;
+    float4 xk[PER], xv[PER];
+    float m = 0.0f;
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+        const int u = threadIdx.x + i * 256, r = u / (D / 4), d = (u % (D / 4)) * 4;
+        const bool in = k0 + r < S;
+        xk[i] = in ? *reinterpret_cast<const float4*>(kb + (int64_t)(k0 + r) * kv.k_ss + d) : make_float4(0.f, 0.f, 0.f, 0.f);
+        xv[i] = in ? *reinterpret_cast<const float4*>(vb + (int64_t)(k0 + r) * kv.v_ss + d) : make_float4(0.f, 0.f, 0.f, 0.f);
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(xk[i].x), fabsf(xk[i].y)), fmaxf(fabsf(xk[i].z), fabsf(xk[i].w))));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = m;
+    __syncthreads();
+    m = wmax[0];
+#pragma unroll
+    for (int w = 1; w < 8; w++) m = fmaxf(m, wmax[w]);
+    const int ek = f16_scale_exp(m);
+    const float sk = pow2i(ek);
+    if (threadIdx.x == 0) kscale[((size_t)h * n_kv + j) * 4 + sub] = pow2i(-ek);
+    const float svs = pow2i(f16_scale_exp(__uint_as_float(vmax[h])));
+    // K: unit = 4 consecutive features of one key
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+        const int u = threadIdx.x + i * 256, r = u / (D / 4), d = (u % (D / 4)) * 4;
+        sv[r][d] = xv[i].x; sv[r][d + 1] = xv[i].y; sv[r][d + 2] = xv[i].z; sv[r][d + 3] = xv[i].w;
+        const float4 x = make_float4(xk[i].x * sk, xk[i].y * sk, xk[i].z * sk, xk[i].w * sk);
+        uint8_t* kc = tile + (size_t)(d >> 6) * CHUNK + (size_t)((d >> 5) & 1) * (BKV * 128);
+        put_f16_b4(kc, sub * 32 + r, d & 31, x);
+    }
+    __syncthreads();
+    // V^T: unit = 4 consecutive keys of one feature
+    const int vc = (sub * 32) / C::V_KEYS, vsub = ((sub * 32) % C::V_KEYS) >> 5;
+    uint8_t* vcp = tile + (size_t)(C::K_CHUNKS + vc) * CHUNK + (size_t)vsub * D * 128;
+    for (int u = threadIdx.x; u < D * 8; u += blockDim.x) {
+        const int d = u >> 3, w = (u & 7) * 4;
+        const float4 x = make_float4(sv[w][d] * svs, sv[w + 1][d] * svs, sv[w + 2][d] * svs, sv[w + 3][d] * svs);
+        put_f16_b4(vcp, d, w, x);
+    }
+}
+
 // One work item = 128 queries of one (batch, head).  The grid is persistent
 // (one CTA per SM); each CTA's producer takes the next item from a global
 // counter, so items run in their list order across the GPU as on a plain
@@ -257,16 +363,17 @@ __device__ __forceinline__ void attn_decode(const AttnTcParams& p, int L, AttnIt
     it.n_tiles = (kv_len + BKV - 1) / BKV;
 }
 
-template <int D, bool CROSS>
+template <int D, int MODE>
 __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_constant__ AttnTcParams p) {
-    using C = AttnTcCfg<D>;
+    constexpr bool CROSS = MODE == AM_CROSS, F16 = MODE == AM_F16;
+    using C = AttnTcCfg<D, F16>;
     constexpr int STAGES = C::STAGES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem =
         reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t* qh = smem;
-    uint8_t* ql = qh + C::Q_BYTES;
-    uint8_t* ring = ql + C::Q_BYTES;
+    uint8_t* ql = qh + C::Q_BYTES;                // (tf32 modes: Q plane 1)
+    uint8_t* ring = qh + C::Q_PLANES * C::Q_BYTES;
     uint64_t* bars = reinterpret_cast<uint64_t*>(ring + STAGES * CHUNK);
     uint64_t* full = bars;                        // [STAGES]
     uint64_t* empty = bars + STAGES;              // [STAGES]
@@ -280,7 +387,8 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
     uint64_t* q_free = s_full + 7;                // the item's score MMAs done: Q space reusable
     uint64_t* pair_bar = s_full + 8;              // [4 quarters][3]
     uint64_t* item_full = pair_bar + 12;          // [4] item ring slot written (producer -> the other roles)
-    constexpr int NBAR = 2 * STAGES + 8 + 12 + 4;
+    uint64_t* qpair = item_full + 4;              // [4 quarters] Q row maxima exchanged (fp16 mode, per item)
+    constexpr int NBAR = 2 * STAGES + 8 + 12 + 4 + 4;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + NBAR);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     int* issued = const_cast<int*>(abort_flag) + 1;    // [STAGES + 1] phase of the last load (ring, Q), -1 none
@@ -288,6 +396,7 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
     volatile int* pv_fresh = items + 4;                // [2] per tile parity: P.V starts a new O accumulator
     static_assert(NBAR * 8 + 8 + 4 * (STAGES + 1) + 16 + 8 <= C::BAR_BYTES, "barrier area");
     float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + C::BAR_BYTES);   // [2][2][128]
+    float* qred = red + 4 * BQ;                                                                  // [2][128]
     if ((smem - smem_raw) + C::BODY > C::SMEM) {   // dynamic shared memory less aligned than assumed
         if (threadIdx.x == 0 && p.err) atomicCAS(p.err, 0, 0x205);
         return;
@@ -299,7 +408,7 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
         for (int i = 0; i < NBAR; i++) {
             uint32_t cnt = 1;
             if (&bars[i] == s_free || &bars[i] == p_full || &bars[i] == q_ready) cnt = 32 * SOFT_WARPS;
-            if (&bars[i] >= pair_bar && &bars[i] < item_full) cnt = 64;
+            if ((&bars[i] >= pair_bar && &bars[i] < item_full) || (&bars[i] >= qpair && &bars[i] < qpair + 4)) cnt = 64;
             ptx::mbar_init(&bars[i], cnt);
         }
         for (int s = 0; s <= STAGES; s++) issued[s] = -1;
@@ -376,6 +485,8 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
             constexpr uint32_t idesc_o = ptx::idesc_tf32(BQ, D);
             constexpr uint32_t idesc_sx = ptx::idesc_bf16(BQ, BKV);
             constexpr uint32_t idesc_ox = ptx::idesc_bf16(BQ, D);
+            constexpr uint32_t idesc_sh = ptx::idesc_f16(BQ, BKV);
+            constexpr uint32_t idesc_oh = ptx::idesc_f16(BQ, D);
             int stage = 0;
             uint32_t ph = 0;
             bool ok = true;
@@ -397,6 +508,25 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
                 for (int c = 0; c < C::K_CHUNKS; c++) {
                     uint8_t* buf = pop();
                     if (!buf) return;
+                    if (F16) {
+                        // 64 features: two 32-feature blocks of Q ([h | l] per 16) and of
+                        // K ([l | h] per 16); per 16 features h.h, h.l, l.h
+#pragma unroll
+                        for (int cs = 0; cs < 2; cs++)
+#pragma unroll
+                            for (int j = 0; j < 2; j++) {
+                                const uint8_t* a = qh + (c * 2 + cs) * BQ * 128 + j * 64;
+                                const uint8_t* b = buf + cs * BKV * 128 + j * 64;
+                                ptx::mma_bf16(tmem + COL_S, ptx::smem_desc(a, 1024, 2), ptx::smem_desc(b + 32, 1024, 2),
+                                              idesc_sh, (c | cs | j) ? 1u : 0u);
+                                ptx::mma_bf16(tmem + COL_S, ptx::smem_desc(a, 1024, 2), ptx::smem_desc(b, 1024, 2),
+                                              idesc_sh, 1u);
+                                ptx::mma_bf16(tmem + COL_S, ptx::smem_desc(a + 32, 1024, 2),
+                                              ptx::smem_desc(b + 32, 1024, 2), idesc_sh, 1u);
+                            }
+                        release();
+                        continue;
+                    }
                     const uint64_t ah = ptx::smem_desc(qh + c * BQ * 128, 1024, 2);
                     const uint64_t al = ptx::smem_desc(ql + c * BQ * 128, 1024, 2);
                     const uint64_t bh0 = ptx::smem_desc(buf, 1024, 2);
@@ -421,6 +551,23 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
                 for (int c = 0; c < C::V_CHUNKS; c++) {
                     uint8_t* buf = pop();
                     if (!buf) return;
+                    if (F16) {
+                        // V_KEYS keys: [D][128 B] per 32 keys ([l | h] per 16); P in TMEM as
+                        // 16 columns per 16 keys (8 of h, then 8 of l)
+#pragma unroll
+                        for (int sb = 0; sb < C::V_KEYS / 32; sb++)
+#pragma unroll
+                            for (int j = 0; j < 2; j++) {
+                                const uint8_t* b = buf + sb * D * 128 + j * 64;
+                                const uint32_t pc = tmem + COL_PH + (uint32_t)((c * C::V_KEYS + sb * 32 + j * 16));
+                                ptx::mma_bf16_ts(tmem + COL_O, pc, ptx::smem_desc(b + 32, 1024, 2), idesc_oh,
+                                                 (c | sb | j | !fresh) ? 1u : 0u);
+                                ptx::mma_bf16_ts(tmem + COL_O, pc, ptx::smem_desc(b, 1024, 2), idesc_oh, 1u);
+                                ptx::mma_bf16_ts(tmem + COL_O, pc + 8, ptx::smem_desc(b + 32, 1024, 2), idesc_oh, 1u);
+                            }
+                        release();
+                        continue;
+                    }
                     const uint64_t bh0 = ptx::smem_desc(buf, 1024, 2);
                     const uint64_t bl0 = ptx::smem_desc(buf + CHUNK / 2, 1024, 2);
 #pragma unroll
@@ -493,8 +640,55 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
         // This thread's half of its Q row: the raw values sit where their hi
         // parts go (the load used the planes' swizzle), so each thread splits
         // its own elements in place and writes plane 1 beside them.
+        float qinv_staged = 1.0f;   // fp16 mode: 2^-e of the staged item's Q row
         auto stage_q = [&](int r) -> bool {
             if (!ptx::wait_bounded(q_full, r & 1, abort_flag, p.err, ERR_A_SOFT, WAIT_NS)) return false;
+            if (F16) {
+                // the row's maximum over both halves, then each 32-feature block of
+                // this half rewritten in place as the fp16 plane ([h | l] per 16)
+                float mx = 0.0f;
+#pragma unroll 4
+                for (int i = 0; i < DH; i += 4) {
+                    const int d = half * DH + i;
+                    const float4 v = *reinterpret_cast<const float4*>(qh + (uint32_t)(d >> 5) * BQ * 128 + swz(row, d & 31));
+                    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+                }
+                qred[half * BQ + row] = mx;
+                ptx::mbar_arrive(&qpair[quarter]);
+                if (!ptx::wait_bounded(&qpair[quarter], r & 1, abort_flag, p.err, ERR_A_SOFT, WAIT_NS)) return false;
+                mx = fmaxf(mx, qred[(half ^ 1) * BQ + row]);
+                const int e = f16_scale_exp(mx);
+                const float sc = pow2i(e);
+                qinv_staged = pow2i(-e);
+#pragma unroll
+                for (int cb = 0; cb < DH / 32; cb++) {
+                    uint8_t* blk = qh + (uint32_t)(half * (DH / 32) + cb) * BQ * 128;
+                    float x[32];
+#pragma unroll
+                    for (int w = 0; w < 32; w += 4) {
+                        const float4 v = *reinterpret_cast<const float4*>(blk + swz(row, w));
+                        x[w] = v.x * sc; x[w + 1] = v.y * sc; x[w + 2] = v.z * sc; x[w + 3] = v.w * sc;
+                    }
+#pragma unroll
+                    for (int f16b = 0; f16b < 2; f16b++) {   // features 16*f16b .. +15
+                        uint32_t hw[8], lw[8];
+#pragma unroll
+                        for (int t = 0; t < 8; t++) {
+                            const float a = x[f16b * 16 + 2 * t], b = x[f16b * 16 + 2 * t + 1];
+                            const float ha = round11(a), hb = round11(b);
+                            hw[t] = f16x2_rn(ha, hb);
+                            lw[t] = f16x2_rn(a - ha, b - hb);
+                        }
+                        *reinterpret_cast<uint4*>(blk + swzb(row, f16b * 64)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                        *reinterpret_cast<uint4*>(blk + swzb(row, f16b * 64 + 16)) = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+                        *reinterpret_cast<uint4*>(blk + swzb(row, f16b * 64 + 32)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+                        *reinterpret_cast<uint4*>(blk + swzb(row, f16b * 64 + 48)) = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+                    }
+                }
+                ptx::fence_proxy_async_smem();
+                ptx::mbar_arrive(q_ready);
+                return true;
+            }
 #pragma unroll 4
             for (int i = 0; i < DH; i += 4) {
                 const int d = half * DH + i;
@@ -522,12 +716,23 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
                 break;
             }
             const int q = it.q0 + row;
+            const float qinv = qinv_staged;   // fp16 mode: this item's Q row scale (1 otherwise)
+            const int bhkv = it.bh / p.group;
+            const float vinv = F16 ? pow2i(-f16_scale_exp(__uint_as_float(p.vmax[bhkv]))) : 1.0f;
             float m = -FLT_MAX, l = 0.0f;   // m in log2 units; -FLT_MAX as the reference's initial max
             int pend = 0;                   // P.V tiles accumulated in TMEM since the last fold
             float o[DH];
 #pragma unroll
             for (int i = 0; i < DH; i++) o[i] = 0.0f;
             for (int j = 0; j < it.n_tiles; j++, T++) {
+                // fp16 mode: scores in log2 units need 2^-e of the Q row and of the
+                // tile's 32-key K groups (two per thread), loaded before the wait
+                float f0 = sl2, f1 = sl2;
+                if (F16) {
+                    const float* ks = p.kscale + ((size_t)bhkv * p.n_kv + j) * 4 + half * 2;
+                    f0 = sl2 * qinv * ks[0];
+                    f1 = sl2 * qinv * ks[1];
+                }
                 if (!(ok = ptx::wait_bounded(s_full, T & 1, abort_flag, p.err, ERR_A_SOFT, WAIT_NS))) break;
                 ptx::tc_fence_after();
                 float sv[KH];
@@ -539,7 +744,7 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
                                        *reinterpret_cast<uint32_t(*)[16]>(&rr[c16 * 16]));
                     ptx::tmem_ld_wait();
 #pragma unroll
-                    for (int i = 0; i < KH; i++) sv[i] = __uint_as_float(rr[i]) * sl2;
+                    for (int i = 0; i < KH; i++) sv[i] = __uint_as_float(rr[i]) * (i < 32 ? f0 : f1);
                 }
                 ptx::tc_fence_before();
                 ptx::mbar_arrive(s_free);   // S may be overwritten by the next tile's MMAs
@@ -621,6 +826,17 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
 #pragma unroll
                 for (int c16 = 0; c16 < KH / 16; c16++) {
                     uint32_t ph[16], pl[16];
+                    if (F16) {   // 16 columns per 16 keys: 8 of h pairs, then 8 of l pairs
+#pragma unroll
+                        for (int t = 0; t < 8; t++) {
+                            const float a = sv[c16 * 16 + 2 * t], b = sv[c16 * 16 + 2 * t + 1];
+                            const float ha = round11(a), hb = round11(b);
+                            ph[t] = f16x2_rn(ha, hb);
+                            ph[8 + t] = f16x2_rn(a - ha, b - hb);
+                        }
+                        ptx::tmem_st16(tmem + lane_off + COL_PH + half * KH + c16 * 16, ph);
+                        continue;
+                    }
                     if (CROSS) {   // plane 1: 8 columns of bf16 pairs of hi, then 8 of lo
 #pragma unroll
                         for (int i = 0; i < 16; i += 2) {
@@ -679,7 +895,7 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
             }
             ptx::tc_fence_before();
             if (q < p.S) {
-                const float inv = 1.0f / l;
+                const float inv = vinv / l;   // (fp16 mode: V was scaled by 1 / vinv)
                 const int64_t e0 = (int64_t)(it.bh / p.H) * p.o_sb + (int64_t)(it.bh % p.H) * p.o_sh +
                                    (int64_t)q * p.o_ss + half * DH;
                 float* orow = p.o + e0;
@@ -741,25 +957,43 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
     }
 }
 
-// Cross-term scheme unless RT_ATTN_3XTF32=1.
-bool attn_cross() {
-    static const bool on = [] {
-        const char* e = getenv("RT_ATTN_3XTF32");
-        return !(e && e[0] == '1');
+// Operand mode: fp16 (default), RT_ATTN_SCHEME=cross for tf32 + bf16 cross
+// terms, RT_ATTN_3XTF32=1 (or RT_ATTN_SCHEME=3xtf32) for three tf32 MMAs.
+int attn_mode() {
+    static const int v = [] {
+        const char* t = getenv("RT_ATTN_3XTF32");
+        const char* e = getenv("RT_ATTN_SCHEME");
+        if ((t && t[0] == '1') || (e && !strcmp(e, "3xtf32"))) return AM_3XTF32;
+        if (e && !strcmp(e, "cross")) return AM_CROSS;
+        return AM_F16;
     }();
-    return on;
+    return v;
 }
 
 template <int D>
 Status launch_tc(const AttnTcParams& prm, int BH, cudaStream_t st) {
     (void)BH;
     const dim3 grid((unsigned)min(prm.n_items, g_num_sms));   // persistent: one CTA per SM
-    if (attn_cross())
-        attn_tc_kernel<D, true><<<grid, ATHREADS, AttnTcCfg<D>::SMEM, st>>>(prm);
+    if (attn_mode() == AM_F16)
+        attn_tc_kernel<D, AM_F16><<<grid, ATHREADS, AttnTcCfg<D, true>::SMEM, st>>>(prm);
+    else if (attn_mode() == AM_CROSS)
+        attn_tc_kernel<D, AM_CROSS><<<grid, ATHREADS, AttnTcCfg<D>::SMEM, st>>>(prm);
     else
-        attn_tc_kernel<D, false><<<grid, ATHREADS, AttnTcCfg<D>::SMEM, st>>>(prm);
+        attn_tc_kernel<D, AM_3XTF32><<<grid, ATHREADS, AttnTcCfg<D>::SMEM, st>>>(prm);
     RT_LAUNCH_CHECK();
     return Status::ok();
+}
+
+// fp16 mode workspace after the packed tiles: K group scales, V head maxima.
+size_t tiles_bytes(int64_t BHkv, int64_t S, int D) {
+    const bool f16 = attn_mode() == AM_F16;
+    const size_t tile = D == 128 ? (f16 ? AttnTcCfg<128, true>::TILE_BYTES : AttnTcCfg<128>::TILE_BYTES)
+                                 : (f16 ? AttnTcCfg<64, true>::TILE_BYTES : AttnTcCfg<64>::TILE_BYTES);
+    return (size_t)BHkv * ((S + BKV - 1) / BKV) * tile;
+}
+size_t scales_bytes(int64_t BHkv, int64_t S) {
+    if (attn_mode() != AM_F16) return 0;
+    return ((size_t)BHkv * ((S + BKV - 1) / BKV) * 4 * 4 + (size_t)BHkv * 4 + 255) & ~(size_t)255;
 }
 
 }  // namespace
@@ -771,21 +1005,17 @@ bool attention_tc_applicable(int64_t S, int D, bool has_mask, int64_t BH) {
 }
 
 size_t attention_tc_workspace(int64_t BHkv, int64_t S, int D) {
-    const size_t tile = D == 128 ? AttnTcCfg<128>::TILE_BYTES : AttnTcCfg<64>::TILE_BYTES;
-    return (size_t)BHkv * ((S + BKV - 1) / BKV) * tile + 256;   // + the item counter
+    return tiles_bytes(BHkv, S, D) + scales_bytes(BHkv, S) + 256;   // + the item counter
 }
 
 Status attention_tc_prepare() {
     static bool done = false;
     if (!done) {
-        RT_CUDA_CHECK(cudaFuncSetAttribute(attn_tc_kernel<64, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           AttnTcCfg<64>::SMEM));
-        RT_CUDA_CHECK(cudaFuncSetAttribute(attn_tc_kernel<128, true>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, AttnTcCfg<128>::SMEM));
-        RT_CUDA_CHECK(cudaFuncSetAttribute(attn_tc_kernel<64, false>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, AttnTcCfg<64>::SMEM));
-        RT_CUDA_CHECK(cudaFuncSetAttribute(attn_tc_kernel<128, false>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, AttnTcCfg<128>::SMEM));
+        const void* ks[] = {(const void*)attn_tc_kernel<64, AM_F16>, (const void*)attn_tc_kernel<128, AM_F16>,
+                            (const void*)attn_tc_kernel<64, AM_CROSS>, (const void*)attn_tc_kernel<128, AM_CROSS>,
+                            (const void*)attn_tc_kernel<64, AM_3XTF32>, (const void*)attn_tc_kernel<128, AM_3XTF32>};
+        for (const void* k : ks)   // every configuration uses the per-CTA maximum (AttnTcCfg::SMEM)
+            RT_CUDA_CHECK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, AttnTcCfg<64>::SMEM));
         done = true;
     }
     return Status::ok();
@@ -801,8 +1031,19 @@ Status launch_attention_tc(const AttnViews& vw, int64_t BH, int64_t S, int D, in
     KvViews kv{vw.k, vw.v, vw.k_sb, vw.k_sh, vw.k_ss, vw.v_sb, vw.v_sh, vw.v_ss, vw.H / group};
     uint8_t* kvbuf = reinterpret_cast<uint8_t*>(ws.base);
     int* counter = reinterpret_cast<int*>(kvbuf + attention_tc_workspace(BHkv, S, D) - 256);
-    const bool cross = attn_cross();
-    if (D == 64 && cross) pack_kv_kernel<64, true><<<pgrid, 256, 0, st>>>(kv, kvbuf, (int)S, n_kv, counter);
+    const int mode = attn_mode();
+    const bool cross = mode == AM_CROSS;
+    float* kscale = reinterpret_cast<float*>(kvbuf + tiles_bytes(BHkv, S, D));
+    unsigned* vmax = reinterpret_cast<unsigned*>(kscale + (size_t)BHkv * n_kv * 4);
+    if (mode == AM_F16) {
+        RT_CUDA_CHECK(cudaMemsetAsync(vmax, 0, (size_t)BHkv * 4, st));
+        const int per_head = (int)std::max<int64_t>(1, std::min<int64_t>(64, (S * D / 4 + 4095) / 4096));
+        v_absmax_kernel<<<dim3((unsigned)per_head, (unsigned)BHkv), 256, 0, st>>>(kv, (int)S, D, vmax);
+        RT_LAUNCH_CHECK();
+        *launches += 1;
+        if (D == 64) pack_kv16_kernel<64><<<pgrid, 256, 0, st>>>(kv, kvbuf, (int)S, n_kv, counter, kscale, vmax);
+        else pack_kv16_kernel<128><<<pgrid, 256, 0, st>>>(kv, kvbuf, (int)S, n_kv, counter, kscale, vmax);
+    } else if (D == 64 && cross) pack_kv_kernel<64, true><<<pgrid, 256, 0, st>>>(kv, kvbuf, (int)S, n_kv, counter);
     else if (D == 64) pack_kv_kernel<64, false><<<pgrid, 256, 0, st>>>(kv, kvbuf, (int)S, n_kv, counter);
     else if (cross) pack_kv_kernel<128, true><<<pgrid, 256, 0, st>>>(kv, kvbuf, (int)S, n_kv, counter);
     else pack_kv_kernel<128, false><<<pgrid, 256, 0, st>>>(kv, kvbuf, (int)S, n_kv, counter);
@@ -812,6 +1053,8 @@ Status launch_attention_tc(const AttnViews& vw, int64_t BH, int64_t S, int D, in
     memset(&prm, 0, sizeof prm);
     prm.kv = reinterpret_cast<const uint8_t*>(ws.base);
     prm.n_kv = n_kv;
+    prm.kscale = kscale;
+    prm.vmax = vmax;
     prm.q = vw.q;
     prm.o = vw.o;
     prm.q_sb = vw.q_sb; prm.q_sh = vw.q_sh; prm.q_ss = vw.q_ss;
@@ -829,7 +1072,7 @@ Status launch_attention_tc(const AttnViews& vw, int64_t BH, int64_t S, int D, in
     {   // heads of one group together hold at most ~budget bytes of packed K/V
         size_t budget = (size_t)48 << 20;
         if (const char* e = getenv("RT_ATTN_GROUP_MB")) budget = (size_t)atoll(e) << 20;
-        const size_t per_head = (size_t)n_kv * (D == 128 ? AttnTcCfg<128>::TILE_BYTES : AttnTcCfg<64>::TILE_BYTES) / group;
+        const size_t per_head = tiles_bytes(1, S, D) / group;
         prm.head_group = (int)std::max<int64_t>(1, std::min<int64_t>(BH, (int64_t)(budget / per_head)));
     }
     prm.scale = 1.0f / sqrtf((float)D);

@@ -275,15 +275,18 @@ def test_matmul_variants(env):
 
 
 @pytest.mark.gpu
-def test_attention_3xtf32_variant():
-    """The three-tf32-MMA attention (RT_ATTN_3XTF32=1, read once per process)
-    passes the same attention cases, in a fresh process."""
+@pytest.mark.parametrize("env", [{"RT_ATTN_3XTF32": "1"}, {"RT_ATTN_SCHEME": "cross"}],
+                         ids=lambda e: ",".join(f"{k}={v}" for k, v in e.items()))
+def test_attention_scheme_variants(env):
+    """The other attention operand forms (three tf32 MMAs; tf32 + bf16 cross
+    terms -- read once per process) pass the same attention cases, each in a
+    fresh process."""
     import os
     import subprocess
     import sys
     r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", "-m", "gpu", "-p", "no:cacheprovider",
                         __file__, "-k", "test_attention and not variant"],
-                       env=dict(os.environ, RT_ATTN_3XTF32="1"), capture_output=True, text=True, timeout=600)
+                       env=dict(os.environ, **env), capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
 
 
