@@ -647,7 +647,7 @@ bool rope_valid(const Analysis& an, const RopeMatch& m, const std::vector<Range>
 void plan_rope_folds(const std::vector<OpNode>& nodes, const std::vector<Range>& protect,
                      std::vector<PlanItem>& items, std::vector<bool>& gone,
                      std::vector<std::pair<int, std::vector<Range>>>& reads_of) {
-    Analysis an(nodes, &gone);
+    Analysis an(nodes, &gone, &reads_of);
     for (int a = 0; a < (int)nodes.size(); a++) {
         if (gone[a]) continue;
         RopeMatch m;
@@ -684,7 +684,8 @@ void plan_rope_folds(const std::vector<OpNode>& nodes, const std::vector<Range>&
 // and the GATED_ACT touches that output (the GEMM now writes it earlier).
 // The GATED_ACT arithmetic is the same fp32 function of the same fp32 values.
 void plan_gated_gemm_folds(const std::vector<OpNode>& nodes, const std::vector<Range>& protect,
-                           std::vector<PlanItem>& items, std::vector<bool>& gone) {
+                           std::vector<PlanItem>& items, std::vector<bool>& gone,
+                           std::vector<std::pair<int, std::vector<Range>>>& reads_of) {
     static const bool on = [] {
         const char* v = getenv("RT_FUSE_GATED_GEMM");
         const char* bn = getenv("RT_GEMM_BN");
@@ -766,13 +767,14 @@ void plan_gated_gemm_folds(const std::vector<OpNode>& nodes, const std::vector<R
         items[m].epi_out = ga.output;
         // The slices vanish from later analyses; the GATED_ACT is not launched
         // but stays in them as the writer of its output (the GEMM now writes
-        // it, earlier), so their dead / recycled reasoning about that region
-        // holds.
+        // it, earlier) that reads nothing, so their dead / recycled reasoning
+        // about both regions holds.
         for (int k : {sx, su}) {
             items[k].skip = true;
             gone[k] = true;
         }
         items[g].skip = true;
+        reads_of.push_back({g, {}});
         if (dbg()) fprintf(stderr, "[fusion] gemm %d applies GATED_ACT %d in its epilogue (slices %d, %d)\n", m, g, sx, su);
     }
 }
@@ -786,11 +788,11 @@ void plan_gated_gemm_folds(const std::vector<OpNode>& nodes, const std::vector<R
 void plan_gated_folds(const std::vector<OpNode>& nodes, const std::vector<Range>& protect,
                       std::vector<PlanItem>& items, std::vector<bool>& gone,
                       std::vector<std::pair<int, std::vector<Range>>>& reads_of) {
-    Analysis an(nodes, &gone);
+    Analysis an(nodes, &gone, &reads_of);
     const int n = (int)nodes.size();
     for (int g = 0; g < n; g++) {
         const OpNode& ga = nodes[g];
-        if (gone[g] || ga.op != RT_OP_GATED_ACT || ga.elem_size != 4) continue;
+        if (gone[g] || items[g].skip || ga.op != RT_OP_GATED_ACT || ga.elem_size != 4) continue;
         const int64_t N = last_dim(ga), rows = N ? total_elements(ga) / N : 0;
         const int slot_x = 0, slot_up = ga.extra[0] ? 2 : 1;
         GatedViews v{static_cast<const float*>(ga.inputs[slot_x]), static_cast<const float*>(ga.inputs[slot_up]), N, N};
@@ -1136,7 +1138,7 @@ std::vector<PlanItem> plan_fusions(const std::vector<OpNode>& nodes,
     std::vector<std::pair<int, std::vector<Range>>> reads_of;
     if (fusion_enabled()) {
         plan_bias_folds(nodes, protect, items, gone, bias_plan ? bias_plan : &local_bp);
-        plan_gated_gemm_folds(nodes, protect, items, gone);   // before the rotary folds: it sees every node
+        plan_gated_gemm_folds(nodes, protect, items, gone, reads_of);   // before the rotary folds: it sees every node
         plan_rope_folds(nodes, protect, items, gone, reads_of);
         plan_gated_folds(nodes, protect, items, gone, reads_of);
     }
