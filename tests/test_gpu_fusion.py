@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 
 import oracle
-from conftest import PLANE_HANDOFFS
+from conftest import GOLDEN, PLANE_HANDOFFS
 from lbr_b200.program import OP, ConstSpec, ProgNode, Program, Ref
 
 pytestmark = pytest.mark.gpu
@@ -253,3 +253,14 @@ def test_gated_gemm_fold_off_matches():
                         os.path.join(os.path.dirname(__file__), "test_gpu_programs.py"), "-k", "qwen3_mini"],
                        env=dict(os.environ, RT_FUSE_GATED_GEMM="0"), capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and " passed" in r.stdout, r.stdout[-3000:] + r.stderr[-2000:]
+
+
+def test_gated_gemm_fold_keeps_the_rotary_folds(gpu_executor_factory):
+    """On the full Qwen3 body (batch 1) the gated GEMM fold and both rotary
+    folds per layer apply together."""
+    prog = Program.load(GOLDEN / "qwen3_b1.json")
+    ex = gpu_executor_factory(prog, prog.make_constants())
+    flags = flags_of(ex, prog)
+    layers = sum(1 for nd in prog.nodes if nd.op == OP["GATED_ACT"])
+    assert flags.count(7) == layers
+    assert flags.count(5) == 2 * layers
