@@ -259,11 +259,12 @@ def test_gated_gemm_fold_off_matches():
 
 
 def test_gated_gemm_fold_keeps_the_rotary_folds(gpu_executor_factory):
-    """On the full Qwen3 body (batch 1) the gated GEMM fold and both rotary
+    """On the full Qwen3 body (batch 8) the gated GEMM fold and both rotary
     folds per layer apply together."""
-    prog = Program.load(GOLDEN / "qwen3_b1.json")
+    prog = Program.load(GOLDEN / "qwen3_b8.json")
     ex = gpu_executor_factory(prog, prog.make_constants())
     flags = flags_of(ex, prog)
+    ex.close()
     layers = sum(1 for nd in prog.nodes if nd.op == OP["GATED_ACT"])
     assert flags.count(7) == layers
     assert flags.count(5) == 2 * layers
