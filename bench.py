@@ -307,6 +307,7 @@ def main():
     launches = ex.kernel_launches
     if rank == 0:
         hbm, bf16, bf16_sus, basis = load_peaks()
+        peak, peak_kind = (bf16_sus, "sustained") if bf16_sus else (bf16, "burst")
         gemm_ids = [i for i, n in enumerate(prog.nodes) if n.op in (OP["MATMUL"], OP["MATMUL_ADD"])]
         gemm_flops = sum(node_flops(prog.nodes[i]) for i in gemm_ids)
         gemm_ms = sum(per_node_ms[i] for i in gemm_ids)
@@ -315,7 +316,8 @@ def main():
             "metric": metric, "value": round(gb / (ms / 1e3), 3), "unit": unit,
             "n_gpus": n_gpus, "steps": args.steps, "warmup": max(args.warmup, 3),
             "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f32 (3xTF32 tensor-core contractions)",
+            "vs_baseline": None,
+            "dtype": "f32 (contractions: fp32 operands as scaled fp16 hi / lo, three tensor-core MMAs per product)",
             "data": "synthetic: seeded N(0,0.02) weights, N(0,1) hidden states",
             "config": {"workload": CONFIGS[args.config], "program": program_name(args.config, b_local),
                        "global_batch": gb, "batch_per_gpu": b_local, "parallelism": f"dp{n_gpus}",
@@ -327,19 +329,18 @@ def main():
                             if pipe is not None else "CudaCompiledExecutor.run"),
                     "single_graph_value": round(gb / (e2e_single_ms / 1e3), 3)},
             "gpu_launches": launches * args.steps,
-            "roofline": {"bound": "tensor", "kernel": "MATMUL/MATMUL_ADD nodes (sum)",
-                         "achieved": round(achieved, 3), "peak": bf16, "unit": "TFLOP/s",
-                         "frac": round(achieved / bf16, 4),
+            "roofline": {"bound": "tensor", "kernel": "MATMUL/MATMUL_ADD nodes (sum, incl. their A split)",
+                         "achieved": round(achieved, 3), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(achieved / peak, 4),
                          "traffic": GEMM_TRAFFIC.get(args.config),
-                         "traffic_source": "profiles/tc_gemm_pair_kernel_gpt2_b8.md (ncu dram__bytes_read+write, "
-                                           "mean per launch of the captured FFN GEMMs)"
-                         if args.config in GEMM_TRAFFIC else None,
-                         "peak_basis": f"{basis} bf16 dense burst",
-                         # fp32 products as one tf32 MMA (half the bf16 rate) + one bf16 MMA over
-                         # a doubled K: 4 bf16-rate units per product, so bf16 / 4 is the ceiling
-                         "peak_split_effective": round(bf16 / 4, 1),
-                         "frac_split": round(achieved / (bf16 / 4), 4)},
-            "roofline_attention": attention_roofline(prog, per_node_ms, bf16),
+                         "traffic_source": GEMM_TRAFFIC_SOURCE.get(args.config),
+                         "peak_basis": f"{basis} bf16 dense, {peak_kind} (the GEMMs run inside a "
+                                       f"seconds-long step)",
+                         "frac_burst": round(achieved / bf16, 4),
+                         # fp32 products from `slots` bf16-rate MMA slots each (fp16 hi / lo: 3)
+                         "peak_split_effective": round(peak / GEMM_SLOTS[gemm_scheme()], 1),
+                         "frac_split": round(achieved / (peak / GEMM_SLOTS[gemm_scheme()]), 4)},
+            "roofline_attention": attention_roofline(prog, per_node_ms, peak),
             "clocks": clocks.summary(),
             "per_op_ms": summarize_ops(prog, per_node_ms),
         }
@@ -365,7 +366,31 @@ def main():
 
 # DRAM bytes per GEMM launch from the committed ncu capture of this workload
 # (mean of the two captured FFN launches), used as the roofline "traffic".
-GEMM_TRAFFIC = {"gpt2": round((70.72 + 56.72 + 293.58 + 23.13) / 2 * 1e6)}
+GEMM_TRAFFIC = {"gpt2": round((70.72 + 56.72 + 293.58 + 23.13) / 2 * 1e6),
+                # 1b8k: mean over the four GEMMs of profiles/tc_gemm_pair_kernel_1b8k_b1.md (B1
+                # capture, 574 MB per launch) scaled by the rows of a B8 launch (x8)
+                "1b8k": round((303.24 + 174.15 + 85.55 + 27.80 + 839.96 + 242.60 + 561.09 + 61.64) / 4 * 8 * 1e6)}
+GEMM_TRAFFIC_SOURCE = {"gpt2": "profiles/tc_gemm_pair_kernel_gpt2_b8.md (ncu dram__bytes_read+write, mean per "
+                               "launch of the captured FFN GEMMs; tf32 + bf16 cross-term form)",
+                       "1b8k": "profiles/tc_gemm_pair_kernel_1b8k_b1.md (ncu dram__bytes_read+write, mean per "
+                               "launch of the four GEMMs at B1, scaled x8 to the B8 launch's rows)"}
+
+
+# bf16-rate MMA slots per fp32 product of each operand scheme (the library's
+# defaults and switches: RT_GEMM_SCHEME / RT_GEMM_3XTF32, RT_ATTN_SCHEME / RT_ATTN_3XTF32)
+GEMM_SLOTS = {"f16": 3, "cross": 4, "3xtf32": 6}
+
+
+def gemm_scheme():
+    if os.environ.get("RT_GEMM_3XTF32") == "1" or os.environ.get("RT_GEMM_SCHEME") == "3xtf32":
+        return "3xtf32"
+    return "cross" if os.environ.get("RT_GEMM_SCHEME") == "cross" else "f16"
+
+
+def attn_scheme():
+    if os.environ.get("RT_ATTN_3XTF32") == "1" or os.environ.get("RT_ATTN_SCHEME") == "3xtf32":
+        return "3xtf32"
+    return "cross" if os.environ.get("RT_ATTN_SCHEME") == "cross" else "f16"
 
 
 def attention_roofline(prog, per_node_ms, bf16):
@@ -377,7 +402,7 @@ def attention_roofline(prog, per_node_ms, bf16):
     ach = fl / (ms / 1e3) / 1e12 if ms else 0.0
     return {"bound": "tensor", "kernel": "ATTENTION nodes (pack + attn_tc_kernel)", "achieved": round(ach, 3),
             "peak": bf16, "unit": "TFLOP/s", "frac": round(ach / bf16, 4),
-            "frac_split": round(ach / (bf16 / 4), 4)}
+            "frac_split": round(ach / (bf16 / GEMM_SLOTS[attn_scheme()]), 4)}
 
 
 def summarize_ops(prog, per_node_ms):
