@@ -32,6 +32,7 @@ constexpr int TT = 512;                 // threads per CTA
 constexpr int TC = 8;                   // CTAs per cluster (portable maximum) of the cluster form
 constexpr int TSMEM = 80 * 1024;        // dynamic shared memory per CTA (attention scores, GEMM tiles)
 constexpr int KC = 256;                 // K per GEMM shared-memory chunk: the toy's GEMMs load A and B once
+constexpr size_t MIRROR_MAX = 144 * 1024;   // largest arena held in shared memory (after TSMEM, within 227 KB)
 constexpr int ATT_S_MAX = 128;          // S x S fp32 scores of one head fit TSMEM
 constexpr int64_t MAX_NODE_ELEMS = (int64_t)1 << 18;
 constexpr int64_t MAX_NODE_MACS = (int64_t)1 << 22;
@@ -382,20 +383,58 @@ __device__ void run_node(const OpNode& n, const Th& t, float* sm) {
 
 // NC == 1: one CTA, a CTA barrier between nodes; NC > 1: a cluster of NC
 // CTAs (launched with the cluster attribute), a cluster barrier.
+// Generic address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ void* map_rank(void* p, uint32_t rank) {
+    uint64_t r;
+    asm volatile("mapa.u64 %0, %1, %2;" : "=l"(r) : "l"(reinterpret_cast<uint64_t>(p)), "r"(rank));
+    return reinterpret_cast<void*>(r);
+}
+
+// The arena mirror: while the launch runs, every node pointer into the
+// mirrored allocation is redirected to the same offset of a shared-memory
+// copy of it (CTA 0's, reached through distributed shared memory by the other
+// CTAs of a cluster); generic loads and stores then stay on the SM.  The
+// allocation is copied in first (nodes only read what earlier nodes wrote,
+// but the copy also keeps any never-written bytes identical) and out last.
 template <int NC>
-__global__ void __launch_bounds__(TT, 1) tiny_graph_kernel(const OpNode* __restrict__ nodes, int n_nodes) {
-    extern __shared__ float sm[];
+__global__ void __launch_bounds__(TT, 1) tiny_graph_kernel(const OpNode* __restrict__ nodes, int n_nodes,
+                                                           char* __restrict__ mirror, size_t mirror_bytes) {
+    extern __shared__ __align__(16) float sm[];
+    __shared__ OpNode cur;
     Th t;
     t.rank = NC > 1 ? (int)ptx::cluster_ctarank() : 0;
     t.C = NC;
     t.tid = threadIdx.x;
     t.g = t.rank * TT + t.tid;
     t.G = NC * TT;
+    char* local_mirror = reinterpret_cast<char*>(sm) + TSMEM;   // CTA 0's copy is the one used
+    char* smirror = mirror_bytes ? (NC > 1 ? static_cast<char*>(map_rank(local_mirror, 0)) : local_mirror) : nullptr;
+    if (mirror_bytes && t.rank == 0) {
+        for (size_t o = (size_t)t.tid * 16; o < mirror_bytes; o += (size_t)TT * 16)
+            *reinterpret_cast<uint4*>(local_mirror + o) = *reinterpret_cast<const uint4*>(mirror + o);
+    }
+    if (NC > 1) ptx::cluster_sync();
+    else __syncthreads();
+    auto redirect = [&](void* p) -> void* {
+        const uintptr_t x = reinterpret_cast<uintptr_t>(p), b = reinterpret_cast<uintptr_t>(mirror);
+        return (smirror && x >= b && x < b + mirror_bytes) ? static_cast<void*>(smirror + (x - b)) : p;
+    };
     for (int i = 0; i < n_nodes; i++) {
-        run_node(nodes[i], t, sm);
+        if (t.tid == 0) {
+            cur = nodes[i];
+            for (int k = 0; k < cur.n_inputs && k < RT_MAX_INPUTS; k++) cur.inputs[k] = redirect(cur.inputs[k]);
+            cur.output = redirect(cur.output);
+        }
+        __syncthreads();
+        run_node(cur, t, sm);
         if (NC > 1) ptx::cluster_sync();   // release / acquire at cluster scope: node i's writes before node i+1
         else __syncthreads();              // CTA scope
     }
+    if (mirror_bytes && t.rank == 0) {
+        for (size_t o = (size_t)t.tid * 16; o < mirror_bytes; o += (size_t)TT * 16)
+            *reinterpret_cast<uint4*>(mirror + o) = *reinterpret_cast<const uint4*>(local_mirror + o);
+    }
+    if (NC > 1) ptx::cluster_sync();   // CTA 0's shared memory outlives the other CTAs' last remote access
 }
 
 // The cluster of TC CTAs by default; RT_TINY_CTAS=1 runs one CTA with CTA
@@ -474,9 +513,28 @@ Status tiny_graph_build(const std::vector<OpNode>& nodes, TinyPlan* out) {
     RT_CUDA_CHECK(cudaMalloc(&t.dev_nodes, bytes));
     cudaError_t e = cudaMemcpy(t.dev_nodes, nodes.data(), bytes, cudaMemcpyHostToDevice);
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(tiny_graph_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, TSMEM);
+        e = cudaFuncSetAttribute(tiny_graph_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)(TSMEM + MIRROR_MAX));
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(tiny_graph_kernel<TC>, cudaFuncAttributeMaxDynamicSharedMemorySize, TSMEM);
+        e = cudaFuncSetAttribute(tiny_graph_kernel<TC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)(TSMEM + MIRROR_MAX));
+    // Mirror the arena in shared memory when every node writes into one
+    // allocation of this library that fits (RT_TINY_MIRROR=0: no mirror).
+    const char* mv = getenv("RT_TINY_MIRROR");
+    uintptr_t base = 0;
+    size_t abytes = 0;
+    bool mirror = !(mv && mv[0] == '0');
+    for (size_t i = 0; i < nodes.size() && mirror; i++) {
+        uintptr_t b;
+        size_t n;
+        if (!allocation_of(nodes[i].output, &b, &n) || (i > 0 && b != base)) mirror = false;
+        base = b;
+        abytes = n;
+    }
+    if (mirror && abytes <= MIRROR_MAX && abytes % 16 == 0 && base % 16 == 0) {
+        t.mirror = reinterpret_cast<char*>(base);
+        t.mirror_bytes = abytes;
+    }
     if (e != cudaSuccess) {
         cudaGetLastError();
         cudaFree(t.dev_nodes);
@@ -489,12 +547,12 @@ Status tiny_graph_build(const std::vector<OpNode>& nodes, TinyPlan* out) {
 
 Status launch_tiny(const TinyPlan& t, cudaStream_t st, int* launches) {
     if (tiny_ctas() == 1) {
-        tiny_graph_kernel<1><<<1, TT, TSMEM, st>>>(t.dev_nodes, t.n);
+        tiny_graph_kernel<1><<<1, TT, TSMEM + t.mirror_bytes, st>>>(t.dev_nodes, t.n, t.mirror, t.mirror_bytes);
     } else {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(TC);
         cfg.blockDim = dim3(TT);
-        cfg.dynamicSmemBytes = TSMEM;
+        cfg.dynamicSmemBytes = TSMEM + t.mirror_bytes;
         cfg.stream = st;
         cudaLaunchAttribute attr;
         attr.id = cudaLaunchAttributeClusterDimension;
@@ -503,7 +561,8 @@ Status launch_tiny(const TinyPlan& t, cudaStream_t st, int* launches) {
         attr.val.clusterDim.z = 1;
         cfg.attrs = &attr;
         cfg.numAttrs = 1;
-        RT_CUDA_CHECK(cudaLaunchKernelEx(&cfg, tiny_graph_kernel<TC>, (const OpNode*)t.dev_nodes, t.n));
+        RT_CUDA_CHECK(cudaLaunchKernelEx(&cfg, tiny_graph_kernel<TC>, (const OpNode*)t.dev_nodes, t.n, t.mirror,
+                                         t.mirror_bytes));
     }
     RT_LAUNCH_CHECK();
     *launches += 1;

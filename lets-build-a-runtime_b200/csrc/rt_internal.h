@@ -111,7 +111,11 @@ Status launch_attention(const OpNode& n, cudaStream_t st, Workspace ws, int* lau
 struct TinyPlan {
     OpNode* dev_nodes = nullptr;   // device copy of the node array
     int n = 0;                     // 0: not used by this plan
+    char* mirror = nullptr;        // the allocation all node outputs live in (the arena), held in
+    size_t mirror_bytes = 0;       //   shared memory during the launch when it fits (0: not mirrored)
 };
+// The allocation containing [p, p+1) made through this library: base and size.
+bool allocation_of(const void* p, uintptr_t* base, size_t* bytes);
 bool tiny_graph_applicable(const std::vector<OpNode>& nodes);
 Status tiny_graph_build(const std::vector<OpNode>& nodes, TinyPlan* out);   // before any capture
 Status launch_tiny(const TinyPlan& t, cudaStream_t st, int* launches);
