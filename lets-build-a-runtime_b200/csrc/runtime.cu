@@ -107,15 +107,6 @@ const Alloc* find_alloc(const void* p, size_t bytes, uintptr_t* base_out = nullp
     return &it->second;
 }
 
-bool allocation_of(const void* p, uintptr_t* base, size_t* bytes) {
-    uintptr_t b;
-    const Alloc* a = find_alloc(p, 1, &b);
-    if (!a || a->host) return false;
-    *base = b;
-    *bytes = a->bytes;
-    return true;
-}
-
 // Device-memory check for a buffer a node reads or writes.
 Status check_buffer(const void* p, size_t bytes, int node, const char* what) {
     char buf[160];
@@ -592,6 +583,16 @@ void clear_plans() {
 }
 
 }  // namespace
+
+bool allocation_of(const void* p, uintptr_t* base, size_t* bytes) {
+    uintptr_t b;
+    const Alloc* a = find_alloc(p, 1, &b);
+    if (!a || a->host) return false;
+    *base = b;
+    *bytes = a->bytes;
+    return true;
+}
+
 
 bool SplitKey::operator<(const SplitKey& o) const {
     if (src != o.src) return src < o.src;
