@@ -32,7 +32,9 @@ constexpr int TT = 512;                 // threads per CTA
 constexpr int TC = 8;                   // CTAs per cluster (portable maximum) of the cluster form
 constexpr int TSMEM = 80 * 1024;        // dynamic shared memory per CTA (attention scores, GEMM tiles)
 constexpr int KC = 256;                 // K per GEMM shared-memory chunk: the toy's GEMMs load A and B once
-constexpr size_t MIRROR_MAX = 144 * 1024;   // largest arena held in shared memory (after TSMEM, within 227 KB)
+constexpr int MAX_NODES = 48;               // node array held in shared memory (48 x 312 B)
+constexpr size_t NODES_SMEM = (MAX_NODES * sizeof(OpNode) + 15) / 16 * 16;
+constexpr size_t MIRROR_MAX = 128 * 1024;   // largest arena held in shared memory (opt-in, RT_TINY_MIRROR=1)
 constexpr int ATT_S_MAX = 128;          // S x S fp32 scores of one head fit TSMEM
 constexpr int64_t MAX_NODE_ELEMS = (int64_t)1 << 18;
 constexpr int64_t MAX_NODE_MACS = (int64_t)1 << 22;
@@ -400,33 +402,39 @@ template <int NC>
 __global__ void __launch_bounds__(TT, 1) tiny_graph_kernel(const OpNode* __restrict__ nodes, int n_nodes,
                                                            char* __restrict__ mirror, size_t mirror_bytes) {
     extern __shared__ __align__(16) float sm[];
-    __shared__ OpNode cur;
     Th t;
     t.rank = NC > 1 ? (int)ptx::cluster_ctarank() : 0;
     t.C = NC;
     t.tid = threadIdx.x;
     t.g = t.rank * TT + t.tid;
     t.G = NC * TT;
-    char* local_mirror = reinterpret_cast<char*>(sm) + TSMEM;   // CTA 0's copy is the one used
+    OpNode* snodes = reinterpret_cast<OpNode*>(reinterpret_cast<char*>(sm) + TSMEM);   // [n_nodes]
+    char* local_mirror = reinterpret_cast<char*>(sm) + TSMEM + NODES_SMEM;   // CTA 0's copy is the one used
     char* smirror = mirror_bytes ? (NC > 1 ? static_cast<char*>(map_rank(local_mirror, 0)) : local_mirror) : nullptr;
     if (mirror_bytes && t.rank == 0) {
         for (size_t o = (size_t)t.tid * 16; o < mirror_bytes; o += (size_t)TT * 16)
             *reinterpret_cast<uint4*>(local_mirror + o) = *reinterpret_cast<const uint4*>(mirror + o);
     }
+    // the whole node array into shared memory at once (all loads in flight),
+    // pointers redirected to the mirror when there is one
+    for (size_t o = (size_t)t.tid * 16; o < (size_t)n_nodes * sizeof(OpNode); o += (size_t)TT * 16)
+        *reinterpret_cast<uint4*>(reinterpret_cast<char*>(snodes) + o) =
+            *reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(nodes) + o);
+    __syncthreads();
+    if (smirror && t.tid < n_nodes) {
+        OpNode& nd = snodes[t.tid];
+        const uintptr_t b = reinterpret_cast<uintptr_t>(mirror);
+        auto redirect = [&](void* p) -> void* {
+            const uintptr_t x = reinterpret_cast<uintptr_t>(p);
+            return (x >= b && x < b + mirror_bytes) ? static_cast<void*>(smirror + (x - b)) : p;
+        };
+        for (int k = 0; k < nd.n_inputs && k < RT_MAX_INPUTS; k++) nd.inputs[k] = redirect(nd.inputs[k]);
+        nd.output = redirect(nd.output);
+    }
     if (NC > 1) ptx::cluster_sync();
     else __syncthreads();
-    auto redirect = [&](void* p) -> void* {
-        const uintptr_t x = reinterpret_cast<uintptr_t>(p), b = reinterpret_cast<uintptr_t>(mirror);
-        return (smirror && x >= b && x < b + mirror_bytes) ? static_cast<void*>(smirror + (x - b)) : p;
-    };
     for (int i = 0; i < n_nodes; i++) {
-        if (t.tid == 0) {
-            cur = nodes[i];
-            for (int k = 0; k < cur.n_inputs && k < RT_MAX_INPUTS; k++) cur.inputs[k] = redirect(cur.inputs[k]);
-            cur.output = redirect(cur.output);
-        }
-        __syncthreads();
-        run_node(cur, t, sm);
+        run_node(snodes[i], t, sm);
         if (NC > 1) ptx::cluster_sync();   // release / acquire at cluster scope: node i's writes before node i+1
         else __syncthreads();              // CTA scope
     }
@@ -462,7 +470,7 @@ bool tiny_graph_applicable(const std::vector<OpNode>& nodes) {
     const char* env = getenv("RT_TINY");
     if (env && env[0] == '0') return false;
     const bool force = env && !strcmp(env, "force");
-    if (nodes.empty() || nodes.size() > 512 || (!force && nodes.size() < 4)) return false;
+    if (nodes.empty() || nodes.size() > (size_t)MAX_NODES || (!force && nodes.size() < 4)) return false;
     int64_t macs = 0;
     for (const OpNode& n : nodes) {
         if (n.elem_size != 4 || n.n_dims < 1 || numel_h(n) > MAX_NODE_ELEMS) return false;
@@ -510,20 +518,23 @@ bool tiny_graph_applicable(const std::vector<OpNode>& nodes) {
 Status tiny_graph_build(const std::vector<OpNode>& nodes, TinyPlan* out) {
     TinyPlan t;
     const size_t bytes = nodes.size() * sizeof(OpNode);
-    RT_CUDA_CHECK(cudaMalloc(&t.dev_nodes, bytes));
+    RT_CUDA_CHECK(cudaMalloc(&t.dev_nodes, (bytes + 15) / 16 * 16));   // read in 16-byte units
     cudaError_t e = cudaMemcpy(t.dev_nodes, nodes.data(), bytes, cudaMemcpyHostToDevice);
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(tiny_graph_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)(TSMEM + MIRROR_MAX));
+                                 (int)(TSMEM + NODES_SMEM + MIRROR_MAX));
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(tiny_graph_kernel<TC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)(TSMEM + MIRROR_MAX));
-    // Mirror the arena in shared memory when every node writes into one
-    // allocation of this library that fits (RT_TINY_MIRROR=0: no mirror).
+                                 (int)(TSMEM + NODES_SMEM + MIRROR_MAX));
+    // Opt-in (RT_TINY_MIRROR=1): mirror the arena in shared memory when every
+    // node writes into one allocation of this library that fits.  Measured on
+    // the toy: slower (165 against 129 us per forward with 8 CTAs) -- the
+    // other CTAs reach CTA 0's copy through distributed shared memory, whose
+    // latency the dot-product loops of the attention and GEMM nodes expose.
     const char* mv = getenv("RT_TINY_MIRROR");
     uintptr_t base = 0;
     size_t abytes = 0;
-    bool mirror = !(mv && mv[0] == '0');
+    bool mirror = mv && mv[0] == '1';
     for (size_t i = 0; i < nodes.size() && mirror; i++) {
         uintptr_t b;
         size_t n;
@@ -547,12 +558,12 @@ Status tiny_graph_build(const std::vector<OpNode>& nodes, TinyPlan* out) {
 
 Status launch_tiny(const TinyPlan& t, cudaStream_t st, int* launches) {
     if (tiny_ctas() == 1) {
-        tiny_graph_kernel<1><<<1, TT, TSMEM + t.mirror_bytes, st>>>(t.dev_nodes, t.n, t.mirror, t.mirror_bytes);
+        tiny_graph_kernel<1><<<1, TT, TSMEM + NODES_SMEM + t.mirror_bytes, st>>>(t.dev_nodes, t.n, t.mirror, t.mirror_bytes);
     } else {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(TC);
         cfg.blockDim = dim3(TT);
-        cfg.dynamicSmemBytes = TSMEM + t.mirror_bytes;
+        cfg.dynamicSmemBytes = TSMEM + NODES_SMEM + t.mirror_bytes;
         cfg.stream = st;
         cudaLaunchAttribute attr;
         attr.id = cudaLaunchAttributeClusterDimension;
