@@ -183,21 +183,32 @@ __device__ void gemm_d(const OpNode& n, const Th& t, float* sm) {
         const float* Bb = B + (b2d ? 0 : bz * N * K);
         float acc0 = 0.f, acc1 = 0.f;
         for (int64_t k0 = 0; k0 < K; k0 += KC) {
-#pragma unroll 4
-            for (int e = t.tid; e < KC * 32; e += TT) {
+            // every load of the chunk in flight before the first shared store
+            // (KC * 32 / TT = 16 values of A and of B per thread)
+            constexpr int PER = KC * 32 / TT;
+            float ra[PER], rb[PER];
+#pragma unroll
+            for (int i = 0; i < PER; i++) {
+                const int e = t.tid + i * TT;
                 const int k = e % KC, r = e / KC;   // A: consecutive threads walk K of one row
                 const int64_t gm = m0 + r, gk = k0 + k;
-                As[k][r] = (gm < M && gk < K) ? Ab[gm * K + gk] : 0.f;
-                const int64_t gn = n0 + r;
-                if (tb) Bs[k][r] = (gn < N && gk < K) ? Bb[gn * K + gk] : 0.f;
-            }
-            if (!tb)
-#pragma unroll 4
-                for (int e = t.tid; e < KC * 32; e += TT) {
-                    const int c = e & 31, k = e >> 5;   // B [K][N]: consecutive threads walk N
-                    const int64_t gn = n0 + c, gk = k0 + k;
-                    Bs[k][c] = (gn < N && gk < K) ? Bb[gk * N + gn] : 0.f;
+                ra[i] = (gm < M && gk < K) ? Ab[gm * K + gk] : 0.f;
+                if (tb) {
+                    const int64_t gn = n0 + r;
+                    rb[i] = (gn < N && gk < K) ? Bb[gn * K + gk] : 0.f;
+                } else {
+                    const int c = e & 31, kk = e >> 5;   // B [K][N]: consecutive threads walk N
+                    const int64_t gn = n0 + c, gk2 = k0 + kk;
+                    rb[i] = (gn < N && gk2 < K) ? Bb[gk2 * N + gn] : 0.f;
                 }
+            }
+#pragma unroll
+            for (int i = 0; i < PER; i++) {
+                const int e = t.tid + i * TT;
+                As[e % KC][e / KC] = ra[i];
+                if (tb) Bs[e % KC][e / KC] = rb[i];
+                else Bs[e >> 5][e & 31] = rb[i];
+            }
             __syncthreads();
             const int kmax = (int)min((int64_t)KC, K - k0);
             for (int k = 0; k < kmax; k++) {
@@ -233,6 +244,21 @@ __device__ void attention_d(const OpNode& n, const Th& t, float* sm) {
         const float* q = Q + bh * S * D;
         const float* k = Kp + (bh / group) * S * D;
         const float* v = V + (bh / group) * S * D;
+        if (S * S + 3 * S * D <= TSMEM / 4) {   // the head's Q, K, V staged in shared memory first
+            float* sq = sm + S * S;
+            float* sk = sq + S * D;
+            float* svv = sk + S * D;
+            for (int e = t.tid; e < S * D; e += TT) {
+                const float a = q[e], b = k[e], c = v[e];
+                sq[e] = a;
+                sk[e] = b;
+                svv[e] = c;
+            }
+            __syncthreads();
+            q = sq;
+            k = sk;
+            v = svv;
+        }
         for (int e = t.tid; e < S * S; e += TT) {
             const int i = e / S, j = e % S;
             float dot = 0.f;
