@@ -911,8 +911,13 @@ void plan_gemm_chains(const Analysis& an, const Effective& e, std::vector<PlanIt
         items[g].epi_out = un.output;
         if (dbg()) fprintf(stderr, "[fusion] gemm %d: GELU %d folded into the epilogue\n", g, u);
 
+        // The hand-off: default on under the fp16 scheme (the plane and its
+        // per-(row, 128 columns) scales replace the fp32 output, and the
+        // consumer's split pass goes); opt-in (RT_FUSE_HANDOFF=1) for the
+        // tf32 schemes, where it measured no faster.
         const char* hv = getenv("RT_FUSE_HANDOFF");   // read per plan
-        if (!(hv && hv[0] == '1') || !gemm_planes_from_epilogues()) continue;
+        const bool f16 = gemm_scheme() == 2;
+        if (f16 ? (hv && hv[0] == '0') : !(hv && hv[0] == '1')) continue;
         const int k = next_reader(u, U);
         if (k < 0) continue;
         const OpNode& kn = an.nodes[k];
@@ -920,17 +925,21 @@ void plan_gemm_chains(const Analysis& an, const Effective& e, std::vector<PlanIt
         GemmProblem gp, kp;
         if (!decode_gemm(gn, &gp).good() || !decode_gemm(kn, &kp).good()) continue;
         if ((uintptr_t)(kp.batches * kp.M * kp.K * 4) != U.hi - U.lo || kp.K != gp.N || kp.K % 4 != 0 ||
-            kp.batches * kp.M != gp.batches * gp.M)
+            kp.batches * kp.M != gp.batches * gp.M || (f16 && kp.K % 128 != 0))
             continue;
         bool only_a = true;
         for (size_t i = 1; i < e.reads[k].size(); i++) only_a &= !overlaps(e.reads[k][i], U);
         if (!only_a || !dead_output(an, u, k, protect)) continue;
+        // fp16: one plane of 4 bytes per element, then a float per 128 columns
         const int64_t plane = (int64_t)(((U.hi - U.lo) + 255) & ~(uintptr_t)255);
-        const int64_t off = carry_alloc.take(g, k, 2 * plane);
+        const int64_t second = f16 ? (int64_t)(((uintptr_t)(kp.batches * kp.M * (kp.K / 128) * 4) + 255) & ~(uintptr_t)255)
+                                   : plane;
+        const int64_t off = carry_alloc.take(g, k, plane + second);
         items[g].carry_off = off;
         items[g].carry_plane_bytes = plane;
         items[k].presplit_off = off;
-        items[k].carry_plane_bytes = plane;
+        items[k].presplit_seg = f16;
+        items[k].presplit_plane_bytes = plane;
         if (dbg()) fprintf(stderr, "[fusion] gemm %d: writes the split A operand of gemm %d\n", g, k);
     }
 }
@@ -1031,7 +1040,7 @@ void plan_norm_handoffs(const Analysis& an, const Effective& e, std::vector<Plan
         it.norm_planes_off = off;
         it.carry_plane_bytes = plane;
         ki.presplit_off = off;
-        ki.carry_plane_bytes = plane;
+        ki.presplit_plane_bytes = plane;
         if (dbg()) fprintf(stderr, "[fusion] norm %d: writes the split A operand of gemm %d\n", m, k);
     }
 }
@@ -1109,7 +1118,7 @@ void plan_attn_handoffs(const Analysis& an, const Effective& e, std::vector<Plan
         it.attn_planes_off = off;
         it.carry_plane_bytes = plane;
         ki.presplit_off = off;
-        ki.carry_plane_bytes = plane;
+        ki.presplit_plane_bytes = plane;
         if (dbg()) fprintf(stderr, "[fusion] attention %d: writes the split A operand of gemm %d\n", a, k);
     }
 }

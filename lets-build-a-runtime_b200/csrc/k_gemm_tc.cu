@@ -116,7 +116,11 @@ struct TcParams {
     const float* b_scale;         // fp16 scheme: 2^-e of the whole B operand (one float); null = 1
     float* plane_hi;              // non-null: write the result as split A planes (hi, plane 1) of a
     uint8_t* plane_x;             //   later GEMM instead of C (row-major [batches*M][N])
-    int plane_mode;               //   plane 1: 0 = lo (fp32), 1 = cross (bf16 [hi | lo] per 16 block)
+    int plane_mode;               //   plane 1: 0 = lo (fp32), 1 = cross (bf16 [hi | lo] per 16 block);
+                                  //   2 = fp16 plane at plane_hi ([h | l] per 16 block, 2N halves per row)
+                                  //   and 2^-e per 128-column segment at plane_x ([rows][N / 128] floats)
+    const float* a_seg;           // A arrived as an fp16 plane with 2^-e per (row, 128 K): one TMEM chunk
+    int a_segs;                   //   of 128 K per segment; a_segs = segments per row
     int* err;
 };
 
@@ -156,6 +160,11 @@ __device__ __forceinline__ float epi_factor(const TcParams& p, int64_t row, int 
     if (p.b_scale) f *= *p.b_scale;
     return f;
 }
+// A given as an fp16 plane with one 2^-e per (row, 128-wide K segment): the
+// row's segment factors (one TMEM chunk spans one segment), or null.
+__device__ __forceinline__ const float* seg_row(const TcParams& p, int64_t row, int bz) {
+    return p.a_seg && row < p.M ? p.a_seg + ((int64_t)bz * p.M + row) * p.a_segs : nullptr;
+}
 
 // One epilogue row: COLS consecutive columns from col0 of output row `row`
 // (within batch bz), accumulator already scaled by epi_factor: bias (first
@@ -164,11 +173,48 @@ __device__ __forceinline__ float epi_factor(const TcParams& p, int64_t row, int 
 // split A planes (a separate instantiation: the plane code's registers would
 // otherwise cost every GEMM's epilogue).
 template <int COLS, bool PLANES, bool RESID = true>
-__device__ __forceinline__ void store_row(const TcParams& p, int64_t row, int bz, int col0, const float* acc,
+__device__ __forceinline__ void store_row(const TcParams& p, int64_t row, int bz, int col0, float* acc,
                                           bool first_split, bool res_in_acc) {
     const bool add_bias = p.bias && first_split;
     const bool add_res = RESID && p.res && first_split && !res_in_acc;   // RESID: compiled in at all
     const int64_t r = (int64_t)bz * p.M + row;
+    if (PLANES && COLS == 128 && p.plane_mode == 2) {
+        // fp16 plane of the consuming GEMM's A: this thread's 128 columns are
+        // one 128-wide K segment of that GEMM, scaled by their own maximum
+        // (N % 128 == 0 here, so a segment is whole or past the end)
+        if (col0 >= p.N) return;
+        float m = 0.0f;
+#pragma unroll
+        for (int j = 0; j < COLS; j++) {
+            float x = acc[j];
+            if (add_bias) x += p.bias[col0 + j];
+            if (p.act == 1) x = gelu_tanh(x);
+            acc[j] = x;
+            m = fmaxf(m, fabsf(x));
+        }
+        const int e = f16_scale_exp(m);
+        const float sc = pow2i(e);
+        reinterpret_cast<float*>(p.plane_x)[r * (p.N / 128) + col0 / 128] = pow2i(-e);
+        uint16_t* prow = reinterpret_cast<uint16_t*>(p.plane_hi) + r * 2 * (int64_t)p.N;
+        // one 16-column block = 64 bytes: 16 h halves, then 16 l halves
+#pragma unroll
+        for (int j = 0; j < COLS; j += 16) {
+            uint32_t hw[8], lw[8];
+#pragma unroll
+            for (int t = 0; t < 16; t += 2) {
+                const float x0 = acc[j + t] * sc, x1 = acc[j + t + 1] * sc;
+                const float h0 = round11(x0), h1 = round11(x1);
+                hw[t / 2] = f16x2_rn(h0, h1);
+                lw[t / 2] = f16x2_rn(x0 - h0, x1 - h1);
+            }
+            uint4* blk = reinterpret_cast<uint4*>(prow + (int64_t)(col0 + j) * 2);
+            blk[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            blk[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+            blk[2] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+            blk[3] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+        }
+        return;
+    }
     if (PLANES) {
         // N % 4 == 0 here (it is the K of the consuming GEMM); splits == 1
         float* hrow = p.plane_hi + r * p.N;
@@ -450,9 +496,13 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
             tile_coords(p, t, m_blk, n_blk, bz, kb_lo, kb_hi);
             const int n_chunks = (kb_hi - kb_lo + p.kb_per_chunk - 1) / p.kb_per_chunk;
             const bool first_split = kb_lo == 0;
-            const float fac = epi_factor(p, (int64_t)m_blk * BM + quarter * 32 + lane, bz);
+            const int64_t erow = (int64_t)m_blk * BM + quarter * 32 + lane;
+            const float fac = epi_factor(p, erow, bz);
+            const float* segp = seg_row(p, erow, bz);
+            const int seg0 = kb_lo / p.kb_per_chunk;
             float acc[EPI_COLS];
             for (int c = 0; c < n_chunks; c++, it++) {
+                const float fc = segp ? fac * segp[seg0 + c] : fac;
                 int b = it & 1;
                 uint32_t acc_phase = (it >> 1) & 1;
                 // warp-uniform outcome: the stores below are warp-collective
@@ -472,8 +522,8 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
                     ptx::tmem_ld_wait();
 #pragma unroll
                     for (int j = 0; j < 16; j++)
-                        acc[q * 16 + j] = c == 0 ? fac * __uint_as_float(r[j])
-                                                 : fmaf(fac, __uint_as_float(r[j]), acc[q * 16 + j]);
+                        acc[q * 16 + j] = c == 0 ? fc * __uint_as_float(r[j])
+                                                 : fmaf(fc, __uint_as_float(r[j]), acc[q * 16 + j]);
                 }
                 ptx::tc_fence_before();
                 ptx::mbar_arrive(&acc_empty[b]);
@@ -718,7 +768,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             tile_coords(p, t, m_blk, n_blk, bz, kb_lo, kb_hi);
             const int n_chunks = (kb_hi - kb_lo + p.kb_per_chunk - 1) / p.kb_per_chunk;
             const bool first_split = kb_lo == 0;
-            const float fac = epi_factor(p, (int64_t)m_blk * 256 + rank * 128 + quarter * 32 + lane, bz);
+            const int64_t erow = (int64_t)m_blk * 256 + rank * 128 + quarter * 32 + lane;
+            const float fac = epi_factor(p, erow, bz);
+            const float* segp = seg_row(p, erow, bz);
+            const int seg0 = kb_lo / p.kb_per_chunk;
             float acc[P_EPI_COLS];
             // RES: a folded residual preloaded into the accumulator registers
             // (zeros on a second split); the TMEM chunks add to it
@@ -729,6 +782,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 #pragma unroll
                 for (int j = 0; j < P_EPI_COLS; j++) acc[j] = 0.0f;
             for (int c = 0; c < n_chunks; c++, it++) {
+                const float fc = segp ? fac * segp[seg0 + c] : fac;
                 const int b = it & 1;
                 const uint32_t acc_phase = (it >> 1) & 1;
                 // warp-uniform outcome: the stores below are warp-collective
@@ -748,8 +802,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                     ptx::tmem_ld_wait();
 #pragma unroll
                     for (int j = 0; j < 16; j++)
-                        acc[q * 16 + j] = c == 0 && !RES ? fac * __uint_as_float(r[j])
-                                                         : fmaf(fac, __uint_as_float(r[j]), acc[q * 16 + j]);
+                        acc[q * 16 + j] = c == 0 && !RES ? fc * __uint_as_float(r[j])
+                                                         : fmaf(fc, __uint_as_float(r[j]), acc[q * 16 + j]);
                 }
                 ptx::tc_fence_before();
                 __syncwarp();
@@ -1170,14 +1224,17 @@ cudaError_t for_each_kernel(F f) {
         (const void*)tc_gemm_kernel<256, SCH_3XTF32, true>, (const void*)tc_gemm_kernel<256, SCH_CROSS, true>,
         (const void*)tc_gemm_kernel<128, SCH_3XTF32, false>, (const void*)tc_gemm_kernel<128, SCH_CROSS, false>,
         (const void*)tc_gemm_kernel<128, SCH_F16, false>,
-        (const void*)tc_gemm_kernel<128, SCH_3XTF32, true>, (const void*)tc_gemm_kernel<128, SCH_CROSS, true>};
+        (const void*)tc_gemm_kernel<128, SCH_3XTF32, true>, (const void*)tc_gemm_kernel<128, SCH_CROSS, true>,
+        (const void*)tc_gemm_pair_kernel<SCH_F16, true>, (const void*)tc_gemm_kernel<256, SCH_F16, true>,
+        (const void*)tc_gemm_kernel<128, SCH_F16, true>};
     const int smem[] = {P0, P1, P2, P0, P1, P0, P1, P2, P0, P1, P2,
                         GCfg<256, SCH_3XTF32>::SMEM_BYTES, GCfg<256, SCH_CROSS>::SMEM_BYTES,
                         GCfg<256, SCH_F16>::SMEM_BYTES, GCfg<256, SCH_3XTF32>::SMEM_BYTES,
                         GCfg<256, SCH_CROSS>::SMEM_BYTES,
                         GCfg<128, SCH_3XTF32>::SMEM_BYTES, GCfg<128, SCH_CROSS>::SMEM_BYTES,
                         GCfg<128, SCH_F16>::SMEM_BYTES, GCfg<128, SCH_3XTF32>::SMEM_BYTES,
-                        GCfg<128, SCH_CROSS>::SMEM_BYTES};
+                        GCfg<128, SCH_CROSS>::SMEM_BYTES, P2, GCfg<256, SCH_F16>::SMEM_BYTES,
+                        GCfg<128, SCH_F16>::SMEM_BYTES};
     static_assert(sizeof(ks) / sizeof(ks[0]) == sizeof(smem) / sizeof(smem[0]), "kernel table");
     for (size_t i = 0; i < sizeof(ks) / sizeof(ks[0]); i++) {
         cudaError_t e = f(ks[i], smem[i]);
@@ -1201,7 +1258,8 @@ void launch_tc_t(bool pair, int BN, int grid, const TcParams& prm, cudaStream_t 
         tc_gemm_kernel<256, SCH, PLANES><<<grid, THREADS, GCfg<256, SCH>::SMEM_BYTES, st>>>(prm);
 }
 void launch_tc(bool pair, int BN, int sch, bool planes, int grid, const TcParams& prm, cudaStream_t st) {
-    if (sch == SCH_F16) launch_tc_t<SCH_F16, false>(pair, BN, grid, prm, st);   // (no split-plane output)
+    if (sch == SCH_F16 && planes) launch_tc_t<SCH_F16, true>(pair, BN, grid, prm, st);
+    else if (sch == SCH_F16) launch_tc_t<SCH_F16, false>(pair, BN, grid, prm, st);
     else if (sch == SCH_CROSS && planes) launch_tc_t<SCH_CROSS, true>(pair, BN, grid, prm, st);
     else if (sch == SCH_CROSS) launch_tc_t<SCH_CROSS, false>(pair, BN, grid, prm, st);
     else if (planes) launch_tc_t<SCH_3XTF32, true>(pair, BN, grid, prm, st);
@@ -1326,6 +1384,8 @@ Status tc_gemm_prepare(const GemmProblem& p, cudaStream_t st, int gate) {
     return r;
 }
 
+static bool prm_planes_out(const GemmFusion* f) { return f && f->plane_hi; }
+
 Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* launches,
                       const GemmFusion* f) {
     if (p.M == 0) return Status::ok();
@@ -1333,8 +1393,12 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
     if (f && f->plane_hi && p.N % 4 != 0) return Status::err(RT_ERR_ARGUMENT, "gemm: split-plane output needs N % 4 == 0");
     const int sch = scheme();
     const bool f16 = sch == SCH_F16;
-    if (f16 && f && f->plane_hi)
-        return Status::err(RT_ERR_ARGUMENT, "gemm: the fp16 scheme takes no split-plane output");
+    // fp16 scheme hand-offs: the output as the next GEMM's fp16 plane with
+    // one scale per (row, 128 columns); an A operand given in that form
+    if (f16 && f && f->plane_hi && p.N % 128 != 0)
+        return Status::err(RT_ERR_ARGUMENT, "gemm: fp16 plane output needs N % 128 == 0");
+    const bool a_seg = f16 && f && f->pre_hi && f->pre_seg;
+    if (a_seg && p.K % 128 != 0) return Status::err(RT_ERR_ARGUMENT, "gemm: a segment-scaled A needs K % 128 == 0");
     const size_t abytes = round256(plane_bytes(p.batches, p.M, p.K));
     const size_t a2bytes = f16 ? a_scale_bytes(p) : abytes;   // second A region: scales or plane 1
     const void *a_hi, *a_lo;
@@ -1357,7 +1421,7 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
         a_hi = ah;
         a_lo = al;
     }
-    if (f16) a_scale = static_cast<const float*>(a_lo);
+    if (f16 && !a_seg) a_scale = static_cast<const float*>(a_lo);
     const int gate = f ? f->gate : 0;
     if (gate && (!b_is_constant(p) || p.N % 256 != 0))
         return Status::err(RT_ERR_ARGUMENT, "gemm: a gated epilogue needs a constant B with N % 256 == 0");
@@ -1388,7 +1452,7 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
         const char* e = getenv("RT_GEMM_BN");
         return e ? atoi(e) : 0;
     }();
-    const int BN = bn_force == 128 ? 128 : 256;
+    const int BN = bn_force == 128 && !(f16 && prm_planes_out(f)) ? 128 : 256;
     if (gate && BN != 256) return Status::err(RT_ERR_ARGUMENT, "gemm: a gated epilogue needs 256-wide N tiles");
     // CTA pairs (256x256 tiles) whenever A has more than one 128-row block.
     const bool pair = BN == 256 && p.M > BM && pair_enabled();
@@ -1408,6 +1472,8 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
     }
     prm.a_scale = a_scale;
     prm.b_scale = b_scale;
+    prm.a_seg = a_seg ? static_cast<const float*>(a_lo) : nullptr;
+    prm.a_segs = a_seg ? (int)(p.K / 128) : 0;
     prm.c = f && f->out ? f->out : p.c;
     prm.bias = f && f->bias ? f->bias : p.bias;
     prm.res = f ? f->res : nullptr;
@@ -1422,7 +1488,7 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
         return Status::err(RT_ERR_ARGUMENT, "gemm: a gated epilogue takes no bias, residual, alpha or other activation");
     prm.plane_hi = f ? f->plane_hi : nullptr;
     prm.plane_x = f ? static_cast<uint8_t*>(f->plane_x) : nullptr;
-    prm.plane_mode = a_mode();
+    prm.plane_mode = f16 ? 2 : a_mode();
     prm.M = (int)p.M;
     prm.N = (int)p.N;
     prm.K = (int)p.K;
@@ -1431,7 +1497,8 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
     prm.m_tiles = (int)((p.M + tile_m - 1) / tile_m);
     prm.n_tiles = (int)((p.N + BN - 1) / BN);
     prm.k_blocks = (int)((p.K + bk - 1) / bk);
-    prm.kb_per_chunk = k_chunk() / bk > 0 ? k_chunk() / bk : 1;
+    // (a segment-scaled A: one chunk per 128-wide segment)
+    prm.kb_per_chunk = a_seg ? 128 / bk : k_chunk() / bk > 0 ? k_chunk() / bk : 1;
     prm.n_chunks = (prm.k_blocks + prm.kb_per_chunk - 1) / prm.kb_per_chunk;
     int64_t total = (int64_t)prm.m_tiles * prm.n_tiles * p.batches;
     if (total > INT32_MAX / 2) return Status::err(RT_ERR_UNSUPPORTED, "gemm: too many tiles");
@@ -1462,6 +1529,7 @@ Status tc_gemm_launch(const GemmProblem& p, cudaStream_t st, Workspace ws, int* 
     }
     // equal halves of the K blocks (each split accumulates its own TMEM chunks)
     prm.kb_split = (prm.k_blocks + prm.splits - 1) / prm.splits;
+    if (a_seg) prm.kb_split = (prm.kb_split + prm.kb_per_chunk - 1) / prm.kb_per_chunk * prm.kb_per_chunk;
     prm.total_items = prm.total_tiles * prm.splits;
     // Opt-in (RT_GEMM_TMA_STORE=1): C through shared memory and TMA stores
     // (pair kernel, plain C output, no split-K).  Alone, the 8192 x 2304 and

@@ -85,6 +85,8 @@ struct GemmFusion {
     void* plane_x = nullptr;
     const float* pre_hi = nullptr;  // this GEMM's A, already split
     const void* pre_x = nullptr;
+    bool pre_seg = false;           // fp16 scheme: pre_x holds 2^-e per (row, 128 K) (a GEMM producer's
+                                    // epilogue), not per row (a norm's)
     const float* bias = nullptr;    // bias to add (a node without one: a folded bias)
     const float* res = nullptr;     // residual added after the bias (same layout as C): a folded ADD
     int gate = 0;                   // 1 / 2: a folded GATED_ACT (SiLU / tanh-GELU): B's rows are taken in
@@ -183,7 +185,10 @@ struct PlanItem {
     void* epi_out = nullptr;
     int64_t carry_off = -1;        // producer: write A planes here (byte offset into the carry buffer)
     int64_t presplit_off = -1;     // consumer: A planes are already here; no split pre-pass
-    int64_t carry_plane_bytes = 0; // bytes of one plane
+    bool presplit_seg = false;     //   fp16 scheme, written by a GEMM epilogue: scales per (row, 128 K)
+    int64_t carry_plane_bytes = 0; // producer: bytes of the first plane it writes at carry_off / norm_planes_off / attn_planes_off
+    int64_t presplit_plane_bytes = 0;  // consumer: bytes of the first plane at presplit_off (a GEMM can
+                                       // both read split planes and write the next GEMM's)
     int64_t norm_planes_off = -1;  // LAYERNORM / RMSNORM: write the consumer GEMM's split A planes here
     int64_t attn_planes_off = -1;  // ATTENTION (merged-layout views): the same, from its O store
     int64_t epi_bias_off = -1;     // GEMM adds this merged bias (byte offset into the plan's bias buffer)

@@ -345,7 +345,8 @@ Status launch_item(Plan& p, size_t i, cudaStream_t st, int* launches) {
             }
             if (it.presplit_off >= 0) {
                 f.pre_hi = reinterpret_cast<const float*>(p.carry + it.presplit_off);
-                f.pre_x = p.carry + it.presplit_off + it.carry_plane_bytes;
+                f.pre_x = p.carry + it.presplit_off + it.presplit_plane_bytes;
+                f.pre_seg = it.presplit_seg;
             }
             OpNode n = p.nodes[i];
             if (it.redirect_slot >= 0) n.inputs[it.redirect_slot] = it.redirect_ptr;

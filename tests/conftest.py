@@ -29,10 +29,18 @@ def gemm_scheme() -> str:
     return "cross" if os.environ.get("RT_GEMM_SCHEME") == "cross" else "f16"
 
 
-# Split-plane hand-offs from a GEMM or attention epilogue (RT_FUSE_HANDOFF,
-# RT_FUSE_ATTN_SPLIT) exist for the tf32 plane schemes only; under the fp16
-# scheme they are never planned.
+# Split-plane hand-offs from an attention epilogue (RT_FUSE_ATTN_SPLIT) exist
+# for the tf32 plane schemes only; under the fp16 scheme they are never planned.
 PLANE_HANDOFFS = gemm_scheme() != "f16"
+
+
+def gemm_handoff(env: str | None, K: int) -> bool:
+    """Whether a GELU-epilogue GEMM hands its output to the next GEMM as that
+    GEMM's split A operand: default on under the fp16 scheme (K % 128 == 0:
+    one scale per 128-wide segment), opt-in (RT_FUSE_HANDOFF=1) otherwise."""
+    if gemm_scheme() == "f16":
+        return env != "0" and K % 128 == 0
+    return env == "1" and K % 4 == 0
 
 
 def pytest_configure(config):

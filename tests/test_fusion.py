@@ -10,7 +10,7 @@ import ctypes
 
 import pytest
 
-from conftest import GOLDEN, PLANE_HANDOFFS
+from conftest import GOLDEN, PLANE_HANDOFFS, gemm_handoff
 from lbr_b200.copnode import build_node_array
 from lbr_b200.executor import load_library
 from lbr_b200.program import OP, Program
@@ -66,11 +66,21 @@ def test_gemm_gelu_gemm_chain_hands_over_split_operand(monkeypatch):
     for u in gelus:
         assert flags[u] == 1
         assert flags[u - 1] == 3 and prog.nodes[u - 1].op == OP["MATMUL_ADD"]
-        assert flags[u + 1] == (4 if PLANE_HANDOFFS else 0) and prog.nodes[u + 1].op == OP["MATMUL_ADD"]
+        assert flags[u + 1] == (4 if gemm_handoff("1", 3072) else 0) and prog.nodes[u + 1].op == OP["MATMUL_ADD"]
 
 
-def test_gelu_folds_without_hand_off_by_default(monkeypatch):
+def test_gelu_fold_hand_off_default(monkeypatch):
+    """By default the hand-off is planned under the fp16 scheme only."""
     monkeypatch.delenv("RT_FUSE_HANDOFF", raising=False)
+    prog = Program.load(GOLDEN / "gpt2_b8.json")
+    arr, _ = bind(prog)
+    _, flags = report(prog, arr)
+    for u in [i for i, nd in enumerate(prog.nodes) if nd.op == OP["GELU"]]:
+        assert flags[u - 1:u + 2] == [3, 1, 4 if gemm_handoff(None, 3072) else 0]
+
+
+def test_gelu_fold_without_hand_off(monkeypatch):
+    monkeypatch.setenv("RT_FUSE_HANDOFF", "0")
     prog = Program.load(GOLDEN / "gpt2_b8.json")
     arr, _ = bind(prog)
     _, flags = report(prog, arr)
@@ -90,7 +100,7 @@ def test_protected_gelu_output_keeps_the_hand_off_out(monkeypatch):
     prog.nodes = prog.nodes[:u + 2]
     arr, res = bind(prog)
     _, flags = report(prog, arr)
-    assert flags[u - 1:u + 2] == [3, 1, 4 if PLANE_HANDOFFS else 0]
+    assert flags[u - 1:u + 2] == [3, 1, 4 if gemm_handoff("1", 3072) else 0]
     nbytes = 4
     for d in prog.nodes[u].out_shape:
         nbytes *= d

@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 
 import oracle
-from conftest import GOLDEN, PLANE_HANDOFFS
+from conftest import GOLDEN, PLANE_HANDOFFS, gemm_handoff
 from lbr_b200.program import OP, ConstSpec, ProgNode, Program, Ref
 
 pytestmark = pytest.mark.gpu
@@ -46,7 +46,8 @@ def flags_of(ex, prog):
     return list(f)
 
 
-@pytest.mark.parametrize("M,D,F", [(1024, 256, 1024), (300, 192, 520), (640, 128, 1028)])
+@pytest.mark.parametrize("M,D,F", [(1024, 256, 1024), (300, 192, 520), (640, 128, 1028), (300, 192, 1024),
+                                   (100, 256, 512), (256, 256, 4096)])
 @pytest.mark.parametrize("kind,handoff", [(1, "0"), (2, "0"), (2, "1")])
 def test_fused_chain_matches_oracle(M, D, F, kind, handoff, gpu_executor_factory, monkeypatch):
     monkeypatch.setenv("RT_FUSE_HANDOFF", handoff)
@@ -56,7 +57,7 @@ def test_fused_chain_matches_oracle(M, D, F, kind, handoff, gpu_executor_factory
     flags = flags_of(ex, prog)
     assert flags[:2] == [3, 1]                       # GELU folded into the first GEMM
     if kind == 2:
-        assert flags[2] == (4 if handoff == "1" and PLANE_HANDOFFS else 0)   # A operand handed over: no split pass
+        assert flags[2] == (4 if gemm_handoff(handoff, F) else 0)   # A operand handed over: no split pass
     ref = oracle.run_program("restated", prog, dict(prog.stored), {})[name]
     np.testing.assert_allclose(got, ref, atol=1e-4, rtol=1e-3)
 
