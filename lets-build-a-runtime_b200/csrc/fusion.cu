@@ -869,8 +869,8 @@ struct CarryAlloc {
 //   GEMM g -> GELU u: g applies the GELU and writes u's output; u is skipped.
 //   ... -> GEMM k reading u's output as its A operand: g writes k's split A
 //   planes (carry buffer) instead, k skips its split pass (opt-in,
-//   RT_FUSE_HANDOFF=1: the plane stores currently cost the first GEMM more
-//   than the second one saves).
+//   RT_FUSE_HANDOFF=1: the plane stores cost the first GEMM more than the
+//   second one saves, under every scheme).
 // Conditions mirror the layout folds: g's output is read by u alone and is
 // not a graph output; nothing between g and u touches u's output, which g
 // now writes earlier (and g's own operands do not overlap it); for the
@@ -911,13 +911,14 @@ void plan_gemm_chains(const Analysis& an, const Effective& e, std::vector<PlanIt
         items[g].epi_out = un.output;
         if (dbg()) fprintf(stderr, "[fusion] gemm %d: GELU %d folded into the epilogue\n", g, u);
 
-        // The hand-off: default on under the fp16 scheme (the plane and its
-        // per-(row, 128 columns) scales replace the fp32 output, and the
-        // consumer's split pass goes); opt-in (RT_FUSE_HANDOFF=1) for the
-        // tf32 schemes, where it measured no faster.
+        // The hand-off (opt-in, RT_FUSE_HANDOFF=1).  Under the fp16 scheme
+        // the plane and its per-(row, 128 columns) scales replace the fp32
+        // output and the consumer's split pass goes, but the plane epilogue
+        // holds up the producer's MMAs (the next tile's accumulator waits on
+        // the stores): 1B-8K FFN pair 1282 -> 1307 us, GPT-2 258 -> 305 us.
         const char* hv = getenv("RT_FUSE_HANDOFF");   // read per plan
         const bool f16 = gemm_scheme() == 2;
-        if (f16 ? (hv && hv[0] == '0') : !(hv && hv[0] == '1')) continue;
+        if (!(hv && hv[0] == '1')) continue;
         const int k = next_reader(u, U);
         if (k < 0) continue;
         const OpNode& kn = an.nodes[k];

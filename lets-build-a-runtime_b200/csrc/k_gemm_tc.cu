@@ -581,7 +581,8 @@ constexpr int P_EPI_STAGE = 32 * 32 * 4;               // per epilogue warp: 32 
 constexpr int P_EPI_OFF = P_STAGES * P_STAGE_BYTES + 1024;   // after the barriers, 1024-aligned
 constexpr int P_SMEM_BYTES = P_EPI_OFF + 8 * P_EPI_STAGE + 1024;
 static_assert(P_SMEM_BYTES <= 232448, "shared memory budget");
-constexpr int P_EPI_COLS = 128;
+constexpr int P_EPI_COLS = 128;   // (two 16-column TMEM loads per wait measured 20-35 % slower:
+                                   //  the register cap of 168 leaves no room for them)
 
 template <int SCH, bool PLANES, bool RES = false, bool TMA = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
@@ -1032,6 +1033,47 @@ __global__ void split16_rows_kernel(const float* __restrict__ x, uint16_t* __res
     }
 }
 
+// Long rows (1024 < K16 <= 8192, 16-byte aligned, K % 4 == 0): one row per
+// 256-thread block iteration, held in registers (V4 float4 per thread), so
+// it is read from memory once -- the warp-per-row kernel above reads it twice
+// (maximum, then planes) and keeps only a few loads in flight per warp.
+template <int V4>
+__global__ void __launch_bounds__(256) split16_rows_block_kernel(const float* __restrict__ x,
+                                                                 uint16_t* __restrict__ plane,
+                                                                 float* __restrict__ scale, int64_t rows, int K,
+                                                                 int K16) {
+    __shared__ float red[8];
+    const int t = threadIdx.x, lane = t & 31, w = t >> 5;
+    for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+        const float4* xr = reinterpret_cast<const float4*>(x + row * K);
+        float4 v[V4];
+        float m = 0.0f;
+#pragma unroll
+        for (int i = 0; i < V4; i++) {
+            const int c = t + i * 256;
+            v[i] = c < K / 4 ? xr[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+            m = fmaxf(m, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+        }
+        m = warp_max_f(m);
+        if (lane == 0) red[w] = m;
+        __syncthreads();
+        m = red[0];
+#pragma unroll
+        for (int j = 1; j < 8; j++) m = fmaxf(m, red[j]);
+        __syncthreads();   // red is rewritten by the next row
+        const int e = f16_scale_exp(m);
+        const float sc = pow2i(e);
+        if (t == 0) scale[row] = pow2i(-e);
+        uint16_t* pr = plane + row * (2 * (int64_t)K16);
+#pragma unroll
+        for (int i = 0; i < V4; i++) {
+            const int c = t + i * 256;
+            if (c < K16 / 4)
+                store_f16x4(pr, 4 * c, make_float4(v[i].x * sc, v[i].y * sc, v[i].z * sc, v[i].w * sc), true);
+        }
+    }
+}
+
 // [batches][K][N] -> plane rows of the transpose ([batches][N][2*K16]), one
 // scale for the whole operand (tensor_max).
 __global__ void split16_transpose_kernel(const float* __restrict__ x, uint16_t* __restrict__ plane, int K, int N,
@@ -1063,10 +1105,22 @@ int64_t k16_of(int64_t K) { return (K + 15) / 16 * 16; }
 // A operand: per-row scales into scale[batches*rows].
 Status run_split16_rows(const float* x, uint16_t* plane, float* scale, int64_t rows, int64_t K, cudaStream_t st) {
     const bool vec = aligned16(x) && K % 4 == 0;
+    const int64_t K16 = k16_of(K);
+    if (rows == 0) return Status::ok();
+    if (vec && K16 > 1024 && K16 <= 8192) {
+        const int grid = (int)std::min<int64_t>(rows, (int64_t)g_num_sms * 8);
+        if (K16 <= 2048)
+            split16_rows_block_kernel<2><<<grid, 256, 0, st>>>(x, plane, scale, rows, (int)K, (int)K16);
+        else if (K16 <= 4096)
+            split16_rows_block_kernel<4><<<grid, 256, 0, st>>>(x, plane, scale, rows, (int)K, (int)K16);
+        else
+            split16_rows_block_kernel<8><<<grid, 256, 0, st>>>(x, plane, scale, rows, (int)K, (int)K16);
+        RT_LAUNCH_CHECK();
+        return Status::ok();
+    }
     const int64_t blocks = (rows + 7) / 8;
     const int grid = (int)std::min<int64_t>(blocks, (int64_t)g_num_sms * 8);
-    if (grid == 0) return Status::ok();
-    split16_rows_kernel<<<grid, 256, 0, st>>>(x, plane, scale, rows, (int)K, (int)k16_of(K), nullptr, true, vec);
+    split16_rows_kernel<<<grid, 256, 0, st>>>(x, plane, scale, rows, (int)K, (int)K16, nullptr, true, vec);
     RT_LAUNCH_CHECK();
     return Status::ok();
 }

@@ -36,11 +36,9 @@ PLANE_HANDOFFS = gemm_scheme() != "f16"
 
 def gemm_handoff(env: str | None, K: int) -> bool:
     """Whether a GELU-epilogue GEMM hands its output to the next GEMM as that
-    GEMM's split A operand: default on under the fp16 scheme (K % 128 == 0:
-    one scale per 128-wide segment), opt-in (RT_FUSE_HANDOFF=1) otherwise."""
-    if gemm_scheme() == "f16":
-        return env != "0" and K % 128 == 0
-    return env == "1" and K % 4 == 0
+    GEMM's split A operand (opt-in, RT_FUSE_HANDOFF=1): under the fp16 scheme
+    when K % 128 == 0 (one scale per 128-wide segment), else when K % 4 == 0."""
+    return env == "1" and K % (128 if gemm_scheme() == "f16" else 4) == 0
 
 
 def pytest_configure(config):

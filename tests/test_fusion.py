@@ -70,7 +70,7 @@ def test_gemm_gelu_gemm_chain_hands_over_split_operand(monkeypatch):
 
 
 def test_gelu_fold_hand_off_default(monkeypatch):
-    """By default the hand-off is planned under the fp16 scheme only."""
+    """The hand-off is opt-in."""
     monkeypatch.delenv("RT_FUSE_HANDOFF", raising=False)
     prog = Program.load(GOLDEN / "gpt2_b8.json")
     arr, _ = bind(prog)
