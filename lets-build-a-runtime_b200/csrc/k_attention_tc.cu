@@ -262,13 +262,15 @@ __device__ __forceinline__ void put_f16_b4(uint8_t* blk, int row, int e, float4 
 }
 
 // |V| maximum per kv head into vmax[h] (zeroed first; float bits).
-__global__ void __launch_bounds__(256) v_absmax_kernel(KvViews kv, int S, int D, unsigned* __restrict__ vmax) {
+template <int D>
+__global__ void __launch_bounds__(256) v_absmax_kernel(KvViews kv, int S, unsigned* __restrict__ vmax) {
     const int h = blockIdx.y, bb = h / kv.Hkv, hh = h % kv.Hkv;
     const float* vb = kv.v + bb * kv.v_sb + hh * kv.v_sh;
     float m = 0.0f;
+#pragma unroll 4
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < (int64_t)S * D / 4;
          i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t key = i / (D / 4), d = (i % (D / 4)) * 4;
+        const int64_t key = i / (D / 4), d = (i % (D / 4)) * 4;   // (D a constant: shifts)
         const float4 x = *reinterpret_cast<const float4*>(vb + key * kv.v_ss + d);
         m = fmaxf(m, fmaxf(fmaxf(fabsf(x.x), fabsf(x.y)), fmaxf(fabsf(x.z), fabsf(x.w))));
     }
@@ -1038,7 +1040,8 @@ Status launch_attention_tc(const AttnViews& vw, int64_t BH, int64_t S, int D, in
     if (mode == AM_F16) {
         RT_CUDA_CHECK(cudaMemsetAsync(vmax, 0, (size_t)BHkv * 4, st));
         const int per_head = (int)std::max<int64_t>(1, std::min<int64_t>(64, (S * D / 4 + 4095) / 4096));
-        v_absmax_kernel<<<dim3((unsigned)per_head, (unsigned)BHkv), 256, 0, st>>>(kv, (int)S, D, vmax);
+        if (D == 64) v_absmax_kernel<64><<<dim3((unsigned)per_head, (unsigned)BHkv), 256, 0, st>>>(kv, (int)S, vmax);
+        else v_absmax_kernel<128><<<dim3((unsigned)per_head, (unsigned)BHkv), 256, 0, st>>>(kv, (int)S, vmax);
         RT_LAUNCH_CHECK();
         *launches += 1;
         if (D == 64) pack_kv16_kernel<64><<<pgrid, 256, 0, st>>>(kv, kvbuf, (int)S, n_kv, counter, kscale, vmax);

@@ -61,27 +61,43 @@ __global__ void __launch_bounds__(256) row_kernel(const float* __restrict__ x,
                                                   bool cross = true) {
     __shared__ float sh[32];
     constexpr int GROUPS = 256 / THREADS;  // rows handled by one CTA at a time
+    // Whole-CTA rows (few values per thread) load the CTA's next row while
+    // this one is reduced and stored: a row in flight per CTA at all times.
+    constexpr bool PF = THREADS == 256 && VPT <= 16;
     int group = threadIdx.x / THREADS;
     int t = threadIdx.x % THREADS;
-    for (int64_t row = (int64_t)blockIdx.x * GROUPS + group; row < rows;
-         row += (int64_t)gridDim.x * GROUPS) {
-        const float* xr = x + row * C;
-        float* yr = y + row * C;
-        float v[VPT];
+    auto load = [&](int64_t rw, float (&a)[VPT]) {
+        const float* xr = x + rw * C;
         if (VEC) {
 #pragma unroll
             for (int i = 0; i < VPT / 4; i++) {
                 int c = (i * THREADS + t) * 4;
                 float4 q = c < C ? *reinterpret_cast<const float4*>(xr + c)
                                  : make_float4(0.f, 0.f, 0.f, 0.f);
-                v[4 * i] = q.x; v[4 * i + 1] = q.y; v[4 * i + 2] = q.z; v[4 * i + 3] = q.w;
+                a[4 * i] = q.x; a[4 * i + 1] = q.y; a[4 * i + 2] = q.z; a[4 * i + 3] = q.w;
             }
         } else {
 #pragma unroll
             for (int i = 0; i < VPT; i++) {
                 int c = i * THREADS + t;
-                v[i] = c < C ? xr[c] : 0.0f;
+                a[i] = c < C ? xr[c] : 0.0f;
             }
+        }
+    };
+    const int64_t row0 = (int64_t)blockIdx.x * GROUPS + group, stride = (int64_t)gridDim.x * GROUPS;
+    float nxt[PF ? VPT : 1];
+    if constexpr (PF) {
+        if (row0 < rows) load(row0, *reinterpret_cast<float(*)[VPT]>(nxt));
+    }
+    for (int64_t row = row0; row < rows; row += stride) {
+        float* yr = y + row * C;
+        float v[VPT];
+        if constexpr (PF) {
+#pragma unroll
+            for (int i = 0; i < VPT; i++) v[i] = nxt[i];
+            if (row + stride < rows) load(row + stride, *reinterpret_cast<float(*)[VPT]>(nxt));
+        } else {
+            load(row, v);
         }
         auto col = [&](int i) -> int {
             return VEC ? ((i / 4) * THREADS + t) * 4 + (i % 4) : i * THREADS + t;
@@ -240,9 +256,25 @@ void launch_rows(const float* x, const float* g, const float* b, float* y, int64
     row_kernel<KIND, THREADS, VPT, VEC, PLANES, F16P><<<grid, 256, 0, st>>>(x, g, b, y, rows, C, eps, x1, cross);
 }
 
+// Rows of 1024 < C <= 2048 run on a whole 256-thread CTA (8 values per
+// thread, the next row prefetched); shorter rows on one warp.  RT_NORM_CTA=1
+// extends the CTA form down to C > 512, RT_NORM_CTA=0 turns it off.
+int norm_cta_min() {
+    static const int c = [] {
+        const char* e = getenv("RT_NORM_CTA");
+        return e && e[0] == '1' ? 512 : e && e[0] == '0' ? 1 << 30 : 1024;
+    }();
+    return c;
+}
+
 template <int KIND, bool F16P>
 void run_rows_planes_t(const float* x, const float* g, const float* b, float* hi, uint16_t* x1, int64_t rows,
                        int C, float eps, bool cross, cudaStream_t st) {
+    if (C > norm_cta_min() && C <= 2048) {
+        if (C <= 1024) launch_rows<KIND, 256, 4, true, true, F16P>(x, g, b, hi, rows, C, eps, st, x1, cross);
+        else launch_rows<KIND, 256, 8, true, true, F16P>(x, g, b, hi, rows, C, eps, st, x1, cross);
+        return;
+    }
     if (C <= 128) launch_rows<KIND, 32, 4, true, true, F16P>(x, g, b, hi, rows, C, eps, st, x1, cross);
     else if (C <= 256) launch_rows<KIND, 32, 8, true, true, F16P>(x, g, b, hi, rows, C, eps, st, x1, cross);
     else if (C <= 512) launch_rows<KIND, 32, 16, true, true, F16P>(x, g, b, hi, rows, C, eps, st, x1, cross);
@@ -266,6 +298,8 @@ Status run_rows(const float* x, const float* g, const float* b, float* y, int64_
         if (C <= 128) launch_rows<KIND, 32, 4, true>(x, g, b, y, rows, C, eps, st);
         else if (C <= 256) launch_rows<KIND, 32, 8, true>(x, g, b, y, rows, C, eps, st);
         else if (C <= 512) launch_rows<KIND, 32, 16, true>(x, g, b, y, rows, C, eps, st);
+        else if (C <= 1024 && C > norm_cta_min()) launch_rows<KIND, 256, 4, true>(x, g, b, y, rows, C, eps, st);
+        else if (C <= 2048 && C > norm_cta_min()) launch_rows<KIND, 256, 8, true>(x, g, b, y, rows, C, eps, st);
         else if (C <= 1024) launch_rows<KIND, 32, 32, true>(x, g, b, y, rows, C, eps, st);
         else if (C <= 2048) launch_rows<KIND, 32, 64, true>(x, g, b, y, rows, C, eps, st);
         else if (C <= 4096) launch_rows<KIND, 256, 16, true>(x, g, b, y, rows, C, eps, st);
