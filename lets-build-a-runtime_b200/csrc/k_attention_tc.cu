@@ -70,6 +70,15 @@ constexpr int CHUNK = 32 * 1024;                      // ring stage / packed chu
 constexpr uint64_t WAIT_NS = 2000000000ull;
 constexpr int ERR_A_PROD = 0x201, ERR_A_MMA = 0x202, ERR_A_SOFT = 0x203, ERR_A_DRAIN = 0x204;
 constexpr uint32_t COL_S = 0, COL_PH = 128, COL_PL = 256, COL_O = 384;   // fp16 mode: P (h | l) at COL_PH
+// fp16 mode: the Q plane is staged in TMEM (columns COL_QT.., 16 per 16
+// features: 8 of h pairs, then 8 of l pairs), so the S MMAs read only K from
+// shared memory (1B-8K B1: 801 -> 790 us).  RT_ATTN_QTMEM=0 builds the
+// shared-memory form.
+#ifndef RT_ATTN_QTMEM
+#define RT_ATTN_QTMEM 1
+#endif
+constexpr bool Q_TMEM = RT_ATTN_QTMEM != 0;
+constexpr uint32_t COL_QT = COL_PL;
 // Operand modes: three tf32 MMAs, tf32 + bf16 cross terms, or scaled fp16
 // hi / lo (three kind::f16 MMAs, one plane per operand: see below).
 constexpr int AM_3XTF32 = 0, AM_CROSS = 1, AM_F16 = 2;
@@ -519,6 +528,15 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
                             for (int j = 0; j < 2; j++) {
                                 const uint8_t* a = qh + (c * 2 + cs) * BQ * 128 + j * 64;
                                 const uint8_t* b = buf + cs * BKV * 128 + j * 64;
+                                if (Q_TMEM) {
+                                    const uint32_t qc = tmem + COL_QT + (uint32_t)((c * 2 + cs) * 32 + j * 16);
+                                    ptx::mma_bf16_ts(tmem + COL_S, qc, ptx::smem_desc(b + 32, 1024, 2), idesc_sh,
+                                                     (c | cs | j) ? 1u : 0u);
+                                    ptx::mma_bf16_ts(tmem + COL_S, qc, ptx::smem_desc(b, 1024, 2), idesc_sh, 1u);
+                                    ptx::mma_bf16_ts(tmem + COL_S, qc + 8, ptx::smem_desc(b + 32, 1024, 2), idesc_sh,
+                                                     1u);
+                                    continue;
+                                }
                                 ptx::mma_bf16(tmem + COL_S, ptx::smem_desc(a, 1024, 2), ptx::smem_desc(b + 32, 1024, 2),
                                               idesc_sh, (c | cs | j) ? 1u : 0u);
                                 ptx::mma_bf16(tmem + COL_S, ptx::smem_desc(a, 1024, 2), ptx::smem_desc(b, 1024, 2),
@@ -681,11 +699,26 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
                             hw[t] = f16x2_rn(ha, hb);
                             lw[t] = f16x2_rn(a - ha, b - hb);
                         }
+                        if (Q_TMEM) {
+                            uint32_t pr[16];
+#pragma unroll
+                            for (int t = 0; t < 8; t++) {
+                                pr[t] = hw[t];
+                                pr[8 + t] = lw[t];
+                            }
+                            ptx::tmem_st16(tmem + lane_off + COL_QT + (uint32_t)((half * (DH / 16) + cb * 2 + f16b) * 16),
+                                           pr);
+                            continue;
+                        }
                         *reinterpret_cast<uint4*>(blk + swzb(row, f16b * 64)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
                         *reinterpret_cast<uint4*>(blk + swzb(row, f16b * 64 + 16)) = make_uint4(hw[4], hw[5], hw[6], hw[7]);
                         *reinterpret_cast<uint4*>(blk + swzb(row, f16b * 64 + 32)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
                         *reinterpret_cast<uint4*>(blk + swzb(row, f16b * 64 + 48)) = make_uint4(lw[4], lw[5], lw[6], lw[7]);
                     }
+                }
+                if (Q_TMEM) {
+                    ptx::tmem_st_wait();
+                    ptx::tc_fence_before();
                 }
                 ptx::fence_proxy_async_smem();
                 ptx::mbar_arrive(q_ready);
