@@ -779,24 +779,30 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
                                        *reinterpret_cast<uint32_t(*)[16]>(&rr[c16 * 16]));
                     ptx::tmem_ld_wait();
 #pragma unroll
-                    for (int i = 0; i < KH; i++) sv[i] = __uint_as_float(rr[i]) * (i < 32 ? f0 : f1);
+                    for (int i = 0; i < KH; i++) sv[i] = __uint_as_float(rr[i]);   // raw: scaled in the exponent
                 }
                 ptx::tc_fence_before();
                 ptx::mbar_arrive(s_free);   // S may be overwritten by the next tile's MMAs
                 const int k0 = j * BKV + half * KH;
                 const bool full_tile = k0 + KH <= p.S && (!p.causal || k0 + KH - 1 <= q);
-                float mt = -INFINITY;
+                // maxima of the raw scores per 32-key group, then scaled (f0, f1 > 0)
+                float g0 = -INFINITY, g1 = -INFINITY;
                 if (full_tile) {
 #pragma unroll
-                    for (int i = 0; i < KH; i++) mt = fmaxf(mt, sv[i]);
+                    for (int i = 0; i < KH; i++) {
+                        if (i < 32) g0 = fmaxf(g0, sv[i]);
+                        else g1 = fmaxf(g1, sv[i]);
+                    }
                 } else {
 #pragma unroll
                     for (int i = 0; i < KH; i++) {
                         const int kj = k0 + i;
                         if (kj >= p.S || (p.causal && kj > q)) sv[i] = -INFINITY;
-                        mt = fmaxf(mt, sv[i]);
+                        if (i < 32) g0 = fmaxf(g0, sv[i]);
+                        else g1 = fmaxf(g1, sv[i]);
                     }
                 }
+                float mt = fmaxf(g0 * f0, g1 * f1);
                 red[((T & 1) * 2 + half) * BQ + row] = mt;
                 if (!(ok = pair_sync(T & 1, (T >> 1) & 1))) break;
                 mt = fmaxf(mt, red[((T & 1) * 2 + (half ^ 1)) * BQ + row]);
@@ -813,7 +819,7 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
                 float lt = 0.0f;
 #pragma unroll
                 for (int i = 0; i < KH; i++) {
-                    sv[i] = ex2_approx(sv[i] - m_new);   // masked: 2^-inf = 0
+                    sv[i] = ex2_approx(fmaf(sv[i], i < 32 ? f0 : f1, -m_new));   // masked: 2^-inf = 0
                     lt += sv[i];
                 }
                 const float corr = m_new > m ? ex2_approx(m - m_new) : 1.0f;
@@ -864,8 +870,10 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
                     if (F16) {   // 16 columns per 16 keys: 8 of h pairs, then 8 of l pairs
 #pragma unroll
                         for (int t = 0; t < 8; t++) {
+                            // h: 11 significant bits by truncation (exact in fp16), l = x - h >= 0
                             const float a = sv[c16 * 16 + 2 * t], b = sv[c16 * 16 + 2 * t + 1];
-                            const float ha = round11(a), hb = round11(b);
+                            const float ha = __uint_as_float(__float_as_uint(a) & 0xFFFFE000u);
+                            const float hb = __uint_as_float(__float_as_uint(b) & 0xFFFFE000u);
                             ph[t] = f16x2_rn(ha, hb);
                             ph[8 + t] = f16x2_rn(a - ha, b - hb);
                         }
