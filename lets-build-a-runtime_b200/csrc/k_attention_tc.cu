@@ -182,6 +182,38 @@ __device__ __forceinline__ uint32_t bf16x2_rn_int(float a, float b) {
 }
 // 2^x with the hardware approximation (flushes results below 2^-126 to 0;
 // 2^-inf = 0, which the causal mask relies on).
+// Blackwell's three-input maximum and paired fp32 arithmetic (one
+// instruction for two lanes of work): the softmax is bounded by its
+// instruction count.
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+__device__ __forceinline__ unsigned long long pk2(float a, float b) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void upk2(unsigned long long r, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ unsigned long long fma2(unsigned long long a, unsigned long long b, unsigned long long c) {
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ unsigned long long add2(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ unsigned long long sub2(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
 __device__ __forceinline__ float ex2_approx(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -789,9 +821,9 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
                 float g0 = -INFINITY, g1 = -INFINITY;
                 if (full_tile) {
 #pragma unroll
-                    for (int i = 0; i < KH; i++) {
-                        if (i < 32) g0 = fmaxf(g0, sv[i]);
-                        else g1 = fmaxf(g1, sv[i]);
+                    for (int i = 0; i < 32; i += 2) {
+                        g0 = max3f(g0, sv[i], sv[i + 1]);
+                        g1 = max3f(g1, sv[32 + i], sv[32 + i + 1]);
                     }
                 } else {
 #pragma unroll
@@ -816,11 +848,23 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
                 const bool fold = !first && pend >= FOLD_EVERY;   // uniform: one accumulator per tile
                 float m_new = m;
                 if (first || mt > m + RESCALE_LOG2 || (fold && mt > m)) m_new = mt > m ? mt : m;
-                float lt = 0.0f;
+                unsigned long long lt2 = pk2(0.0f, 0.0f);
+                {
+                    const unsigned long long ff0 = pk2(f0, f0), ff1 = pk2(f1, f1), mm = pk2(-m_new, -m_new);
 #pragma unroll
-                for (int i = 0; i < KH; i++) {
-                    sv[i] = ex2_approx(fmaf(sv[i], i < 32 ? f0 : f1, -m_new));   // masked: 2^-inf = 0
-                    lt += sv[i];
+                    for (int i = 0; i < KH; i += 2) {
+                        float a, b;
+                        upk2(fma2(pk2(sv[i], sv[i + 1]), i < 32 ? ff0 : ff1, mm), a, b);
+                        sv[i] = ex2_approx(a);   // masked: 2^-inf = 0
+                        sv[i + 1] = ex2_approx(b);
+                        lt2 = add2(lt2, pk2(sv[i], sv[i + 1]));
+                    }
+                }
+                float lt;
+                {
+                    float a, b;
+                    upk2(lt2, a, b);
+                    lt = a + b;
                 }
                 const float corr = m_new > m ? ex2_approx(m - m_new) : 1.0f;
                 if (!first) {   // PV of tile j-1 done: P may be overwritten, pending O is complete
@@ -874,8 +918,10 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
                             const float a = sv[c16 * 16 + 2 * t], b = sv[c16 * 16 + 2 * t + 1];
                             const float ha = __uint_as_float(__float_as_uint(a) & 0xFFFFE000u);
                             const float hb = __uint_as_float(__float_as_uint(b) & 0xFFFFE000u);
+                            float la, lb;
+                            upk2(sub2(pk2(a, b), pk2(ha, hb)), la, lb);
                             ph[t] = f16x2_rn(ha, hb);
-                            ph[8 + t] = f16x2_rn(a - ha, b - hb);
+                            ph[8 + t] = f16x2_rn(la, lb);
                         }
                         ptx::tmem_st16(tmem + lane_off + COL_PH + half * KH + c16 * 16, ph);
                         continue;
