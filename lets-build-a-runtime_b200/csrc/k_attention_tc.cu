@@ -182,38 +182,6 @@ __device__ __forceinline__ uint32_t bf16x2_rn_int(float a, float b) {
 }
 // 2^x with the hardware approximation (flushes results below 2^-126 to 0;
 // 2^-inf = 0, which the causal mask relies on).
-// Blackwell's three-input maximum and paired fp32 arithmetic (one
-// instruction for two lanes of work): the softmax is bounded by its
-// instruction count.
-__device__ __forceinline__ float max3f(float a, float b, float c) {
-    float d;
-    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-    return d;
-}
-__device__ __forceinline__ unsigned long long pk2(float a, float b) {
-    unsigned long long r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
-    return r;
-}
-__device__ __forceinline__ void upk2(unsigned long long r, float& a, float& b) {
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
-}
-__device__ __forceinline__ unsigned long long fma2(unsigned long long a, unsigned long long b, unsigned long long c) {
-    unsigned long long d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-    return d;
-}
-__device__ __forceinline__ unsigned long long add2(unsigned long long a, unsigned long long b) {
-    unsigned long long d;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-__device__ __forceinline__ unsigned long long sub2(unsigned long long a, unsigned long long b) {
-    unsigned long long d;
-    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-    return d;
-}
-
 __device__ __forceinline__ float ex2_approx(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -882,7 +850,10 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
                                        *reinterpret_cast<uint32_t(*)[16]>(&rr[16]));
                         ptx::tmem_ld_wait();
 #pragma unroll
-                        for (int i = 0; i < 32; i++) o[g * 32 + i] += __uint_as_float(rr[i]);
+                        for (int i = 0; i < 32; i += 2)
+                            upk2(add2(pk2(o[g * 32 + i], o[g * 32 + i + 1]),
+                                      pk2(__uint_as_float(rr[i]), __uint_as_float(rr[i + 1]))),
+                                 o[g * 32 + i], o[g * 32 + i + 1]);
                     }
                 } else if (!first && __any_sync(0xffffffffu, m_new > m)) {
                     // rescale this warp's rows of the pending TMEM O (warp-collective;
@@ -893,16 +864,23 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
                         const uint32_t at = tmem + lane_off + COL_O + half * DH + g * 16;
                         ptx::tmem_ld16(at, rr);
                         ptx::tmem_ld_wait();
+                        const unsigned long long cc = pk2(corr, corr);
 #pragma unroll
-                        for (int i = 0; i < 16; i++) rr[i] = __float_as_uint(__uint_as_float(rr[i]) * corr);
+                        for (int i = 0; i < 16; i += 2) {
+                            float a, b;
+                            upk2(mul2(pk2(__uint_as_float(rr[i]), __uint_as_float(rr[i + 1])), cc), a, b);
+                            rr[i] = __float_as_uint(a);
+                            rr[i + 1] = __float_as_uint(b);
+                        }
                         ptx::tmem_st16(at, rr);
                     }
                     ptx::tmem_st_wait();
                 }
                 if (m_new > m) {   // running max grew: rescale the folded part (corr would be 1 otherwise)
                     l *= corr;
+                    const unsigned long long cc = pk2(corr, corr);
 #pragma unroll
-                    for (int i = 0; i < DH; i++) o[i] *= corr;
+                    for (int i = 0; i < DH; i += 2) upk2(mul2(pk2(o[i], o[i + 1]), cc), o[i], o[i + 1]);
                     m = m_new;
                 }
                 l += lt;

@@ -520,10 +520,13 @@ __global__ void __launch_bounds__(THREADS, 1) tc_gemm_kernel(const __grid_consta
                     uint32_t r[16];
                     ptx::tmem_ld16(tbase + q * 16, r);
                     ptx::tmem_ld_wait();
+                    const unsigned long long f2 = pk2(fc, fc);
 #pragma unroll
-                    for (int j = 0; j < 16; j++)
-                        acc[q * 16 + j] = c == 0 ? fc * __uint_as_float(r[j])
-                                                 : fmaf(fc, __uint_as_float(r[j]), acc[q * 16 + j]);
+                    for (int j = 0; j < 16; j += 2) {
+                        const unsigned long long rv = pk2(__uint_as_float(r[j]), __uint_as_float(r[j + 1]));
+                        upk2(c == 0 ? mul2(f2, rv) : fma2(f2, rv, pk2(acc[q * 16 + j], acc[q * 16 + j + 1])),
+                             acc[q * 16 + j], acc[q * 16 + j + 1]);
+                    }
                 }
                 ptx::tc_fence_before();
                 ptx::mbar_arrive(&acc_empty[b]);
@@ -801,10 +804,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                     uint32_t r[16];
                     ptx::tmem_ld16(tbase + q * 16, r);
                     ptx::tmem_ld_wait();
+                    const unsigned long long f2 = pk2(fc, fc);
 #pragma unroll
-                    for (int j = 0; j < 16; j++)
-                        acc[q * 16 + j] = c == 0 && !RES ? fc * __uint_as_float(r[j])
-                                                         : fmaf(fc, __uint_as_float(r[j]), acc[q * 16 + j]);
+                    for (int j = 0; j < 16; j += 2) {
+                        const unsigned long long rv = pk2(__uint_as_float(r[j]), __uint_as_float(r[j + 1]));
+                        upk2(c == 0 && !RES ? mul2(f2, rv) : fma2(f2, rv, pk2(acc[q * 16 + j], acc[q * 16 + j + 1])),
+                             acc[q * 16 + j], acc[q * 16 + j + 1]);
+                    }
                 }
                 ptx::tc_fence_before();
                 __syncwarp();
