@@ -953,8 +953,9 @@ void plan_gemm_chains(const Analysis& an, const Effective& e, std::vector<PlanIt
 // writes) -- and u's output is x itself or clear of it (the epilogue reads
 // each x element just before writing it).  Opt-in (RT_FUSE_RESIDUAL=1): the
 // epilogue's residual loads (one row per thread, like its stores) double its
-// L1 -> L2 requests; measured GPT-2 1.367 -> 1.387 ms, Qwen3 2.768 -> 2.786,
-// 1b8k 31.99 -> 32.31, 7b 11.20 -> 11.04.
+// L1 -> L2 requests; measured GPT-2 1.040 -> 1.160 ms, Qwen3 1.884 -> 1.901,
+// 7b 8.52 -> 8.66; only the 1B-8K block gains (22.45 -> 22.04 ms at the same
+// clock: its K = 2048 / 8192 GEMMs leave the epilogue room).
 void plan_residual_folds(const Analysis& an, const Effective& e, std::vector<PlanItem>& items,
                          const std::vector<Range>& protect) {
     const int n = (int)an.nodes.size();
