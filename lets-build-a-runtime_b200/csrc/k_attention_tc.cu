@@ -285,7 +285,15 @@ __global__ void __launch_bounds__(256) v_absmax_kernel(KvViews kv, int S, unsign
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if ((threadIdx.x & 31) == 0) atomicMax(vmax + h, __float_as_uint(m));
+    // one atomic per block (per-warp atomics on the BHkv words serialised)
+    __shared__ float wm[8];
+    if ((threadIdx.x & 31) == 0) wm[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+#pragma unroll
+        for (int w = 1; w < 8; w++) m = fmaxf(m, wm[w]);
+        atomicMax(vmax + h, __float_as_uint(m));
+    }
 }
 
 // K (as K chunks of 64 features x 128 keys: two [128 keys][128 B] blocks) and
@@ -1104,7 +1112,7 @@ Status launch_attention_tc(const AttnViews& vw, int64_t BH, int64_t S, int D, in
     unsigned* vmax = reinterpret_cast<unsigned*>(kscale + (size_t)BHkv * n_kv * 4);
     if (mode == AM_F16) {
         RT_CUDA_CHECK(cudaMemsetAsync(vmax, 0, (size_t)BHkv * 4, st));
-        const int per_head = (int)std::max<int64_t>(1, std::min<int64_t>(64, (S * D / 4 + 4095) / 4096));
+        const int per_head = (int)std::max<int64_t>(1, std::min<int64_t>(128, (S * D / 4 + 2047) / 2048));
         if (D == 64) v_absmax_kernel<64><<<dim3((unsigned)per_head, (unsigned)BHkv), 256, 0, st>>>(kv, (int)S, vmax);
         else v_absmax_kernel<128><<<dim3((unsigned)per_head, (unsigned)BHkv), 256, 0, st>>>(kv, (int)S, vmax);
         RT_LAUNCH_CHECK();
