@@ -13,7 +13,9 @@
 //   * the source the fused consumer reads instead is not written by any node
 //     between the skipped producer and the consumer;
 //   * for the output side, nothing between attention and the merge TRANSPOSE
-//     touches the merge's output region.
+//     touches the merge's output region;
+//   * the fused output does not overlap Q; it may overlap K and V, which the
+//     tensor-core path's pre-passes have consumed before O is written.
 // Every node's read and write extents are computed from its op, shape and
 // extras; a node whose read extent is not known blocks any fusion across it.
 // RT_FUSE=0 disables the pass (RT_FUSE_GEMM=0 only the GEMM epilogue chains;
@@ -175,6 +177,7 @@ struct Proposal {
     AttnViews views{};
     std::vector<std::pair<int, int>> skips;       // (folded node, its consumer in the original schedule)
     std::vector<std::pair<Range, int>> sources;   // range read through a view, chain start index
+    std::vector<int> source_op;                   // which operand each source feeds: 0 Q, 1 K, 2 V
     Range out{};                                  // what the fused attention writes
     int out_skip = -1;                            // merge TRANSPOSE folded into the attention
     std::vector<std::pair<int, int>> redirect;    // (node, input slot) now reading `out` instead of the merge's output
@@ -223,6 +226,7 @@ bool match_operand(const Analysis& an, int a, int which, int64_t B, int64_t Hx, 
     if (which == 1) { v.k = base; v.k_sb = sb; v.k_sh = sh; v.k_ss = ss; }
     if (which == 2) { v.v = base; v.v_sb = sb; v.v_sh = sh; v.v_ss = ss; }
     pr.sources.push_back({src, start});
+    pr.source_op.push_back(which);
     return true;
 }
 
@@ -369,11 +373,16 @@ static bool dbg() {
     } while (0)
 
 bool valid(const Analysis& an, const Effective& e, const Proposal& p, const std::vector<Range>& protect) {
-    // view sources intact from the start of their chain to the attention
-    for (auto& sr : p.sources) {
+    // view sources intact from the start of their chain to the attention.
+    // The output may overlap K / V (views or not): a fused attention always
+    // runs the tensor-core path, whose pre-passes (V maximum, K/V pack into
+    // the plan's workspace) read all of K and V before the attention kernel
+    // writes any of O.  Q is read by the attention kernel itself.
+    for (size_t i = 0; i < p.sources.size(); i++) {
+        const auto& sr = p.sources[i];
         for (int j = sr.second + 1; j < p.a; j++)
             if (overlaps(e.writes[j], sr.first)) FAIL("source overwritten before the attention");
-        if (overlaps(p.out, sr.first)) FAIL("output overlaps a source");
+        if (p.source_op[i] == 0 && overlaps(p.out, sr.first)) FAIL("output overlaps the Q source");
     }
     for (auto& k : p.skips)
         if (!dead_output(an, k.first, k.second, protect)) FAIL("a folded node's output is still needed");
@@ -397,17 +406,15 @@ bool valid(const Analysis& an, const Effective& e, const Proposal& p, const std:
         if (!rewritten)
             for (const Range& pr : protect)
                 if (overlaps(pr, U)) FAIL("merge output is a graph output");
-        for (auto& sr : p.sources)
-            if (overlaps(sr.first, p.out)) FAIL("output overlaps a source");
+        for (size_t i = 0; i < p.sources.size(); i++)
+            if (p.source_op[i] == 0 && overlaps(p.sources[i].first, p.out)) FAIL("output overlaps the Q source");
     } else if (p.out_skip >= 0) {
         // nothing between the attention and the folded merge touches either buffer
         for (int j = p.a + 1; j < p.out_skip; j++)
             if (overlaps(e.writes[j], p.out) || eff_reads(e, j, p.out) || eff_reads(e, j, an.writes[p.a]))
                 FAIL("merge buffer touched between attention and merge");
-        for (int i = 0; i < 3; i++) {   // nor does the output overlap an unfused operand
-            const Range in = an.reads[p.a][i];
-            if (overlaps(in, p.out)) FAIL("merge output overlaps an operand");
-        }
+        // nor does the output overlap Q (K and V are consumed by the pre-passes)
+        if (overlaps(an.reads[p.a][0], p.out)) FAIL("merge output overlaps Q");
         if (!dead_output(an, p.a, p.out_skip, protect)) FAIL("attention output still needed");
     }
     return true;

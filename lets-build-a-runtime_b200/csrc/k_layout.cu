@@ -14,6 +14,7 @@
 // the widest access (16, 8 or 4 bytes ... 1) that divides every run length
 // and every base address, so head-split transposes of 64/128-float rows move
 // 16-byte vectors with fully coalesced reads and writes.
+#include <algorithm>
 #include <initializer_list>
 #include <type_traits>
 
@@ -30,22 +31,100 @@ inline int pick_unit(std::initializer_list<uint64_t> vals) {
     return u;
 }
 
-template <typename T>
-__global__ void transpose_nd_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t A,
-                                    int64_t M, int64_t B, int64_t inner, int64_t total) {
-    // output order: [o][b][m][a][i]  (i in units of T)
-    for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
-         idx += (int64_t)gridDim.x * blockDim.x) {
-        int64_t i = idx % inner;
-        int64_t r = idx / inner;
-        int64_t a = r % A;
-        r /= A;
-        int64_t m = r % M;
-        r /= M;
-        int64_t b = r % B;
-        int64_t o = r / B;
-        y[idx] = x[(((o * A + a) * M + m) * B + b) * inner + i];
+// A layout op as a list of runs: the output is `runs` runs of `len` units,
+// each copied from one contiguous source run.  Index arithmetic (64-bit
+// divisions) happens once per run and thread, not per element: a group of G
+// lanes (a power of two, <= 32) copies one run, each lane moving up to four
+// units per round with all loads issued before the stores.
+//   MODE 0 TRANSPOSE N-D: run r = (((o*B + b)*M + m)*A + a), source run
+//          (((o*A + a)*M + m)*B + b); runs are contiguous in the output
+//   MODE 1 SLICE:  run o at y + o*len, from x + o*stride + off
+//   MODE 2 CAT piece: run o from x + o*len, to y + o*stride + off
+struct RunMap {
+    int64_t A, M, B;      // MODE 0
+    int64_t stride, off;  // MODES 1 / 2 (units)
+};
+
+template <typename T, int MODE>
+__global__ void __launch_bounds__(256) runs_kernel(const T* __restrict__ x, T* __restrict__ y, RunMap p,
+                                                   int64_t runs, int64_t len, int lg_g, int parts,
+                                                   int64_t chunk) {
+    const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int G = 1 << lg_g, lane = (int)(tid & (G - 1));
+    const int64_t groups = ((int64_t)gridDim.x * blockDim.x) >> lg_g;
+    const int64_t W = runs * parts;   // work items: a run, or a piece of one
+    for (int64_t w = tid >> lg_g; w < W; w += 4 * groups) {
+        // four work items at a time, so a lane has four loads in flight
+        const T* src[4];
+        T* dst[4];
+        int64_t n[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int64_t wk = w + k * groups;
+            n[k] = 0;
+            src[k] = x;
+            dst[k] = y;
+            if (wk >= W) continue;
+            const int64_t r = parts == 1 ? wk : wk / parts;
+            const int64_t i0 = parts == 1 ? 0 : (wk % parts) * chunk;
+            n[k] = (parts == 1 || i0 + chunk > len ? len : i0 + chunk) - i0;
+            if (MODE == 0) {
+                int64_t q = r;
+                const int64_t a = q % p.A;
+                q /= p.A;
+                const int64_t m = q % p.M;
+                q /= p.M;
+                const int64_t b = q % p.B, o = q / p.B;
+                src[k] = x + (((o * p.A + a) * p.M + m) * p.B + b) * len + i0;
+                dst[k] = y + r * len + i0;
+            } else if (MODE == 1) {
+                src[k] = x + r * p.stride + p.off + i0;
+                dst[k] = y + r * len + i0;
+            } else {
+                src[k] = x + r * len + i0;
+                dst[k] = y + r * p.stride + p.off + i0;
+            }
+        }
+        const int64_t span = parts == 1 ? len : chunk;
+        for (int64_t i = lane; i < span; i += G) {
+            T v[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+                if (i < n[k]) v[k] = src[k][i];
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+                if (i < n[k]) dst[k][i] = v[k];
+        }
     }
+}
+
+template <typename T, int MODE>
+void launch_runs(const T* x, T* y, RunMap p, int64_t runs, int64_t len, cudaStream_t st) {
+    if (runs <= 0 || len <= 0) return;
+    int lg_g = 0;
+    while (lg_g < 5 && ((int64_t)1 << lg_g) < len) lg_g++;
+    // Few long runs: cut each into `parts` pieces of `chunk` units (a multiple
+    // of 4*G) so that every SM gets work (four pieces per group round).
+    const int64_t want = (int64_t)g_num_sms * 2048 * 4;       // resident threads x 4 items
+    const int64_t round_units = (int64_t)4 << lg_g;
+    int parts = 1;
+    int64_t chunk = len;
+    if ((runs << lg_g) < want && len > round_units) {
+        const int64_t max_parts = (len + round_units - 1) / round_units;
+        const int64_t need = (want + (runs << lg_g) - 1) / (runs << lg_g);
+        parts = (int)std::min<int64_t>(max_parts, std::min<int64_t>(need, 1 << 20));
+        chunk = ((len + parts - 1) / parts + round_units - 1) / round_units * round_units;
+        parts = (int)((len + chunk - 1) / chunk);
+    }
+    const int64_t threads = (((runs * parts) + 3) / 4) << lg_g;   // four work items per group round
+    runs_kernel<T, MODE><<<grid_for(threads, 256), 256, 0, st>>>(x, y, p, runs, len, lg_g, parts, chunk);
+}
+
+// Plain copy of n units.
+template <typename T>
+__global__ void copy_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        y[i] = x[i];
 }
 
 __global__ void transpose_2d_kernel(const float* __restrict__ x, float* __restrict__ y, int R,
@@ -64,30 +143,6 @@ __global__ void transpose_2d_kernel(const float* __restrict__ x, float* __restri
             }
             __syncthreads();
         }
-}
-
-// y[o][j] = x[o][start + j] for j < len (all counted in units of T).
-template <typename T>
-__global__ void strided_rows_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t rows,
-                                    int64_t len, int64_t src_stride, int64_t start) {
-    int64_t total = rows * len;
-    for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
-         idx += (int64_t)gridDim.x * blockDim.x) {
-        int64_t o = idx / len, j = idx % len;
-        y[idx] = x[o * src_stride + start + j];
-    }
-}
-
-// One CAT input: y[o][off + j] = x[o][j], j < len (units of T).
-template <typename T>
-__global__ void cat_piece_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t rows,
-                                 int64_t len, int64_t dst_stride, int64_t off) {
-    int64_t total = rows * len;
-    for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
-         idx += (int64_t)gridDim.x * blockDim.x) {
-        int64_t o = idx / len, j = idx % len;
-        y[o * dst_stride + off + j] = x[idx];
-    }
 }
 
 __global__ void embedding_kernel(const int64_t* __restrict__ ids, const float* __restrict__ table,
@@ -121,7 +176,7 @@ Status copy_bytes(const void* src, void* dst, size_t bytes, cudaStream_t st) {
     return dispatch_unit(unit, [&](auto* tag) {
         using T = std::remove_pointer_t<decltype(tag)>;
         int64_t n = bytes / sizeof(T);
-        strided_rows_kernel<T><<<grid_for(n, kT), kT, 0, st>>>((const T*)src, (T*)dst, 1, n, n, 0);
+        copy_kernel<T><<<grid_for(n, kT), kT, 0, st>>>((const T*)src, (T*)dst, n);
     });
 }
 
@@ -151,11 +206,10 @@ Status launch_layout(const OpNode& nd, cudaStream_t st, int* launches) {
             int unit = pick_unit({run, (uint64_t)(uintptr_t)nd.inputs[0],
                                   (uint64_t)(uintptr_t)nd.output});
             int64_t inner = run / unit;
-            int64_t total = O * A * M * B * inner;
             return dispatch_unit(unit, [&](auto* tag) {
                 using T = std::remove_pointer_t<decltype(tag)>;
-                transpose_nd_kernel<T><<<grid_for(total, kT), kT, 0, st>>>(
-                    (const T*)nd.inputs[0], (T*)nd.output, A, M, B, inner, total);
+                RunMap p{A, M, B, 0, 0};
+                launch_runs<T, 0>((const T*)nd.inputs[0], (T*)nd.output, p, O * A * M * B, inner, st);
             });
         }
         case RT_OP_SLICE: {
@@ -168,9 +222,8 @@ Status launch_layout(const OpNode& nd, cudaStream_t st, int* launches) {
                                   (uint64_t)(uintptr_t)nd.output});
             return dispatch_unit(unit, [&](auto* tag) {
                 using T = std::remove_pointer_t<decltype(tag)>;
-                int64_t len = row / unit;
-                strided_rows_kernel<T><<<grid_for(O * len, kT), kT, 0, st>>>(
-                    (const T*)nd.inputs[0], (T*)nd.output, O, len, src_row / unit, start / unit);
+                RunMap p{1, 1, 1, (int64_t)(src_row / unit), (int64_t)(start / unit)};
+                launch_runs<T, 1>((const T*)nd.inputs[0], (T*)nd.output, p, O, (int64_t)(row / unit), st);
             });
         }
         case RT_OP_CAT: {
@@ -190,10 +243,8 @@ Status launch_layout(const OpNode& nd, cudaStream_t st, int* launches) {
                                       (uint64_t)(uintptr_t)nd.output});
                 Status s = dispatch_unit(unit, [&](auto* tag) {
                     using T = std::remove_pointer_t<decltype(tag)>;
-                    int64_t l = len / unit;
-                    cat_piece_kernel<T><<<grid_for(outer * l, kT), kT, 0, st>>>(
-                        (const T*)nd.inputs[k], (T*)nd.output, outer, l, dst_row / unit,
-                        off / unit);
+                    RunMap p{1, 1, 1, (int64_t)(dst_row / unit), (int64_t)(off / unit)};
+                    launch_runs<T, 2>((const T*)nd.inputs[k], (T*)nd.output, p, outer, (int64_t)(len / unit), st);
                 });
                 if (!s.good()) return s;
                 *launches += 1;

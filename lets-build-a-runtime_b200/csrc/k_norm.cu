@@ -45,6 +45,35 @@ __device__ __forceinline__ float block_reduce(float v, float* sh) {
     return MAX ? warp_max(r) : warp_sum(r);
 }
 
+// Two sums and one maximum across the threads of a group (a warp or the
+// CTA) in one round: one barrier pair instead of one per quantity.  All
+// threads get the results.  sh holds 24 floats.
+template <int THREADS>
+__device__ __forceinline__ void group_reduce_ssm(float& s, float& q, float& m, float* sh) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        s += __shfl_xor_sync(0xffffffffu, s, o);
+        q += __shfl_xor_sync(0xffffffffu, q, o);
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    }
+    if constexpr (THREADS != 32) {
+    static_assert(THREADS == 256, "whole-CTA rows are 256 threads");
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();  // sh may still be read from the previous row
+    if (l == 0) {
+        sh[w] = s;
+        sh[8 + w] = q;
+        sh[16 + w] = m;
+    }
+    __syncthreads();
+    const float4* s4 = reinterpret_cast<const float4*>(sh);
+    const float4 a0 = s4[0], a1 = s4[1], b0 = s4[2], b1 = s4[3], c0 = s4[4], c1 = s4[5];
+    s = ((a0.x + a0.y) + (a0.z + a0.w)) + ((a1.x + a1.y) + (a1.z + a1.w));
+    q = ((b0.x + b0.y) + (b0.z + b0.w)) + ((b1.x + b1.y) + (b1.z + b1.w));
+    m = fmaxf(fmaxf(fmaxf(c0.x, c0.y), fmaxf(c0.z, c0.w)), fmaxf(fmaxf(c1.x, c1.y), fmaxf(c1.z, c1.w)));
+    }
+}
+
 // One row per group of THREADS threads (a warp or the whole CTA); each
 // thread holds VPT floats of the row: elements (v*THREADS + t)*4 .. +3 when
 // VEC (C % 4 == 0; x, y, gamma, beta 16-byte aligned), else elements v*THREADS + t.
@@ -53,13 +82,13 @@ __device__ __forceinline__ float block_reduce(float v, float* sh) {
 // its fp16 plane to y (2*C halves per row, C % 16 == 0) and its 2^-e scale
 // to ((float*)x1)[row], from the maximum of the normalised row.
 template <int KIND, int THREADS, int VPT, bool VEC, bool PLANES = false, bool F16P = false>
-__global__ void __launch_bounds__(256) row_kernel(const float* __restrict__ x,
+__global__ void __launch_bounds__(256, THREADS == 256 ? (VPT <= 8 ? 5 : 1) : (VPT <= 24 ? 3 : VPT <= 32 ? 2 : 1)) row_kernel(const float* __restrict__ x,
                                                   const float* __restrict__ g,
                                                   const float* __restrict__ b,
                                                   float* __restrict__ y, int64_t rows, int C,
                                                   float eps, uint16_t* __restrict__ x1 = nullptr,
                                                   bool cross = true) {
-    __shared__ float sh[32];
+    __shared__ __align__(16) float sh[32];
     constexpr int GROUPS = 256 / THREADS;  // rows handled by one CTA at a time
     // Whole-CTA rows (few values per thread) load the CTA's next row while
     // this one is reduced and stored: a row in flight per CTA at all times.
@@ -84,6 +113,32 @@ __global__ void __launch_bounds__(256) row_kernel(const float* __restrict__ x,
             }
         }
     };
+    // Whole-CTA F16P rows take their fp16 scale from a bound instead of a
+    // further reduction: |y| <= scale * (max|x| + |mean|) * max|gamma| +
+    // max|beta|; the gamma / beta maxima over the row once per CTA.
+    // Whole-CTA rows: one reduction round per row (two sums and a maximum).
+    // Warp rows keep the sequential warp reductions, which need fewer
+    // registers (occupancy decides the warp form's speed).
+    constexpr bool STATS1 = VEC && THREADS == 256 && (KIND == N_LAYER || KIND == N_RMS);
+    constexpr bool ONE_PASS = STATS1 && PLANES && F16P;
+    float gmax = 0.0f, bmax = 0.0f;
+    if constexpr (ONE_PASS) {
+#pragma unroll
+        for (int i = 0; i < VPT / 4; i++) {
+            const int c = (i * THREADS + t) * 4;
+            if (c < C) {
+                const float4 g4 = *reinterpret_cast<const float4*>(g + c);
+                gmax = fmaxf(gmax, fmaxf(fmaxf(fabsf(g4.x), fabsf(g4.y)), fmaxf(fabsf(g4.z), fabsf(g4.w))));
+                if (KIND == N_LAYER) {
+                    const float4 b4 = *reinterpret_cast<const float4*>(b + c);
+                    bmax = fmaxf(bmax, fmaxf(fmaxf(fabsf(b4.x), fabsf(b4.y)), fmaxf(fabsf(b4.z), fabsf(b4.w))));
+                }
+            }
+        }
+        float unused = 0.0f;
+        group_reduce_ssm<THREADS>(unused, unused, gmax, sh);
+        if (KIND == N_LAYER) group_reduce_ssm<THREADS>(unused, unused, bmax, sh);
+    }
     const int64_t row0 = (int64_t)blockIdx.x * GROUPS + group, stride = (int64_t)gridDim.x * GROUPS;
     float nxt[PF ? VPT : 1];
     if constexpr (PF) {
@@ -103,7 +158,38 @@ __global__ void __launch_bounds__(256) row_kernel(const float* __restrict__ x,
             return VEC ? ((i / 4) * THREADS + t) * 4 + (i % 4) : i * THREADS + t;
         };
         float scale = 1.0f, shift = 0.0f;
-        if (KIND == N_LAYER) {
+        float bound = 0.0f;   // F16P: an upper bound of the normalised row's magnitudes
+        if (STATS1 && KIND == N_LAYER) {
+            // One reduction round: sums of d = x - x[0] and d^2 (shifted sums:
+            // no cancellation unless the mean is far from x[0] relative to the
+            // spread), and max |x| for the plane's scale bound.
+            const float k0 = __ldg(x + row * C);
+            float s = 0.0f, q = 0.0f, xm = 0.0f;
+#pragma unroll
+            for (int i = 0; i < VPT; i++) {
+                const float d = col(i) < C ? v[i] - k0 : 0.0f;
+                s += d;
+                q = fmaf(d, d, q);
+                xm = fmaxf(xm, fabsf(v[i]));   // padding lanes hold 0
+            }
+            group_reduce_ssm<THREADS>(s, q, xm, sh);
+            const float mean = k0 + s / C;
+            const float var = fmaxf(q - s * (s / C), 0.0f);
+            scale = 1.0f / sqrtf(var / C + eps);
+#pragma unroll
+            for (int i = 0; i < VPT; i++) v[i] = col(i) < C ? v[i] - mean : 0.0f;
+            bound = fmaf(scale * (xm + fabsf(mean)), gmax, bmax);
+        } else if (STATS1 && KIND == N_RMS) {
+            float q = 0.0f, xm = 0.0f, unused = 0.0f;
+#pragma unroll
+            for (int i = 0; i < VPT; i++) {
+                q = fmaf(v[i], v[i], q);
+                xm = fmaxf(xm, fabsf(v[i]));
+            }
+            group_reduce_ssm<THREADS>(q, unused, xm, sh);
+            scale = 1.0f / sqrtf(q / C + eps);
+            bound = scale * xm * gmax;
+        } else if (KIND == N_LAYER) {
             float s = 0.0f;
 #pragma unroll
             for (int i = 0; i < VPT; i++) s += v[i];
@@ -154,12 +240,12 @@ __global__ void __launch_bounds__(256) row_kernel(const float* __restrict__ x,
                         float val = v[4 * i + k] * scale * gg[k];
                         if (KIND == N_LAYER) val += bv[k];
                         v[4 * i + k] = val;
-                        m = fmaxf(m, fabsf(val));
+                        if (!ONE_PASS) m = fmaxf(m, fabsf(val));
                     }
                 }
             }
-            m = block_reduce<THREADS, true>(m, sh);
-            const int e = f16_scale_exp(m);
+            if (!ONE_PASS) m = block_reduce<THREADS, true>(m, sh);
+            const int e = f16_scale_exp(ONE_PASS ? bound : m);
             const float sc = pow2i(e);
             if (t == 0) reinterpret_cast<float*>(x1)[row] = pow2i(-e);
             uint16_t* pr = reinterpret_cast<uint16_t*>(y) + row * C * 2;
@@ -278,6 +364,7 @@ void run_rows_planes_t(const float* x, const float* g, const float* b, float* hi
     if (C <= 128) launch_rows<KIND, 32, 4, true, true, F16P>(x, g, b, hi, rows, C, eps, st, x1, cross);
     else if (C <= 256) launch_rows<KIND, 32, 8, true, true, F16P>(x, g, b, hi, rows, C, eps, st, x1, cross);
     else if (C <= 512) launch_rows<KIND, 32, 16, true, true, F16P>(x, g, b, hi, rows, C, eps, st, x1, cross);
+    else if (C <= 768) launch_rows<KIND, 32, 24, true, true, F16P>(x, g, b, hi, rows, C, eps, st, x1, cross);
     else if (C <= 1024) launch_rows<KIND, 32, 32, true, true, F16P>(x, g, b, hi, rows, C, eps, st, x1, cross);
     else if (C <= 2048) launch_rows<KIND, 32, 64, true, true, F16P>(x, g, b, hi, rows, C, eps, st, x1, cross);
     else launch_rows<KIND, 256, 16, true, true, F16P>(x, g, b, hi, rows, C, eps, st, x1, cross);
@@ -300,6 +387,7 @@ Status run_rows(const float* x, const float* g, const float* b, float* y, int64_
         else if (C <= 512) launch_rows<KIND, 32, 16, true>(x, g, b, y, rows, C, eps, st);
         else if (C <= 1024 && C > norm_cta_min()) launch_rows<KIND, 256, 4, true>(x, g, b, y, rows, C, eps, st);
         else if (C <= 2048 && C > norm_cta_min()) launch_rows<KIND, 256, 8, true>(x, g, b, y, rows, C, eps, st);
+        else if (C <= 768) launch_rows<KIND, 32, 24, true>(x, g, b, y, rows, C, eps, st);
         else if (C <= 1024) launch_rows<KIND, 32, 32, true>(x, g, b, y, rows, C, eps, st);
         else if (C <= 2048) launch_rows<KIND, 32, 64, true>(x, g, b, y, rows, C, eps, st);
         else if (C <= 4096) launch_rows<KIND, 256, 16, true>(x, g, b, y, rows, C, eps, st);

@@ -145,12 +145,21 @@ def test_protected_output_blocks_folding():
 def test_qwen3_rotary_chains_fold():
     """Qwen3 q/k paths: SLICE -> RMSNORM -> TRANSPOSE -> rotary (MUL, SLICE, SLICE,
     NEG, CAT, MUL, ADD) run as one fused kernel at the ADD: 9 of 10 nodes per
-    chain skipped, 2 chains per layer."""
+    chain skipped, 2 chains per layer.  The V path (SLICE -> head-split
+    TRANSPOSE) and the head-merge TRANSPOSE fold into the attention although
+    the planner put the attention output over the QKV projection V is sliced
+    from: the tensor-core path's pre-passes consume V before O is written."""
     prog = Program.load(GOLDEN / "qwen3_b8.json")
     arr, _ = bind(prog)
     n, flags = report(prog, arr)
-    assert n == 36
+    assert n == 36 + 2 * 3
     assert [prog.nodes[i].op for i, f in enumerate(flags) if f == 5] == [OP["ADD"]] * 4
+    att = [i for i, nd in enumerate(prog.nodes) if nd.op == OP["ATTENTION"]]
+    for a in att:
+        assert flags[a] == 2
+        assert [prog.nodes[a - 2].op, prog.nodes[a - 1].op, prog.nodes[a + 1].op] == \
+            [OP["SLICE"], OP["TRANSPOSE"], OP["TRANSPOSE"]]
+        assert flags[a - 2] == flags[a - 1] == flags[a + 1] == 1
     folded = sorted({prog.nodes[i].op for i, f in enumerate(flags) if f == 1})
     assert folded == sorted({OP[k] for k in ("SLICE", "RMSNORM", "TRANSPOSE", "MUL", "NEG", "CAT")})
 

@@ -239,6 +239,31 @@ def test_slice_and_cat(inner_odd, gpu_executor_factory):
     np.testing.assert_array_equal(got, np.concatenate([a, b], axis=3))
 
 
+def test_layout_runs_long_short_and_scalar(gpu_executor_factory):
+    """Run-based layout copies: few long runs (cut into pieces across the
+    grid), runs shorter than a warp, and 4-byte units with inner == 1."""
+    a, b = rand(1, 300001), rand(1, 70000)       # CAT along dim 1: one run per input
+    got, ref = run_both(gpu_executor_factory,
+                        single_node_program(OP["CAT"], [a, b], [1, 370001], [1, 300001, 70000]))
+    np.testing.assert_array_equal(got, np.concatenate([a, b], axis=1))
+    x = rand(2, 200003)                           # SLICE: two long rows, odd start
+    got, ref = run_both(gpu_executor_factory,
+                        single_node_program(OP["SLICE"], [x], [2, 150000], [2, 200003, 17, 150000, 1]))
+    np.testing.assert_array_equal(got, x[:, 17:17 + 150000])
+    y = rand(3, 7, 5, 11)                         # TRANSPOSE dims 1, 2 with inner 11 (scalar units)
+    got, ref = run_both(gpu_executor_factory,
+                        single_node_program(OP["TRANSPOSE"], [y], [3, 5, 7, 11], [3, 7, 1, 5, 11]))
+    np.testing.assert_array_equal(got, np.swapaxes(y, 1, 2))
+    z = rand(4, 64, 8, 128)                       # head split [B, S, H, D] -> [B, H, S, D]
+    got, ref = run_both(gpu_executor_factory,
+                        single_node_program(OP["TRANSPOSE"], [z], [4, 8, 64, 128], [4, 64, 1, 8, 128]))
+    np.testing.assert_array_equal(got, np.swapaxes(z, 1, 2))
+    u = rand(6, 9, 4)                             # TRANSPOSE dims 0, 2 with inner 1
+    got, ref = run_both(gpu_executor_factory,
+                        single_node_program(OP["TRANSPOSE"], [u], [4, 9, 6], [1, 6, 9, 4, 1]))
+    np.testing.assert_array_equal(got, np.swapaxes(u, 0, 2))
+
+
 def test_reshape_copy_and_embedding(gpu_executor_factory):
     x = rand(4, 6)
     got, ref = run_both(gpu_executor_factory, single_node_program(OP["RESHAPE"], [x], [24], []))
