@@ -509,6 +509,10 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
             int stage = 0;
             uint32_t ph = 0;
             bool ok = true;
+            // 128-byte-swizzle descriptor of ring stage 0; stage s starts CHUNK * s
+            // bytes later (the start-address field counts 16-byte units and the
+            // whole shared window fits it, so the offset adds without carry)
+            const uint64_t ring_desc0 = ptx::smem_desc(ring, 1024, 2);
             auto pop = [&]() -> uint8_t* {
                 if (!ok) return nullptr;
                 if (!(ok = ptx::wait_bounded(&full[stage], ph, abort_flag, p.err, ERR_A_MMA, WAIT_NS)))
@@ -537,12 +541,11 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
                                 const uint8_t* a = qh + (c * 2 + cs) * BQ * 128 + j * 64;
                                 const uint8_t* b = buf + cs * BKV * 128 + j * 64;
                                 if (Q_TMEM) {
-                                    const uint32_t qc = tmem + COL_QT + (uint32_t)((c * 2 + cs) * 32 + j * 16);
-                                    ptx::mma_bf16_ts(tmem + COL_S, qc, ptx::smem_desc(b + 32, 1024, 2), idesc_sh,
-                                                     (c | cs | j) ? 1u : 0u);
-                                    ptx::mma_bf16_ts(tmem + COL_S, qc, ptx::smem_desc(b, 1024, 2), idesc_sh, 1u);
-                                    ptx::mma_bf16_ts(tmem + COL_S, qc + 8, ptx::smem_desc(b + 32, 1024, 2), idesc_sh,
-                                                     1u);
+                                    // descriptors from the stage's precomputed base + constant offsets
+                                    const uint64_t bl = ring_desc0 + (uint64_t)stage * (CHUNK >> 4) +
+                                                        (uint64_t)((cs * BKV * 128 + j * 64) >> 4);
+                                    ptx::mma_f16x3_ts(tmem + COL_S, tmem + COL_QT + (uint32_t)((c * 2 + cs) * 32 + j * 16),
+                                                      bl + 2, bl, idesc_sh, (c | cs | j) ? 1u : 0u);
                                     continue;
                                 }
                                 ptx::mma_bf16(tmem + COL_S, ptx::smem_desc(a, 1024, 2), ptx::smem_desc(b + 32, 1024, 2),
@@ -586,12 +589,11 @@ __global__ void __launch_bounds__(ATHREADS, 1) attn_tc_kernel(const __grid_const
                         for (int sb = 0; sb < C::V_KEYS / 32; sb++)
 #pragma unroll
                             for (int j = 0; j < 2; j++) {
-                                const uint8_t* b = buf + sb * D * 128 + j * 64;
-                                const uint32_t pc = tmem + COL_PH + (uint32_t)((c * C::V_KEYS + sb * 32 + j * 16));
-                                ptx::mma_bf16_ts(tmem + COL_O, pc, ptx::smem_desc(b + 32, 1024, 2), idesc_oh,
-                                                 (c | sb | j | !fresh) ? 1u : 0u);
-                                ptx::mma_bf16_ts(tmem + COL_O, pc, ptx::smem_desc(b, 1024, 2), idesc_oh, 1u);
-                                ptx::mma_bf16_ts(tmem + COL_O, pc + 8, ptx::smem_desc(b + 32, 1024, 2), idesc_oh, 1u);
+                                const uint64_t bl = ring_desc0 + (uint64_t)stage * (CHUNK >> 4) +
+                                                    (uint64_t)((sb * D * 128 + j * 64) >> 4);
+                                ptx::mma_f16x3_ts(tmem + COL_O,
+                                                  tmem + COL_PH + (uint32_t)((c * C::V_KEYS + sb * 32 + j * 16)),
+                                                  bl + 2, bl, idesc_oh, (c | sb | j | !fresh) ? 1u : 0u);
                             }
                         release();
                         continue;

@@ -170,6 +170,24 @@ __device__ __forceinline__ void mma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, ui
         "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
+// The fp16 split product of one 16-wide K step with A in TMEM, as one
+// instruction group: D (+)= A_h.B_h + A_h.B_l + A_l.B_h, with A_h at column
+// a_h, A_l at a_h + 8, and B's h / l halves at descriptors b_h / b_l.  One
+// predicate set-up for the three MMAs keeps the issuing thread's instruction
+// stream short (its issue rate, not the tensor pipe, bounds a tile loop whose
+// MMAs are 128 x 128 x 16).
+__device__ __forceinline__ void mma_f16x3_ts(uint32_t tmem_d, uint32_t a_h, uint64_t b_h, uint64_t b_l,
+                                             uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p, t;\n\t"
+        "setp.ne.b32 p, %5, 0;\n\t"
+        "setp.eq.b32 t, %5, %5;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %3, %4, p;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %4, t;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%6], %3, %4, t;\n\t}" ::"r"(tmem_d),
+        "r"(a_h), "l"(b_l), "l"(b_h), "r"(idesc), "r"(accumulate), "r"(a_h + 8)
+        : "memory");
+}
 // Arrive once on `bar` when all tcgen05 ops issued so far by this thread complete.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
